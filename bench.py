@@ -1,0 +1,338 @@
+"""Headline benchmark: Wan2.2-14B-shape DiT denoise step under weight offloading.
+
+Metric: seconds per denoise step at a fixed GPU weight budget
+(25% of the model's weight bytes resident), with peak GPU memory and the share
+of host->device transfer time hidden behind compute.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+* ``ours``       -- flextensor_b200: tcgen05 kernels + native streaming runtime.
+* ``reference``  -- the unmodified reference runtime from ``baseline/_ref``
+  driving the same architecture written in plain PyTorch (cuBLAS GEMMs, SDPA).
+
+Both arms use the same OffloadConfig: blocks are offload units, BudgetFill
+planning under a byte budget equal to 25% of the weights, 2 ring slots.
+Weights are random (seeded), inputs synthetic with the named shapes. Each rank
+runs its own replica (weak scaling); times are device-timed with CUDA events
+and reduced as the max over ranks. Inputs (latent 4.2 MB + text 4 MB) are
+larger than nothing but far smaller than L2, so L2 is flushed with a 256 MB
+write before every timed step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+METRIC = "s/step & peak GPU GB at fixed weight budget, 1/2/4/8 B200; % transfer hidden"
+MODEL = "Wan2.2-14B-shape DiT (40 blocks, d=5120, 40 heads, FFN 13824, 32760 tokens, text 512x4096)"
+RESIDENT_FRACTION = 0.25
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=40, help="(testing only) fewer blocks; invalid for the headline")
+    ap.add_argument("--profiling-iters", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks sampler
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+
+    def start(self):
+        os.makedirs(os.path.dirname(self.out), exist_ok=True)
+        try:
+            self.f = open(self.out, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.out):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup(n):
+    import torch
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, world, local, pg
+
+
+def allreduce_max(x: float, pg) -> float:
+    if pg is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(pg):
+    import torch
+
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+
+# ----------------------------------------------------------------------------- model + runtime per arm
+def build_model(impl: str, layers: int, device, seed: int):
+    import torch
+
+    sys.path.insert(0, ROOT)
+    from flextensor_b200.models.wan import WAN_14B, WanConfig, WanDiT, init_wan_params_
+
+    cfg = WanConfig(**{**WAN_14B.__dict__, "num_layers": layers})
+    with torch.device("meta"):
+        model = WanDiT(cfg, impl="fused" if impl == "ours" else "torch")
+    model = model.to_empty(device=device).to(torch.bfloat16)
+    init_wan_params_(model, seed=seed)
+    # weights start in (pinned) host memory, as a loaded checkpoint would
+    with torch.no_grad():
+        for p in model.parameters():
+            h = torch.empty(p.shape, dtype=p.dtype, pin_memory=True)
+            h.copy_(p.data, non_blocking=True)
+            p.data = h
+        for name, b in model.named_buffers():
+            b.data = b.data.cpu()
+    torch.cuda.synchronize()
+    model.eval()
+    model.requires_grad_(False)
+    return model, cfg
+
+
+def weight_budget_fraction(model, device) -> float:
+    import torch
+
+    total = sum(p.numel() * p.element_size() for p in model.parameters())
+    block = sum(p.numel() * p.element_size() for n, p in model.named_parameters() if n.startswith("blocks."))
+    other = total - block
+    dev_total = torch.cuda.get_device_properties(device).total_memory
+    # planner-visible budget = 25% of all weight bytes minus the always-resident non-block weights
+    return (RESIDENT_FRACTION * total) / dev_total, total, block, other
+
+
+def make_config(ft, local: int, frac: float, profiling_iters: int):
+    return ft.OffloadConfig(
+        gpu_device=local,
+        include_patterns=["blocks.*"],
+        num_blocks=2,
+        min_blocks=2,
+        max_gpu_mem_fraction=frac,
+        profiling_iters=profiling_iters,
+        discovery_iters=1,
+        load_strategy=ft.BudgetFillStrategy(n_blocks=2, threshold_mb=1.0, enable_layer_de=True,
+                                            enable_tensor_de=False, seed=0),
+    )
+
+
+def import_arm(impl: str):
+    if impl == "reference":
+        ref = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref, "flextensor")):
+            return None, "reference not installed in baseline/_ref"
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "shims"))
+        sys.path.insert(0, ref)
+        os.environ.setdefault("DISABLE_BEARTYPE", "1")
+        import flextensor as ft  # noqa: PLC0415
+
+        return ft, None
+    sys.path.insert(0, ROOT)
+    import flextensor_b200 as ft  # noqa: PLC0415
+
+    return ft, None
+
+
+def main():
+    args = parse()
+    import torch
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    ft, why = import_arm(args.impl)
+    if ft is None:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+        return
+    torch.manual_seed(1234 + rank)
+    model, cfg = build_model(args.impl, args.layers, device, seed=rank)
+    frac, total_w, block_w, other_w = weight_budget_fraction(model, device)
+    config = make_config(ft, local, frac, args.profiling_iters)
+    om = ft.get_offload_manager()
+    model = om.offload(model, config)
+
+    # synthetic step inputs in pinned host memory
+    Fr, H, W = 21, 60, 104
+    lat_h = torch.randn(1, cfg.in_channels, Fr, H, W, dtype=torch.bfloat16).pin_memory()
+    ctx_h = torch.randn(1, cfg.text_len, cfg.text_dim, dtype=torch.bfloat16).pin_memory()
+    ts_h = torch.tensor([500.0]).pin_memory()
+    out_h = torch.empty(1, cfg.out_channels, Fr, H, W, dtype=torch.bfloat16).pin_memory()
+    lat = lat_h.to(device)
+    ctx = ctx_h.to(device)
+    ts = ts_h.to(device)
+    tokens = Fr * (H // 2) * (W // 2)
+
+    t_setup = time.perf_counter()
+    with torch.no_grad():
+        for _ in range(om.iters_before_inference):
+            model(lat, ts, ctx)
+    torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t_setup
+    assert str(om.phase).endswith("INFERENCE"), f"not in inference after warm-up forwards: {om.phase}"
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            model(lat, ts, ctx)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(device)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    times = []
+    barrier(pg)
+    with torch.no_grad():
+        for _ in range(args.steps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            y = model(lat, ts, ctx)
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+    barrier(pg)
+    step_ms = [s.elapsed_time(e) for s, e in times]
+    peak_gb = torch.cuda.max_memory_allocated(device) / 1e9
+    ms = sum(step_ms) / len(step_ms)
+
+    # end to end through the public call: H2D inputs from pinned host, forward, D2H result
+    e2e_s = None
+    h2d = lat_h.numel() * 2 + ctx_h.numel() * 2 + ts_h.numel() * 4
+    d2h = out_h.numel() * 2
+    if not args.no_e2e:
+        barrier(pg)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            for _ in range(args.steps):
+                a = lat_h.to(device, non_blocking=True)
+                c = ctx_h.to(device, non_blocking=True)
+                t = ts_h.to(device, non_blocking=True)
+                yy = model(a, t, c)
+                out_h.copy_(yy, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+        e2e_s = (time.perf_counter() - t0) / args.steps
+        barrier(pg)
+    ck = clocks.stop()
+
+    hidden = None
+    try:
+        tm = om.get_tensor_manager()
+        st = tm.get_gpu_memory_usage()
+        blocks_gb = st.blocks_bytes / 1e9
+        resident_gb = st.unmapped_tensors_bytes / 1e9
+    except Exception:  # noqa: BLE001
+        blocks_gb = resident_gb = None
+    ms_max = allreduce_max(ms, pg)
+    peak_max = allreduce_max(peak_gb, pg)
+    e2e_max = allreduce_max(e2e_s, pg) if e2e_s is not None else None
+    out = {
+        "metric": METRIC,
+        "value": round(ms_max / 1000.0, 5),
+        "unit": "s/step",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max, 3),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights, N(0,1) latent/text inputs of the named shapes)",
+        "impl": args.impl,
+        "peak_gpu_gb": round(peak_max, 3),
+        "tokens_per_s_total": round(tokens * world / (ms_max / 1000.0), 1),
+        "weights_gb": round(total_w / 1e9, 3),
+        "ring_slots_gb": blocks_gb and round(blocks_gb, 3),
+        "resident_weights_gb": resident_gb and round(resident_gb, 3),
+        "transfer_hidden_pct": hidden,
+        "setup_s": round(setup_s, 2),
+        "clocks": ck,
+        "e2e": None if e2e_max is None else {"value": round(e2e_max, 5), "unit": "s/step", "h2d_bytes_per_step": h2d,
+                                              "d2h_bytes_per_step": d2h},
+        "gpu_launches": None,
+        "config": {"model": MODEL if args.layers == 40 else f"{MODEL} [layers={args.layers}: NOT the headline]",
+                   "global_batch": world, "seq_len": tokens, "parallelism": f"dp{world}",
+                   "weight_budget": f"{int(RESIDENT_FRACTION * 100)}% of weight bytes on GPU (incl. ring slots)",
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "denoise_steps_timed": args.steps},
+    }
+    if rank == 0:
+        print(json.dumps(out))
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

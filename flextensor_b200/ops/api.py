@@ -1,0 +1,86 @@
+"""Python entry points of the native kernels.
+
+All ops run on the caller's current CUDA stream, take bf16 activations and
+return bf16; reductions and epilogues are computed in fp32 inside the kernels.
+They require the native extension on CUDA tensors (no silent fallback).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from flextensor_b200.ops import native
+
+EPI = {"none": 0, "bias": 1, "gelu": 2, "gate_res": 3, "res": 4}
+
+
+def _2d(t: torch.Tensor) -> torch.Tensor:
+    return t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, epi: str = "bias",
+           residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, gate_rows: int = 0,
+           out: torch.Tensor | None = None, force_bn: int = 0) -> torch.Tensor:
+    """``epi(x @ weight.T + bias)`` on tcgen05 tensor cores.
+
+    epi: ``none`` | ``bias`` | ``gelu`` (tanh GELU) | ``res`` (residual + y) |
+    ``gate_res`` (residual + gate * y; gate fp32 ``[N]`` or ``[M/gate_rows, N]``).
+    ``out`` may alias ``residual`` (in-place residual update).
+    """
+    lead = x.shape[:-1]
+    a = _2d(x)
+    if a.stride(-1) != 1:
+        a = a.contiguous()
+    n = weight.shape[0]
+    if out is None:
+        out = torch.empty(*lead, n, dtype=torch.bfloat16, device=x.device)
+    o2 = _2d(out)
+    r2 = _2d(residual) if residual is not None else None
+    e = EPI[epi]
+    if e in (1, 2) and bias is None:
+        e = EPI["none"] if e == 1 else e
+    native.lib().gemm(a, weight, o2, bias, r2, gate, int(gate_rows), e, int(force_bn))
+    return out
+
+
+def layernorm_modulate(x: torch.Tensor, scale: torch.Tensor | None = None, shift: torch.Tensor | None = None, *,
+                       weight: torch.Tensor | None = None, bias: torch.Tensor | None = None, mod_rows: int = 0,
+                       eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``LN(x) [*w+b] [*(1+scale)+shift]`` per row; scale/shift fp32 ``[D]`` or ``[M/mod_rows, D]``."""
+    x2 = _2d(x)
+    if out is None:
+        out = torch.empty_like(x)
+    native.lib().ln_modulate(x2, _2d(out), weight, bias, scale, shift, int(mod_rows), float(eps))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None = None, *, eps: float = 1e-6,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    x2 = _2d(x)
+    if out is None:
+        out = torch.empty(x2.shape, dtype=x.dtype, device=x.device).view(x.shape)
+    native.lib().rmsnorm(x2, _2d(out), weight, None, None, 0, 0, float(eps))
+    return out
+
+
+def qk_rmsnorm_rope(x: torch.Tensor, weight: torch.Tensor | None, cos: torch.Tensor, sin: torch.Tensor,
+                    head_dim: int, seq_len: int, *, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over the full row, then interleaved-pair RoPE per head (tables ``[seq_len, head_dim/2]``)."""
+    x2 = _2d(x)
+    if out is None:
+        out = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    native.lib().rmsnorm(x2, _2d(out), weight, cos, sin, int(head_dim), int(seq_len), float(eps))
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
+              causal: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Softmax attention on ``[B, S, H, 128]`` bf16 tensors (GQA when k/v have fewer heads)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    native.lib().attention(q, k, v, out, float(scale), bool(causal))
+    return out

@@ -1,0 +1,256 @@
+// Python bindings of the native kernels and runtime (module ft_b200_C).
+//
+// Every op validates device, dtype, shape and stride before launching and
+// launches on the caller's current CUDA stream; a failed launch raises.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "ft_attn.h"
+#include "ft_ops.h"
+#include "ft_ops_norm.h"
+#include "ft_runtime.h"
+
+namespace {
+
+using at::Tensor;
+
+void check_cuda_bf16(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have unit inner stride");
+}
+
+void check_ok(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+int num_sms_for(int dev) {
+  static int cache[64] = {0};
+  if (dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+void gemm(const Tensor& A, const Tensor& W, Tensor& C, const c10::optional<Tensor>& bias,
+          const c10::optional<Tensor>& residual, const c10::optional<Tensor>& gate, int64_t gate_rows, int64_t epi,
+          int64_t force_bn) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(W, "W");
+  check_cuda_bf16(C, "C");
+  TORCH_CHECK(A.size(1) == W.size(1), "K mismatch: A ", A.sizes(), " W ", W.sizes());
+  TORCH_CHECK(C.size(0) == A.size(0) && C.size(1) == W.size(0), "C shape ", C.sizes(), " != [M, N]");
+  TORCH_CHECK(A.get_device() == W.get_device() && A.get_device() == C.get_device(), "tensors on different devices");
+  c10::cuda::CUDAGuard g(A.device());
+  ft::GemmProblem p;
+  p.M = A.size(0);
+  p.N = W.size(0);
+  p.K = A.size(1);
+  p.A = reinterpret_cast<const __nv_bfloat16*>(A.data_ptr());
+  p.lda = A.stride(0);
+  p.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  p.ldw = W.stride(0);
+  p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr());
+  p.ldc = C.stride(0);
+  p.epi = (int)epi;
+  if (bias && bias->defined()) {
+    TORCH_CHECK(bias->is_cuda() && bias->scalar_type() == at::kBFloat16 && bias->is_contiguous() &&
+                    bias->numel() == p.N, "bias must be contiguous bf16 [N]");
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (residual && residual->defined()) {
+    check_cuda_bf16(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == p.M && residual->size(1) == p.N, "residual must be [M, N]");
+    p.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+  }
+  if (gate && gate->defined()) {
+    TORCH_CHECK(gate->is_cuda() && gate->scalar_type() == at::kFloat && gate->is_contiguous(),
+                "gate must be contiguous fp32");
+    TORCH_CHECK(gate->numel() % p.N == 0, "gate numel must be a multiple of N");
+    if (gate_rows > 0) TORCH_CHECK((p.M + gate_rows - 1) / gate_rows * p.N <= gate->numel(), "gate too small");
+    p.gate = gate->data_ptr<float>();
+    p.gate_rows = (int)gate_rows;
+  }
+  p.num_sms = num_sms_for(A.get_device());
+  p.force_bn = (int)force_bn;
+  check_ok(ft::gemm_bf16(p, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
+}
+
+const void* opt_ptr(const c10::optional<Tensor>& t) { return (t && t->defined()) ? t->data_ptr() : nullptr; }
+
+void ln_modulate(const Tensor& x, Tensor& y, const c10::optional<Tensor>& weight, const c10::optional<Tensor>& bias,
+                 const c10::optional<Tensor>& scale, const c10::optional<Tensor>& shift, int64_t mod_rows,
+                 double eps) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(y, "y");
+  TORCH_CHECK(x.sizes() == y.sizes(), "x/y shape mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  ft::LnArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.ldy = y.stride(0);
+  a.D = x.size(1);
+  a.eps = (float)eps;
+  if (weight && weight->defined()) {
+    TORCH_CHECK(weight->numel() == a.D && weight->is_contiguous(), "weight must be [D]");
+    a.weight = weight->data_ptr();
+    a.affine_bf16 = weight->scalar_type() == at::kBFloat16;
+    if (bias && bias->defined()) {
+      TORCH_CHECK(bias->scalar_type() == weight->scalar_type() && bias->numel() == a.D, "bias must match weight");
+      a.bias = bias->data_ptr();
+    }
+  }
+  for (const c10::optional<Tensor>* t : {&scale, &shift}) {
+    if (*t && (*t)->defined()) {
+      TORCH_CHECK((*t)->scalar_type() == at::kFloat && (*t)->stride(-1) == 1, "scale/shift must be fp32 rows");
+      TORCH_CHECK((*t)->size(-1) == a.D, "scale/shift last dim must be D");
+    }
+  }
+  if (scale && scale->defined()) {
+    a.scale = scale->data_ptr<float>();
+    a.mod_stride = scale->dim() > 1 ? scale->stride(-2) : 0;
+  }
+  if (shift && shift->defined()) {
+    a.shift = shift->data_ptr<float>();
+    if (shift->dim() > 1) TORCH_CHECK(shift->stride(-2) == a.mod_stride || !a.scale, "scale/shift row strides differ");
+    if (!a.scale) a.mod_stride = shift->dim() > 1 ? shift->stride(-2) : 0;
+  }
+  a.mod_rows = (int)mod_rows;
+  check_ok(ft::ln_modulate(a, x.size(0), at::cuda::getCurrentCUDAStream()), "ln_modulate");
+}
+
+void rmsnorm(const Tensor& x, Tensor& y, const c10::optional<Tensor>& weight, const c10::optional<Tensor>& cos,
+             const c10::optional<Tensor>& sin, int64_t head_dim, int64_t seq_len, double eps) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(y, "y");
+  TORCH_CHECK(x.sizes() == y.sizes(), "x/y shape mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  ft::RmsArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.ldy = y.stride(0);
+  a.D = x.size(1);
+  a.eps = (float)eps;
+  if (weight && weight->defined()) {
+    TORCH_CHECK(weight->numel() == a.D && weight->is_contiguous(), "weight must be [D]");
+    a.weight = weight->data_ptr();
+    a.weight_bf16 = weight->scalar_type() == at::kBFloat16;
+  }
+  if (cos && cos->defined()) {
+    TORCH_CHECK(sin && sin->defined(), "sin table required with cos");
+    TORCH_CHECK(cos->scalar_type() == at::kFloat && sin->scalar_type() == at::kFloat && cos->is_contiguous() &&
+                    sin->is_contiguous(), "rope tables must be contiguous fp32");
+    TORCH_CHECK(cos->numel() == seq_len * head_dim / 2 && sin->numel() == cos->numel(),
+                "rope tables must be [seq_len, head_dim/2]");
+    a.cos = cos->data_ptr<float>();
+    a.sin = sin->data_ptr<float>();
+    a.head_dim = (int)head_dim;
+    a.seq_len = (int)seq_len;
+  }
+  check_ok(ft::rmsnorm(a, x.size(0), at::cuda::getCurrentCUDAStream()), "rmsnorm");
+}
+
+void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, double scale, bool causal) {
+  for (const Tensor* p : {&q, &k, &v, const_cast<const Tensor*>(&o)}) {
+    TORCH_CHECK(p->is_cuda() && p->scalar_type() == at::kBFloat16 && p->dim() == 4,
+                "attention tensors must be 4-D bf16 CUDA [B, S, H, D]");
+    TORCH_CHECK(p->stride(3) == 1, "head dim must be contiguous");
+  }
+  TORCH_CHECK(q.size(3) == 128 && k.size(3) == 128 && v.size(3) == 128, "head_dim 128 only");
+  TORCH_CHECK(k.sizes() == v.sizes(), "k/v shape mismatch");
+  TORCH_CHECK(q.size(0) == k.size(0) && q.sizes() == o.sizes(), "q/k/o batch or shape mismatch");
+  TORCH_CHECK(q.size(2) % k.size(2) == 0, "query heads must be a multiple of kv heads");
+  c10::cuda::CUDAGuard g(q.device());
+  ft::AttnProblem p;
+  p.B = q.size(0);
+  p.Sq = q.size(1);
+  p.Sk = k.size(1);
+  p.Hq = q.size(2);
+  p.Hk = k.size(2);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.q_row = q.stride(1);
+  p.k_row = k.stride(1);
+  p.v_row = v.stride(1);
+  p.o_row = o.stride(1);
+  p.q_batch = q.stride(0);
+  p.k_batch = k.stride(0);
+  p.v_batch = v.stride(0);
+  p.o_batch = o.stride(0);
+  TORCH_CHECK(q.stride(2) == 128 && k.stride(2) == 128 && v.stride(2) == 128 && o.stride(2) == 128,
+              "heads must be packed (stride 128 between heads)");
+  p.scale = (float)scale;
+  p.causal = causal;
+  p.num_sms = num_sms_for(q.get_device());
+  check_ok(ft::attention_fwd(p, at::cuda::getCurrentCUDAStream()), "attention_fwd");
+}
+
+int device_error(bool reset) {
+  int e = ft::gemm_device_error(reset);
+  int n = ft::norm_device_error(reset);
+  int a = ft::attn_device_error(reset);
+  return e ? e : (n ? n : a);
+}
+
+struct PyEngine {
+  std::unique_ptr<ft::TransferEngine> e;
+  int device;
+  PyEngine(int dev, int n_slots, int n_keys, bool timing) : device(dev) {
+    c10::cuda::CUDAGuard g(dev);
+    e = std::make_unique<ft::TransferEngine>(dev, n_slots, n_keys, timing);
+  }
+  cudaStream_t cs() { return at::cuda::getCurrentCUDAStream(device).stream(); }
+  void begin() { e->begin(cs()); }
+  void submit(int slot, const Tensor& dst, const Tensor& src, int key) {
+    TORCH_CHECK(dst.is_cuda() && src.device().is_cpu(), "submit copies host -> device");
+    const size_t n = src.numel() * src.element_size();
+    TORCH_CHECK(dst.numel() * dst.element_size() >= n, "destination slot too small");
+    c10::cuda::CUDAGuard g(device);
+    e->submit(slot, dst.data_ptr(), src.data_ptr(), n, key);
+  }
+  void wait_ready(int key) { e->wait_ready(key, cs()); }
+  void finish_use(int slot) { e->finish_use(slot, cs()); }
+  void join() { e->join(cs()); }
+  void synchronize() { e->synchronize(); }
+  std::vector<std::tuple<int, size_t, float, float>> take_samples() {
+    std::vector<std::tuple<int, size_t, float, float>> out;
+    for (auto& s : e->take_samples()) out.emplace_back(s.key, s.bytes, s.transfer_ms, s.wait_ms);
+    return out;
+  }
+};
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "flextensor_b200 native kernels (sm_100a) and runtime";
+  m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A W^T)", py::arg("A"), py::arg("W"), py::arg("C"),
+        py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("gate") = py::none(),
+        py::arg("gate_rows") = 0, py::arg("epi") = 0, py::arg("force_bn") = 0);
+  m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("y"), py::arg("weight") = py::none(),
+        py::arg("bias") = py::none(), py::arg("scale") = py::none(), py::arg("shift") = py::none(),
+        py::arg("mod_rows") = 0, py::arg("eps") = 1e-6);
+  m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("y"), py::arg("weight") = py::none(), py::arg("cos") = py::none(),
+        py::arg("sin") = py::none(), py::arg("head_dim") = 0, py::arg("seq_len") = 0, py::arg("eps") = 1e-6);
+  m.def("attention", &attention, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("scale"),
+        py::arg("causal") = false);
+  m.def("device_error", &device_error, py::arg("reset") = false);
+  m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
+  m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
+  py::class_<PyEngine>(m, "TransferEngine")
+      .def(py::init<int, int, int, bool>())
+      .def("begin", &PyEngine::begin)
+      .def("submit", &PyEngine::submit)
+      .def("wait_ready", &PyEngine::wait_ready)
+      .def("finish_use", &PyEngine::finish_use)
+      .def("join", &PyEngine::join)
+      .def("synchronize", &PyEngine::synchronize)
+      .def("take_samples", &PyEngine::take_samples);
+}

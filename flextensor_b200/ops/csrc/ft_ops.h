@@ -1,0 +1,54 @@
+// Host-side declarations of the flextensor_b200 native kernels and runtime.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ft {
+
+enum Epilogue : int {
+  EPI_NONE = 0,          // C = A.W^T
+  EPI_BIAS = 1,          // C = A.W^T + b
+  EPI_BIAS_GELU = 2,     // C = gelu_tanh(A.W^T + b)
+  EPI_BIAS_GATE_RES = 3, // C = R + g * (A.W^T + b)        (g fp32 per column, per gate_rows rows)
+  EPI_BIAS_RES = 4,      // C = R + (A.W^T + b)
+};
+
+struct GemmProblem {
+  int M = 0, N = 0, K = 0;
+  const __nv_bfloat16* A = nullptr;
+  int lda = 0;
+  const __nv_bfloat16* W = nullptr;
+  int ldw = 0;
+  __nv_bfloat16* C = nullptr;
+  int ldc = 0;
+  const __nv_bfloat16* bias = nullptr;
+  const __nv_bfloat16* residual = nullptr;
+  int ldr = 0;
+  const float* gate = nullptr;
+  int gate_rows = 0;
+  int epi = EPI_NONE;
+  int num_sms = 0;
+  int force_bn = 0;
+};
+
+cudaError_t gemm_bf16(const GemmProblem& g, cudaStream_t stream);
+
+// 2-D bf16 tensor map: inner extent `inner` (contiguous), `outer` rows with row
+// stride `ld` elements; box = box_inner x box_outer; 128-byte swizzle when
+// box_inner*2 == 128, zero fill out of bounds.
+bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, int inner, int outer, int ld, int box_inner,
+                       int box_outer);
+bool make_tmap_2d_bf16_swz(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                           int box_inner, int box_outer, int swizzle_bytes);
+
+// 3-D bf16 tensor map (inner, rows, batches) with element strides; 128-byte swizzle box.
+bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t batches,
+                       uint64_t row_stride_elems, uint64_t batch_stride_elems, int box_inner, int box_rows);
+
+int gemm_device_error(bool reset);
+int norm_device_error(bool reset);
+int attn_device_error(bool reset);
+
+}  // namespace ft

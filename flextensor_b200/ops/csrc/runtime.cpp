@@ -1,0 +1,222 @@
+// Native runtime pieces: TMA descriptor encoding, host-page registration and
+// the ring-slot transfer engine (dedicated copy stream, per-slot "free" events,
+// per-ticket "ready" events, optional timing events).
+//
+// The engine is the hot path of weight streaming: one call per trap boundary,
+// each a handful of CUDA runtime calls with no Python objects involved. It is
+// CUDA-graph aware: when the compute stream is capturing, events recorded
+// before the capture are forgotten so every wait inside the graph refers to an
+// event recorded in the same capture (cross-replay ordering is implied by
+// graph launches on one stream).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "ft_ops.h"
+#include "ft_runtime.h"
+
+namespace ft {
+
+// ------------------------------------------------------------------ TMA descriptors
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_tmap_2d_bf16_swz(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                           int box_inner, int box_outer, int swizzle_bytes) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld_elems * 2) & 15)) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, int inner, int outer, int ld, int box_inner,
+                       int box_outer) {
+  return make_tmap_2d_bf16_swz(map, base, (uint64_t)inner, (uint64_t)outer, (uint64_t)ld, box_inner, box_outer,
+                               box_inner * 2 == 128 ? 128 : 0);
+}
+
+bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t batches,
+                       uint64_t row_stride_elems, uint64_t batch_stride_elems, int box_inner, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((row_stride_elems * 2) & 15) || ((batch_stride_elems * 2) & 15))
+    return false;
+  if (batches > 1 && batch_stride_elems == 0) return false;
+  cuuint64_t dims[3] = {inner, rows, batches};
+  cuuint64_t strides[2] = {row_stride_elems * 2, (batches > 1 ? batch_stride_elems : rows * row_stride_elems) * 2};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, box_inner * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                                      : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------------ host registration
+void host_register(void* ptr, size_t bytes) {
+  cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaHostRegister failed: ") + cudaGetErrorString(e));
+}
+
+void host_unregister(void* ptr) {
+  cudaError_t e = cudaHostUnregister(ptr);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaHostUnregister failed: ") + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------------ transfer engine
+#define FT_CHECK(x)                                                                                \
+  do {                                                                                             \
+    cudaError_t _e = (x);                                                                          \
+    if (_e != cudaSuccess) throw std::runtime_error(std::string(#x " failed: ") + cudaGetErrorString(_e)); \
+  } while (0)
+
+TransferEngine::TransferEngine(int device, int n_slots, int n_keys, bool timing)
+    : device_(device), timing_(timing) {
+  int prev;
+  FT_CHECK(cudaGetDevice(&prev));
+  FT_CHECK(cudaSetDevice(device));
+  int lo, hi;
+  FT_CHECK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+  FT_CHECK(cudaStreamCreateWithPriority(&copy_, cudaStreamNonBlocking, hi));
+  slot_free_.resize(n_slots);
+  slot_recorded_.assign(n_slots, 0);
+  ready_.resize(n_keys);
+  ready_recorded_.assign(n_keys, 0);
+  for (auto& e : slot_free_) FT_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (auto& e : ready_) FT_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  FT_CHECK(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
+  FT_CHECK(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming));
+  if (timing_) {
+    t_start_.resize(n_keys);
+    t_end_.resize(n_keys);
+    w_start_.resize(n_keys);
+    w_end_.resize(n_keys);
+    for (int i = 0; i < n_keys; i++) {
+      FT_CHECK(cudaEventCreate(&t_start_[i]));
+      FT_CHECK(cudaEventCreate(&t_end_[i]));
+      FT_CHECK(cudaEventCreate(&w_start_[i]));
+      FT_CHECK(cudaEventCreate(&w_end_[i]));
+    }
+    bytes_.assign(n_keys, 0);
+    t_valid_.assign(n_keys, 0);
+    w_valid_.assign(n_keys, 0);
+  }
+  cudaSetDevice(prev);
+}
+
+TransferEngine::~TransferEngine() {
+  int prev;
+  if (cudaGetDevice(&prev) != cudaSuccess) return;
+  cudaSetDevice(device_);
+  cudaStreamSynchronize(copy_);
+  for (auto e : slot_free_) cudaEventDestroy(e);
+  for (auto e : ready_) cudaEventDestroy(e);
+  for (auto* v : {&t_start_, &t_end_, &w_start_, &w_end_})
+    for (auto e : *v) cudaEventDestroy(e);
+  cudaEventDestroy(fork_);
+  cudaEventDestroy(join_);
+  cudaStreamDestroy(copy_);
+  cudaSetDevice(prev);
+}
+
+void TransferEngine::begin(cudaStream_t compute) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  FT_CHECK(cudaStreamIsCapturing(compute, &st));
+  const bool capturing = st != cudaStreamCaptureStatusNone;
+  if (capturing != capturing_) {
+    // entering or leaving a capture: events recorded on the other side are not waitable
+    std::fill(slot_recorded_.begin(), slot_recorded_.end(), 0);
+    std::fill(ready_recorded_.begin(), ready_recorded_.end(), 0);
+    capturing_ = capturing;
+  }
+  FT_CHECK(cudaEventRecord(fork_, compute));
+  FT_CHECK(cudaStreamWaitEvent(copy_, fork_, 0));
+}
+
+void TransferEngine::submit(int slot, void* dst, const void* src, size_t bytes, int key) {
+  if (slot_recorded_[slot]) FT_CHECK(cudaStreamWaitEvent(copy_, slot_free_[slot], 0));
+  const bool t = timing_ && !capturing_;
+  if (t) FT_CHECK(cudaEventRecord(t_start_[key], copy_));
+  FT_CHECK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, copy_));
+  FT_CHECK(cudaEventRecord(ready_[key], copy_));
+  ready_recorded_[key] = 1;
+  if (t) {
+    FT_CHECK(cudaEventRecord(t_end_[key], copy_));
+    bytes_[key] = bytes;
+    t_valid_[key] = 1;
+  }
+}
+
+void TransferEngine::wait_ready(int key, cudaStream_t compute) {
+  if (!ready_recorded_[key]) return;
+  const bool t = timing_ && !capturing_;
+  if (t) FT_CHECK(cudaEventRecord(w_start_[key], compute));
+  FT_CHECK(cudaStreamWaitEvent(compute, ready_[key], 0));
+  if (t) {
+    FT_CHECK(cudaEventRecord(w_end_[key], compute));
+    w_valid_[key] = 1;
+  }
+}
+
+void TransferEngine::finish_use(int slot, cudaStream_t compute) {
+  FT_CHECK(cudaEventRecord(slot_free_[slot], compute));
+  slot_recorded_[slot] = 1;
+}
+
+void TransferEngine::join(cudaStream_t compute) {
+  FT_CHECK(cudaEventRecord(join_, copy_));
+  FT_CHECK(cudaStreamWaitEvent(compute, join_, 0));
+}
+
+void TransferEngine::synchronize() { FT_CHECK(cudaStreamSynchronize(copy_)); }
+
+std::vector<TransferSample> TransferEngine::take_samples() {
+  std::vector<TransferSample> out;
+  if (!timing_) return out;
+  FT_CHECK(cudaStreamSynchronize(copy_));
+  for (size_t k = 0; k < t_valid_.size(); k++) {
+    if (!t_valid_[k]) continue;
+    TransferSample s;
+    s.key = (int)k;
+    s.bytes = bytes_[k];
+    FT_CHECK(cudaEventSynchronize(t_end_[k]));
+    FT_CHECK(cudaEventElapsedTime(&s.transfer_ms, t_start_[k], t_end_[k]));
+    if (w_valid_[k]) {
+      FT_CHECK(cudaEventSynchronize(w_end_[k]));
+      FT_CHECK(cudaEventElapsedTime(&s.wait_ms, w_start_[k], w_end_[k]));
+    }
+    out.push_back(s);
+    t_valid_[k] = 0;
+    w_valid_[k] = 0;
+  }
+  return out;
+}
+
+}  // namespace ft

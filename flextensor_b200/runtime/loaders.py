@@ -1,0 +1,234 @@
+"""Prefetch scheduler: per-trap ``enter``/``exit`` driving the transfer engine.
+
+Block loader (``allocation_block_transfer`` / ``raw_block_transfer``), the
+counterpart of ``src/flextensor/loaders.py:1473-1858``:
+
+* every offloaded parameter's ``.data`` is a permanent typed view into its
+  GPU ring slot, so trap boundaries never rebind tensors (no Python work per
+  tensor, and a whole forward can be captured in one CUDA graph);
+* ``enter(L)``: first label forks the copy stream; if L computes on streamed
+  weights, the compute stream waits for them HERE (as late as possible, which
+  also covers plans whose transfer was issued several traps earlier); if L is
+  a transfer label, its host block is copied into its slot with ONE H2D;
+* ``exit(L)``: marks L's slot free for the next writer; the last label joins.
+
+Wrap-around transfers (compute label earlier than the transfer label) are
+issued once at construction so the first forward finds them resident
+(``src/flextensor/loaders.py:1508-1531``). A pass that raised before its last
+label is recovered at the next pass start by draining the copy stream and
+re-issuing those preloads (``src/flextensor/loaders.py:1538-1551``).
+
+Per-tensor loader (``strategy``): each streamed tensor gets its own device
+buffer from the caching allocator on the copy stream, bound at the compute
+label's ``enter`` and dropped at its ``exit`` (``src/flextensor/loaders.py:677-900``).
+"""
+
+from __future__ import annotations
+
+import logging
+from dataclasses import dataclass, field
+
+import torch
+
+from flextensor_b200.core.host_store import HostBlock, PackedEntry
+
+logger = logging.getLogger(__name__)
+
+
+@dataclass
+class SlotPlan:
+    order: list[str]
+    transfer_slot: dict[str, int]          # transfer label -> slot
+    t2c: dict[str, str]                    # transfer label -> compute label
+    slot_bytes: dict[int, int]
+    host_blocks: dict[str, HostBlock]      # transfer label -> packed host bytes
+    preload: list[str] = field(default_factory=list)  # transfer labels to issue at construction
+
+
+class BlockLoader:
+    kind = "block"
+
+    def __init__(self, device: torch.device, plan: SlotPlan, engine, timing=None):
+        self.device = torch.device(device)
+        self.plan = plan
+        self.engine = engine
+        self.timing = timing
+        self.order = plan.order
+        self.first = plan.order[0] if plan.order else None
+        self.last = plan.order[-1] if plan.order else None
+        self.c2t = {c: t for t, c in plan.t2c.items()}
+        self.compute_slot = {c: plan.transfer_slot[t] for t, c in plan.t2c.items()}
+        self.slots: dict[int, torch.Tensor] = {
+            s: torch.empty(max(n, 256), dtype=torch.uint8, device=self.device) for s, n in plan.slot_bytes.items()
+        }
+        self._pass_active = False
+        self._closed = False
+
+    # -------------------------------------------------------------- views
+    def slot_view(self, transfer_label: str, e: PackedEntry) -> torch.Tensor:
+        s = self.slots[self.plan.transfer_slot[transfer_label]]
+        return s[e.offset:e.offset + e.nbytes].view(e.dtype).view(e.shape)
+
+    def bind(self, params_by_tid: dict[int, torch.nn.Parameter]) -> None:
+        for t, blk in self.plan.host_blocks.items():
+            for e in blk.entries:
+                p = params_by_tid[e.tensor_id]
+                p.data = self.slot_view(t, e)
+
+    def host_views(self, params_by_tid: dict[int, torch.nn.Parameter]) -> None:
+        """Rebind parameters to their packed host bytes (release with preserve_model)."""
+        for blk in self.plan.host_blocks.values():
+            for e in blk.entries:
+                params_by_tid[e.tensor_id].data = blk.view(e)
+
+    @property
+    def blocks_bytes(self) -> int:
+        return sum(t.numel() for t in self.slots.values())
+
+    # -------------------------------------------------------------- schedule
+    def _issue(self, t: str) -> None:
+        blk = self.plan.host_blocks[t]
+        n = blk.data.numel()
+        slot = self.plan.transfer_slot[t]
+        self.engine.submit(slot, self.slots[slot][:n], blk.data, self.plan.t2c[t])
+
+    def preload(self) -> None:
+        if not self.plan.preload:
+            return
+        self.engine.begin()
+        for t in self.plan.preload:
+            self._issue(t)
+        for t in self.plan.preload:
+            self.engine.wait_ready(self.plan.t2c[t])
+        self.engine.join()
+        self.engine.synchronize()
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+
+    def recover(self) -> None:
+        logger.warning("offload pass aborted before its last trap; draining copies and re-issuing preloads")
+        self.engine.reset()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        self._pass_active = False
+        self.preload()
+
+    def enter(self, label: str) -> None:
+        if label == self.first:
+            if self._pass_active:
+                self.recover()
+            self._pass_active = True
+            self.engine.begin()
+            if self.timing is not None:
+                self.timing.on_pass_start()
+        if label in self.compute_slot:
+            self.engine.wait_ready(label)
+        if label in self.plan.transfer_slot:
+            self._issue(label)
+        if self.timing is not None:
+            self.timing.on_enter(label)
+
+    def exit(self, label: str) -> None:
+        if self.timing is not None:
+            self.timing.on_exit(label)
+        if label in self.compute_slot:
+            self.engine.finish_use(self.compute_slot[label])
+        if label == self.last:
+            self.join_after_forward()
+
+    def join_after_forward(self) -> None:
+        if self._pass_active:
+            self.engine.join()
+            self._pass_active = False
+            if self.timing is not None:
+                self.timing.on_pass_end(self.engine)
+
+    def sync_prev_onload(self) -> None:
+        self.engine.synchronize()
+
+    def close(self) -> None:
+        if self._closed:
+            return
+        self._closed = True
+        try:
+            self.engine.synchronize()
+        finally:
+            self.slots.clear()
+
+
+class TensorStrategyLoader:
+    """Per-tensor streaming: device buffers come from the caching allocator."""
+
+    kind = "strategy"
+
+    def __init__(self, device, order, load_strategy: dict[str, list[int]], t2c: dict[str, str],
+                 host_tensors: dict[int, torch.Tensor], params_by_tid: dict[int, torch.nn.Parameter]):
+        self.device = torch.device(device)
+        self.order = order
+        self.first = order[0] if order else None
+        self.last = order[-1] if order else None
+        self.load_strategy = load_strategy
+        self.t2c = t2c
+        self.c2t = {c: t for t, c in t2c.items()}
+        self.host = host_tensors
+        self.params = params_by_tid
+        self.cuda = self.device.type == "cuda"
+        self.stream = torch.cuda.Stream(device=self.device) if self.cuda else None
+        self._staged: dict[str, tuple[list[tuple[int, torch.Tensor]], object]] = {}
+        self.blocks_bytes = 0
+
+    def bind(self, params_by_tid) -> None:
+        for tid, t in self.host.items():
+            params_by_tid[tid].data = t
+
+    def host_views(self, params_by_tid) -> None:
+        self.bind(params_by_tid)
+
+    def preload(self) -> None:
+        pass
+
+    def enter(self, label: str) -> None:
+        if label == self.first and self.cuda:
+            self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        if label in self.c2t:
+            staged = self._staged.pop(label, None)
+            if staged is None:  # first pass of a wrap-around transfer: load synchronously
+                staged = (self._copy(self.load_strategy.get(self.c2t[label], [])), None)
+            bufs, ev = staged
+            if ev is not None:
+                torch.cuda.current_stream(self.device).wait_event(ev)
+            for tid, buf in bufs:
+                if self.cuda:
+                    buf.record_stream(torch.cuda.current_stream(self.device))
+                self.params[tid].data = buf
+        if label in self.t2c:
+            tids = self.load_strategy.get(label, [])
+            if self.cuda:
+                with torch.cuda.stream(self.stream):
+                    bufs = self._copy(tids)
+                    ev = torch.cuda.Event()
+                    ev.record(self.stream)
+            else:
+                bufs, ev = self._copy(tids), None
+            self._staged[self.t2c[label]] = (bufs, ev)
+
+    def _copy(self, tids):
+        return [(tid, self.host[tid].to(self.device, non_blocking=True)) for tid in tids]
+
+    def exit(self, label: str) -> None:
+        if label in self.c2t:
+            for tid in self.load_strategy.get(self.c2t[label], []):
+                self.params[tid].data = self.host[tid]
+        if label == self.last and self.cuda:
+            torch.cuda.current_stream(self.device).wait_stream(self.stream)
+
+    def join_after_forward(self) -> None:
+        if self.cuda:
+            torch.cuda.current_stream(self.device).wait_stream(self.stream)
+
+    def sync_prev_onload(self) -> None:
+        if self.cuda:
+            self.stream.synchronize()
+
+    def close(self) -> None:
+        self._staged.clear()

@@ -1,0 +1,656 @@
+"""TensorManager: the per-model engine behind the DISCOVERY -> PROFILING -> INFERENCE phases.
+
+Phase work (reference: ``src/flextensor/tensor_manager.py:827-915``, ``1661-1800``):
+
+* ``initialize_warmup`` (DISCOVERY): every offloadable unit parameter moves to
+  (pinned) host memory; all other parameters and buffers move to the device.
+  Discovery traps materialise their own tensors on the device for the duration
+  of the trap and record any *other* unit's host tensor the forward touches
+  (``__torch_function__``); such cross-unit tensors become resident, because a
+  streamed tensor may only belong to one trap.
+* ``initialize_profile`` (PROFILING): ``view`` mode stages each trap's tensors
+  into one reusable device buffer with ONE H2D, synchronises, then times only
+  the compute with CUDA events; ``getter``/``torch_function`` copy tensor by
+  tensor.
+* ``initialize_inference``: median durations + per-tensor H2D costs ->
+  :class:`LayerStatistics`; a size-sweep H2D benchmark feeds the interpolator;
+  the strategy plans under the memory budget; host blocks are packed and
+  parameters are bound to ring-slot views.
+
+The plan round-trips through :class:`TensorManagerState` (``profile.json`` v3)
+and is restored by tensor *name*.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import logging
+import time
+from enum import Enum
+from typing import Any
+
+import torch
+from torch import nn
+from torch.overrides import TorchFunctionMode
+
+from flextensor_b200.core.host_store import HostBlock, make_host_pinner, pack_tensors, tensor_nbytes
+from flextensor_b200.core.state import PROFILE_FILENAME, TensorManagerState
+from flextensor_b200.core.stats import (
+    IterativeLayerStatisticsCollector,
+    LayerStatistics,
+    TensorStatistics,
+    compute_layer_statistics,
+)
+from flextensor_b200.planner.common import calculate_transfer_to_compute_map
+from flextensor_b200.planner.protocol import Strategy, StrategyResult
+from flextensor_b200.runtime.engine import make_engine
+from flextensor_b200.runtime.loaders import BlockLoader, SlotPlan, TensorStrategyLoader
+from flextensor_b200.runtime.timing import OffloadTimingCollector
+from flextensor_b200.runtime.units import Unit
+from flextensor_b200.types import GPUMemoryUsage
+
+logger = logging.getLogger(__name__)
+
+
+class TMPhase(Enum):
+    NONE = 0
+    DISCOVERY = 1
+    PROFILING = 2
+    INFERENCE = 3
+
+
+class TrapNestingError(RuntimeError):
+    pass
+
+
+class _ForeignReadMode(TorchFunctionMode):
+    """During discovery: move host tensors of *other* units to the device and record them."""
+
+    def __init__(self, tm: "TensorManager", label: str):
+        super().__init__()
+        self.tm, self.label = tm, label
+        self.cache: dict[int, torch.Tensor] = {}
+
+    def _swap(self, x):
+        if isinstance(x, torch.Tensor) and x.device.type == "cpu" and self.tm.device.type != "cpu":
+            tid = self.tm._host_ptr_to_tid.get(x.data_ptr())
+            if tid is not None:
+                self.tm._foreign_reads.setdefault(tid, set()).add(self.label)
+                d = self.cache.get(tid)
+                if d is None:
+                    d = x.to(self.tm.device, non_blocking=True)
+                    self.cache[tid] = d
+                return d
+        return x
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        args = torch.utils._pytree.tree_map(self._swap, args)
+        kwargs = torch.utils._pytree.tree_map(self._swap, kwargs)
+        return func(*args, **kwargs)
+
+
+class TensorManager:
+    """Owns tensors, traps, plan and loader for one model."""
+
+    def __init__(
+        self,
+        device_gpu: str | torch.device,
+        tensor_manager_load_strategy: Strategy,
+        loader_type: str = "allocation_block_transfer",
+        remove_layers_operations: list[dict[str, Any]] | None = None,
+        blocks: int = 4,
+        move_top_level_buffers_to_gpu: bool = True,
+        *,
+        pinned_memory: bool = True,
+        pinned_memory_mode: str = "torch",
+        profile_mode: str = "view",
+        max_gpu_mem_fraction: float | None = None,
+        offload_timing: str = "off",
+        enable_diagnostics: bool = False,
+        shm_store: Any = None,
+        _compute_transfer_gap: int | None = None,
+        _direct_mode: bool = True,
+        _use_trace_tensor: bool = False,
+        _rearrange_transfers: bool | None = None,
+        _enable_untraced_tensor_discovery: bool = True,
+        _offload_timing_log_every: int = 0,
+        _offload_timing_measure_max_passes: int = 1024,
+    ) -> None:
+        self.device = torch.device(device_gpu)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.strategy = tensor_manager_load_strategy
+        self.loader_type = loader_type
+        self.remove_layers_operations = remove_layers_operations or []
+        self.blocks = blocks
+        self.move_top_level_buffers_to_gpu = move_top_level_buffers_to_gpu
+        self.pinned_memory = pinned_memory and self.device.type == "cuda"
+        self.pinner = make_host_pinner(self.pinned_memory, pinned_memory_mode)
+        self.profile_mode = profile_mode
+        self.max_gpu_mem_fraction = max_gpu_mem_fraction
+        self.offload_timing = offload_timing
+        self.enable_diagnostics = enable_diagnostics
+        self.shm_store = shm_store
+        self.compute_transfer_gap = _compute_transfer_gap
+        self.phase = TMPhase.NONE
+
+        self.model: nn.Module | None = None
+        self.units: list[Unit] = []
+        self.labels: list[str] = []
+        self.id_to_name: dict[int, str] = {}
+        self.name_to_id: dict[str, int] = {}
+        self.params_by_tid: dict[int, nn.Parameter] = {}
+        self.owner: dict[int, str] = {}                # offloadable tid -> unit label
+        self.unit_tids: dict[str, list[int]] = {}
+        self.host: dict[int, torch.Tensor] = {}        # offloadable tid -> host tensor
+        self._host_ptr_to_tid: dict[int, int] = {}
+        self.resident: set[int] = set()                # tids permanently on device
+        self._foreign_reads: dict[int, set[str]] = {}
+        self.collector = IterativeLayerStatisticsCollector()
+        self._trap_depth = 0
+        self._suspend = 0
+        self._staging: torch.Tensor | None = None
+        self.loader: BlockLoader | TensorStrategyLoader | None = None
+        self.state: TensorManagerState | None = None
+        self.layer_stats: list[LayerStatistics] = []
+        self.memory_stats: dict[int, float] | None = None
+        self.strategy_result: StrategyResult | None = None
+        self.timing = OffloadTimingCollector(self.device, offload_timing) if offload_timing != "off" else None
+        self._orig_device: dict[int, torch.device] = {}
+        self.unmapped_bytes = 0
+        self.load_from_shm = False
+        self._state_restored_from_profile = False
+
+    # ================================================================== model / units
+    def set_model(self, model: nn.Module) -> None:
+        self.model = model
+        names = [n for n, _ in model.named_parameters(remove_duplicate=True)]
+        self.id_to_name = dict(enumerate(names))
+        self.name_to_id = {n: i for i, n in self.id_to_name.items()}
+        self.params_by_tid = {self.name_to_id[n]: p for n, p in model.named_parameters(remove_duplicate=True)}
+
+    def set_units(self, units: list[Unit]) -> None:
+        self.units = units
+        self.labels = [u.label for u in units]
+        pid_to_tid = {id(p): t for t, p in self.params_by_tid.items()}
+        self.owner, self.unit_tids = {}, {}
+        for u in units:
+            tids = [pid_to_tid[id(p)] for _, p in u.params if id(p) in pid_to_tid]
+            self.unit_tids[u.label] = tids
+            for t in tids:
+                self.owner[t] = u.label
+
+    def build_parameters_mapping(self, model: nn.Module | dict[str, torch.Tensor]) -> None:
+        if isinstance(model, nn.Module):
+            self.set_model(model)
+
+    # ================================================================== placement helpers
+    def _to_host(self, tid: int) -> None:
+        p = self.params_by_tid[tid]
+        self._orig_device.setdefault(tid, p.device)
+        t = p.data
+        p.requires_grad_(False)
+        if t.device.type == "meta":
+            # follower of a shared store: bytes arrive from SHM weight blocks later
+            self.host[tid] = t
+            return
+        if t.device.type != "cpu":
+            t = t.to("cpu")
+        if self.pinned_memory:
+            t = self.pinner.pin(t)
+        p.data = t
+        self.host[tid] = t
+        self._host_ptr_to_tid[t.data_ptr()] = tid
+
+    def _to_device(self, tid: int) -> None:
+        p = self.params_by_tid[tid]
+        self._orig_device.setdefault(tid, p.device)
+        if p.device != self.device:
+            p.data = p.data.to(self.device)
+        self.resident.add(tid)
+        old = self.host.pop(tid, None)
+        if old is not None:
+            self._host_ptr_to_tid.pop(old.data_ptr(), None)
+
+    def _move_non_unit_to_device(self) -> None:
+        for tid in self.params_by_tid:
+            if tid not in self.owner:
+                self._to_device(tid)
+        for _, b in self.model.named_buffers():
+            if b.device != self.device:
+                b.data = b.data.to(self.device)
+
+    # ================================================================== phases
+    def initialize_warmup(self) -> nn.Module:
+        assert self.model is not None, "set_model first"
+        with torch.no_grad():
+            for tid in self.owner:
+                self._to_host(tid)
+            self._move_non_unit_to_device()
+        self.phase = TMPhase.DISCOVERY
+        return self.model
+
+    def static_discovery(self) -> None:
+        """skip_discovery: a trap's tensors are exactly its unit's parameters."""
+        for label, tids in self.unit_tids.items():
+            self.collector.record_tensors(label, tids)
+
+    def initialize_profile(self) -> nn.Module:
+        # cross-unit reads seen in discovery -> resident
+        for tid, readers in self._foreign_reads.items():
+            if tid in self.owner:
+                logger.info("tensor %s is read by %s outside its trap; keeping it resident",
+                            self.id_to_name[tid], sorted(readers))
+                with torch.no_grad():
+                    self._to_device(tid)
+                for label in list(self.unit_tids):
+                    if tid in self.unit_tids[label]:
+                        self.unit_tids[label].remove(tid)
+                self.owner.pop(tid, None)
+        for label in self.labels:
+            if label not in self.collector.labels():
+                self.collector.record_tensors(label, self.unit_tids.get(label, []))
+        if self.profile_mode == "view":
+            need = max((self._trap_bytes(l) for l in self.labels), default=0)
+            self._staging = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+        self.phase = TMPhase.PROFILING
+        return self.model
+
+    def _offloadable(self, label: str) -> list[int]:
+        return [t for t in self.unit_tids.get(label, []) if t in self.host]
+
+    def _trap_bytes(self, label: str) -> int:
+        from flextensor_b200.core.host_store import packed_layout
+
+        return packed_layout([tensor_nbytes(self.host[t]) for t in self._offloadable(label)])[1]
+
+    # ================================================================== traps
+    def is_profiling_suspended(self) -> bool:
+        return self._suspend > 0
+
+    def suspend_profiling(self) -> None:
+        self._suspend += 1
+
+    def resume_profiling(self) -> None:
+        if self._suspend <= 0:
+            raise RuntimeError("resume_profiling() without a matching suspend_profiling()")
+        self._suspend -= 1
+
+    @contextlib.contextmanager
+    def pause_profiling(self):
+        self.suspend_profiling()
+        try:
+            yield
+        finally:
+            self.resume_profiling()
+
+    def clear_profiling_durations(self) -> None:
+        self.collector.clear_durations()
+
+    @contextlib.contextmanager
+    def trap(self, name: str):
+        if self._trap_depth:
+            raise TrapNestingError(f"nested trap {name!r}: offload units may not contain each other")
+        self._trap_depth += 1
+        try:
+            if self.phase == TMPhase.DISCOVERY:
+                with self._discovery_trap(name):
+                    yield
+            elif self.phase == TMPhase.PROFILING:
+                with self._profile_trap(name):
+                    yield
+            elif self.phase == TMPhase.INFERENCE and self.loader is not None:
+                self.loader.enter(name)
+                try:
+                    yield
+                finally:
+                    self.loader.exit(name)
+            else:
+                yield
+        finally:
+            self._trap_depth -= 1
+
+    @contextlib.contextmanager
+    def _discovery_trap(self, label: str):
+        tids = self._offloadable(label)
+        with torch.no_grad():
+            for t in tids:
+                self.params_by_tid[t].data = self.host[t].to(self.device, non_blocking=True)
+        mode = _ForeignReadMode(self, label)
+        try:
+            with mode:
+                yield
+        finally:
+            if self.device.type == "cuda":
+                torch.cuda.current_stream(self.device).synchronize()
+            for t in tids:
+                self.params_by_tid[t].data = self.host[t]
+            self.collector.record_tensors(label, self.unit_tids.get(label, []))
+
+    def _now_events(self):
+        if self.device.type == "cuda":
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            return a, b
+        return None, None
+
+    @contextlib.contextmanager
+    def _profile_trap(self, label: str):
+        tids = self._offloadable(label)
+        cuda = self.device.type == "cuda"
+        with torch.no_grad():
+            if self.profile_mode == "view" and self._staging is not None:
+                from flextensor_b200.core.host_store import packed_layout
+
+                offs, _ = packed_layout([tensor_nbytes(self.host[t]) for t in tids])
+                for t, o in zip(tids, offs):
+                    h = self.host[t]
+                    v = self._staging[o:o + tensor_nbytes(h)].view(h.dtype).view(h.shape)
+                    v.copy_(h, non_blocking=True)
+                    self.params_by_tid[t].data = v
+            else:
+                for t in tids:
+                    self.params_by_tid[t].data = self.host[t].to(self.device, non_blocking=True)
+        if cuda:
+            torch.cuda.current_stream(self.device).synchronize()
+            start, end = self._now_events()
+            start.record()
+        t0 = time.perf_counter()
+        try:
+            yield
+        finally:
+            if cuda:
+                end.record()
+                end.synchronize()
+                ms = start.elapsed_time(end)
+            else:
+                ms = (time.perf_counter() - t0) * 1e3
+            for t in tids:
+                self.params_by_tid[t].data = self.host[t]
+            if not self.is_profiling_suspended():
+                self.collector.record_duration(label, ms)
+
+    # ================================================================== inference planning
+    def _benchmark_sizes(self, sizes: list[int], reps: int = 3) -> dict[int, float]:
+        """Median H2D ms per size from pinned host memory (CPU device: memcpy timing)."""
+        from flextensor_b200.core.host_store import alloc_host_bytes
+
+        out: dict[int, float] = {}
+        if not sizes:
+            return out
+        big = max(sizes)
+        src = alloc_host_bytes(big, self.pinned_memory)
+        dst = torch.empty(big, dtype=torch.uint8, device=self.device)
+        for s in sorted(set(sizes)):
+            samples = []
+            for _ in range(reps):
+                if self.device.type == "cuda":
+                    a, b = self._now_events()
+                    a.record()
+                    dst[:s].copy_(src[:s], non_blocking=True)
+                    b.record()
+                    b.synchronize()
+                    samples.append(a.elapsed_time(b))
+                else:
+                    t0 = time.perf_counter()
+                    dst[:s].copy_(src[:s])
+                    samples.append(max((time.perf_counter() - t0) * 1e3, 1e-6))
+            samples.sort()
+            out[s] = max(samples[len(samples) // 2], 1e-6)
+        del src, dst
+        return out
+
+    def get_memory_transfer_stats(self) -> dict[int, float] | None:
+        return self.memory_stats
+
+    def benchmark_memory_transfers(self, max_bytes: int) -> dict[int, float]:
+        """Power-of-two size sweep up to the largest label (capped at 4 GiB)."""
+        top = min(max(max_bytes, 1 << 20), 4 << 30)
+        sizes, s = [], 1 << 16
+        while s < top:
+            sizes.append(s)
+            s <<= 1
+        sizes.append(top)
+        return self._benchmark_sizes(sizes)
+
+    def _tensor_statistics(self) -> dict[int, TensorStatistics]:
+        sizes = {tensor_nbytes(self.host[t]) for t in self.host}
+        ms = self._benchmark_sizes(sorted(sizes), reps=3)
+        return {t: TensorStatistics(tensor_id=t, name=self.id_to_name[t], size_bytes=tensor_nbytes(h),
+                                    load_time_ms=ms[tensor_nbytes(h)]) for t, h in self.host.items()}
+
+    def _gpu_budget(self) -> int | None:
+        if self.max_gpu_mem_fraction is None:
+            return None
+        from flextensor_b200.runtime.gpu_budget import resolve_gpu_budget
+
+        invisible = sum(tensor_nbytes(self.params_by_tid[t].data) for t in self.resident if t not in self.owner)
+        invisible += sum(b.numel() * b.element_size() for b in self.model.buffers())
+        return resolve_gpu_budget(self.device, self.max_gpu_mem_fraction, invisible)
+
+    def initialize_inference(self) -> nn.Module:
+        self._staging = None
+        rows = [r for r in self.collector.get_layer_stats() if r.label in self.unit_tids]
+        untimed = [r.label for r in rows if r.duration is None]
+        if untimed:
+            logger.warning("traps never timed during profiling (kept resident): %s", untimed)
+        tstats = self._tensor_statistics()
+        tstats = {t: s for t, s in tstats.items() if t in self.owner}
+        self.layer_stats = compute_layer_statistics(rows, tstats)
+        max_label = max((sum(t.size_bytes for t in l.tensors) for l in self.layer_stats), default=1 << 20)
+        self.memory_stats = self.benchmark_memory_transfers(max_label)
+        budget = self._gpu_budget()
+        result = self.strategy.compute(self.layer_stats, self.memory_stats, budget)
+        self.strategy_result = result
+        self._build_from_result(result)
+        if self.enable_diagnostics:
+            from flextensor_b200.runtime.diagnostics import log_plan
+
+            log_plan(self)
+        return self.model
+
+    # ---------------------------------------------------------------- plan -> runtime
+    def _build_from_result(self, result: StrategyResult) -> None:
+        order = [l.label for l in self.layer_stats]
+        load = {k: [t.tensor_id for t in v] for k, v in result.strategy_map.items() if v}
+        t2c = (result.block_data.transfer_to_compute_map if result.block_data is not None
+               else calculate_transfer_to_compute_map(self.layer_stats, result.strategy_map))
+        l2b = result.block_data.label_to_block_id if result.block_data is not None else {}
+        self._build_runtime(order, load, t2c, l2b)
+        self.state = self.export_state()
+
+    def _build_runtime(self, order: list[str], load: dict[str, list[int]], t2c: dict[str, str],
+                       l2b: dict[str, int]) -> None:
+        streamed = {t for ts in load.values() for t in ts}
+        with torch.no_grad():
+            for tid in list(self.host):
+                if tid not in streamed:
+                    self._to_device(tid)
+        self.unmapped_bytes = sum(tensor_nbytes(self.params_by_tid[t].data) for t in self.resident)
+        idx = {l: i for i, l in enumerate(order)}
+        if self.loader_type == "strategy":
+            self.loader = TensorStrategyLoader(self.device, order, load, {k: t2c[k] for k in load}, dict(self.host),
+                                               self.params_by_tid)
+            self.loader.bind(self.params_by_tid)
+            self.phase = TMPhase.INFERENCE
+            return
+        host_blocks: dict[str, HostBlock] = {}
+        for label in order:
+            tids = load.get(label)
+            if not tids:
+                continue
+            items = [(t, self.id_to_name[t], self.host[t]) for t in tids]
+            buf = self.shm_store.block_buffer(label, items) if self.shm_store is not None else None
+            if buf is not None and self.load_from_shm:
+                from flextensor_b200.core.host_store import PackedEntry, packed_layout
+
+                offs, _ = packed_layout([tensor_nbytes(h) for _, _, h in items])
+                blk = HostBlock(label, buf, [PackedEntry(t, n, o, tensor_nbytes(h), h.dtype, tuple(h.shape))
+                                             for (t, n, h), o in zip(items, offs)])
+            else:
+                blk = pack_tensors(label, items, buffer=buf, pinned=self.pinned_memory,
+                                   release_sources=self._release_host)
+            host_blocks[label] = blk
+        slot_of = {l: l2b.get(l, i % max(2, self.blocks)) for i, l in enumerate(host_blocks)}
+        slot_bytes: dict[int, int] = {}
+        for l, b in slot_of.items():
+            slot_bytes[b] = max(slot_bytes.get(b, 0), host_blocks[l].data.numel())
+        preload = [t for t in host_blocks if idx[t2c[t]] <= idx[t]]
+        plan = SlotPlan(order=order, transfer_slot=slot_of, t2c={t: t2c[t] for t in host_blocks},
+                        slot_bytes=slot_bytes, host_blocks=host_blocks, preload=preload)
+        engine = make_engine(self.device, max(slot_bytes, default=0) + 1,
+                             timing=self.timing is not None, external_events=self.offload_timing == "cuda_graph")
+        self.loader = BlockLoader(self.device, plan, engine, timing=self.timing)
+        self.loader.bind(self.params_by_tid)
+        self.loader.preload()
+        self.phase = TMPhase.INFERENCE
+
+    def _release_host(self, tid: int) -> None:
+        old = self.host.get(tid)
+        if old is not None:
+            self._host_ptr_to_tid.pop(old.data_ptr(), None)
+
+    # ================================================================== state / profile
+    def export_state(self) -> TensorManagerState:
+        r = self.strategy_result
+        if self.loader is None:
+            raise RuntimeError("no inference plan yet")
+        load = {}
+        if r is not None:
+            load = {k: list(v) for k, v in r.strategy_map.items() if v}
+        elif self.state is not None:
+            load = self.state.load_strategy
+        bd = r.block_data if r is not None else None
+        if isinstance(self.loader, BlockLoader):
+            alloc: dict[int, list[str]] = {}
+            for l in self.loader.order:
+                if l in self.loader.plan.transfer_slot:
+                    alloc.setdefault(self.loader.plan.transfer_slot[l], []).append(l)
+            l2b = dict(self.loader.plan.transfer_slot)
+            bsz = {b: int(n) for b, n in self.loader.plan.slot_bytes.items()}
+            lsz = {l: int(b.data.numel()) for l, b in self.loader.plan.host_blocks.items()}
+            t2c = dict(self.loader.plan.t2c)
+        else:
+            alloc, l2b, bsz = {}, {}, {}
+            lsz = {k: sum(t.size_bytes for t in v) for k, v in load.items()}
+            t2c = dict(self.loader.t2c)
+        if bd is not None and not t2c:
+            t2c = dict(bd.transfer_to_compute_map)
+        view_ids = sorted(t for ts in load.values() for t in (x.tensor_id for x in ts))
+        dt, lay = {}, {}
+        for tid in view_ids:
+            p = self.params_by_tid[tid]
+            nm = self.id_to_name[tid]
+            dt[nm] = str(p.dtype).replace("torch.", "")
+            lay[nm] = {"shape": list(p.shape), "stride": list(p.stride())}
+        return TensorManagerState(
+            loader_type=self.loader_type,
+            tensor_id_to_name_map=dict(self.id_to_name),
+            allocation_ordered=alloc,
+            label_to_size_map=lsz,
+            block_sizes=bsz,
+            load_strategy=load,
+            release_strategy={},
+            label_to_block_id=l2b,
+            stats=list(self.layer_stats),
+            transfer_to_compute_map=t2c,
+            view_tensors_ids=view_ids,
+            view_tensors_names=[self.id_to_name[t] for t in view_ids],
+            gpu_tensors_names=sorted(self.id_to_name[t] for t in self.resident),
+            shm_block_name_map=(self.shm_store.block_name_map() if self.shm_store is not None else None),
+            managed_tensor_dtypes=dt,
+            managed_tensor_layouts=lay,
+        )
+
+    def save_profile(self, profile_directory: str) -> None:
+        import pathlib
+
+        st = self.state or self.export_state()
+        TensorManagerState.save_to_file(pathlib.Path(profile_directory) / PROFILE_FILENAME, st)
+
+    def load_state(self, profile_directory: str) -> TensorManagerState:
+        import pathlib
+
+        return TensorManagerState.load_from_file(pathlib.Path(profile_directory) / PROFILE_FILENAME)
+
+    def load_profile(self, profile_directory: str, model: nn.Module) -> None:
+        self.restore_state(self.load_state(profile_directory), model)
+
+    def restore_state(self, state: TensorManagerState, model: nn.Module | None = None) -> None:
+        """Adopt a saved plan: rebind ids by name, then build the loader directly (no profiling)."""
+        if model is not None and model is not self.model:
+            self.set_model(model)
+        name_to_tid = self.name_to_id
+        missing = [t.name for ts in state.load_strategy.values() for t in ts if t.name not in name_to_tid]
+        if missing:
+            raise ValueError(f"Saved state mismatch: {len(missing)} streamed tensors not in the model "
+                             f"(e.g. {missing[:3]}). Re-profile the model.")
+        self.layer_stats = [
+            LayerStatistics(label=s.label, duration=s.duration, tensors=[
+                TensorStatistics(tensor_id=name_to_tid[t.name], name=t.name, size_bytes=t.size_bytes,
+                                 load_time_ms=t.load_time_ms) for t in s.tensors if t.name in name_to_tid])
+            for s in state.stats]
+        load = {k: [name_to_tid[t.name] for t in v] for k, v in state.load_strategy.items() if v}
+        self.strategy_result = StrategyResult(strategy_map={
+            k: [TensorStatistics(tensor_id=name_to_tid[t.name], name=t.name, size_bytes=t.size_bytes,
+                                 load_time_ms=t.load_time_ms) for t in v] for k, v in state.load_strategy.items()})
+        self._state_restored_from_profile = True
+        if self.phase == TMPhase.NONE:
+            self.initialize_warmup()
+        self._build_runtime([s.label for s in state.stats], load, dict(state.transfer_to_compute_map),
+                            dict(state.label_to_block_id))
+        self.state = state
+
+    # ================================================================== misc API
+    def get_gpu_memory_usage(self) -> GPUMemoryUsage:
+        blocks = self.loader.blocks_bytes if self.loader is not None else 0
+        unmapped = sum(tensor_nbytes(self.params_by_tid[t].data) for t in self.resident)
+        return GPUMemoryUsage(blocks_bytes=int(blocks), unmapped_tensors_bytes=int(unmapped),
+                              total_bytes=int(blocks + unmapped))
+
+    def collect_offload_timing(self):
+        return self.timing.report() if self.timing is not None else None
+
+    def reset_offload_timing(self) -> None:
+        if self.timing is not None:
+            self.timing.reset()
+
+    def sync_prev_onload(self) -> None:
+        if self.loader is not None:
+            self.loader.sync_prev_onload()
+
+    def join_after_forward(self) -> None:
+        if self.loader is not None:
+            self.loader.join_after_forward()
+
+    def release_memory(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    def shutdown(self, *, preserve_model: bool = True) -> None:
+        """Tear down the loader; with ``preserve_model`` every parameter ends up on the host."""
+        with torch.no_grad():
+            if self.loader is not None:
+                if preserve_model:
+                    self.loader.host_views(self.params_by_tid)
+                    for tid, p in self.params_by_tid.items():
+                        if p.device.type != "cpu":
+                            p.data = p.data.to("cpu")
+                        else:
+                            p.data = p.data.clone()
+                self.loader.close()
+                self.loader = None
+            elif preserve_model and self.model is not None:
+                for p in self.params_by_tid.values():
+                    if p.device.type != "cpu":
+                        p.data = p.data.to("cpu")
+            if preserve_model and self.model is not None:
+                for _, b in self.model.named_buffers():
+                    if b.device.type != "cpu":
+                        b.data = b.data.to("cpu")
+        self.pinner.release_all()
+        if self.shm_store is not None:
+            self.shm_store.close(unlink=not self.load_from_shm)
+        self.host.clear()
+        self._host_ptr_to_tid.clear()
+        self.phase = TMPhase.NONE

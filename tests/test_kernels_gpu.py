@@ -1,0 +1,158 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references (GPU only)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover - CPU collection
+    pytest.skip("CUDA device required", allow_module_level=True)
+
+from flextensor_b200 import ops  # noqa: E402
+from flextensor_b200.ops import native  # noqa: E402
+
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+def _lin_ref(x, w, b=None):
+    y = x.float() @ w.float().t()
+    return y + b.float() if b is not None else y
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 320), (1000, 384, 512), (4096, 5120, 5120),
+                                   (257, 64, 128), (130, 136, 72)])
+def test_gemm_plain(M, N, K):
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    y = ops.linear(x, w, None, epi="none")
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    assert rel_err(y, _lin_ref(x, w)) < 1e-2
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_tile_widths(bn):
+    torch.manual_seed(1)
+    x = torch.randn(700, 1024, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(768, 1024, device=DEV, dtype=torch.bfloat16) / 32
+    y = ops.linear(x, w, None, epi="none", force_bn=bn)
+    assert rel_err(y, _lin_ref(x, w)) < 1e-2
+
+
+def test_gemm_epilogues():
+    torch.manual_seed(2)
+    M, N, K = 513, 1024, 768
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    b = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    ref = _lin_ref(x, w, b)
+    assert rel_err(ops.linear(x, w, b, epi="bias"), ref) < 1e-2
+    g = torch.nn.functional.gelu(ref, approximate="tanh")
+    assert rel_err(ops.linear(x, w, b, epi="gelu"), g) < 1e-2
+    res = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    gate = torch.randn(N, device=DEV, dtype=torch.float32)
+    assert rel_err(ops.linear(x, w, b, epi="gate_res", residual=res, gate=gate), res.float() + gate * ref) < 1e-2
+    assert rel_err(ops.linear(x, w, b, epi="res", residual=res), res.float() + ref) < 1e-2
+    # in place: out aliases residual
+    r2 = res.clone()
+    ops.linear(x, w, b, epi="gate_res", residual=r2, gate=gate, out=r2)
+    assert rel_err(r2, res.float() + gate * ref) < 1e-2
+    # per-sample gates
+    gate2 = torch.randn(2, N, device=DEV, dtype=torch.float32)
+    rows = (M + 1) // 2
+    y = ops.linear(x, w, b, epi="gate_res", residual=res, gate=gate2, gate_rows=rows)
+    gfull = torch.cat([gate2[0].expand(rows, N), gate2[1].expand(M - rows, N)])
+    assert rel_err(y, res.float() + gfull * ref) < 1e-2
+
+
+def test_gemm_strided_views():
+    torch.manual_seed(3)
+    big = torch.randn(400, 3 * 512, device=DEV, dtype=torch.bfloat16)
+    x = big[:, 512:1024]                      # strided A (row stride 1536)
+    w = torch.randn(256, 512, device=DEV, dtype=torch.bfloat16) / 22
+    out = torch.zeros(400, 3 * 256, device=DEV, dtype=torch.bfloat16)
+    ops.linear(x, w, None, epi="none", out=out[:, 256:512])
+    assert rel_err(out[:, 256:512], _lin_ref(x, w)) < 1e-2
+    assert out[:, :256].abs().sum().item() == 0 and out[:, 512:].abs().sum().item() == 0
+
+
+def test_layernorm_modulate():
+    torch.manual_seed(4)
+    M, D = 777, 5120
+    x = (torch.randn(M, D, device=DEV) * 3 + 1).bfloat16()
+    sc = torch.randn(D, device=DEV) * 0.1
+    sh = torch.randn(D, device=DEV) * 0.1
+    ref = torch.nn.functional.layer_norm(x.float(), (D,), eps=1e-6) * (1 + sc) + sh
+    assert rel_err(ops.layernorm_modulate(x, sc, sh), ref) < 1e-2
+    w = torch.randn(D, device=DEV)
+    b = torch.randn(D, device=DEV)
+    ref2 = torch.nn.functional.layer_norm(x.float(), (D,), w, b, eps=1e-6)
+    assert rel_err(ops.layernorm_modulate(x, weight=w, bias=b), ref2) < 1e-2
+
+
+def test_rmsnorm_and_rope():
+    torch.manual_seed(5)
+    S, H, Dh = 300, 8, 128
+    x = torch.randn(2 * S, H * Dh, device=DEV).bfloat16()
+    w = torch.randn(H * Dh, device=DEV)
+    ref = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w
+    assert rel_err(ops.rmsnorm(x, w), ref) < 1e-2
+    ang = torch.randn(S, Dh // 2, device=DEV)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    y = ops.qk_rmsnorm_rope(x, w, cos, sin, Dh, S)
+    r = ref.view(2, S, H, Dh // 2, 2)
+    re, im = r[..., 0], r[..., 1]
+    c, s = cos[None, :, None, :], sin[None, :, None, :]
+    rot = torch.stack([re * c - im * s, re * s + im * c], -1).view(2 * S, H * Dh)
+    assert rel_err(y, rot) < 1e-2
+
+
+def _attn_ref(q, k, v, causal=False):
+    qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
+    if kf.shape[1] != qf.shape[1]:
+        rep = qf.shape[1] // kf.shape[1]
+        kf = kf.repeat_interleave(rep, 1)
+        vf = vf.repeat_interleave(rep, 1)
+    o = torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=causal)
+    return o.transpose(1, 2)
+
+
+@pytest.mark.parametrize("B,Sq,Sk,H,Hk", [(1, 128, 128, 1, 1), (2, 300, 300, 4, 4), (1, 256, 512, 2, 2),
+                                          (2, 200, 77, 3, 3), (1, 384, 384, 8, 2), (1, 1000, 1000, 2, 2)])
+def test_attention(B, Sq, Sk, H, Hk):
+    torch.manual_seed(6)
+    q = torch.randn(B, Sq, H, 128, device=DEV).bfloat16()
+    k = torch.randn(B, Sk, Hk, 128, device=DEV).bfloat16()
+    v = torch.randn(B, Sk, Hk, 128, device=DEV).bfloat16()
+    o = ops.attention(q, k, v)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    assert rel_err(o, _attn_ref(q, k, v)) < 2e-2
+
+
+def test_attention_causal():
+    torch.manual_seed(7)
+    q = torch.randn(2, 500, 4, 128, device=DEV).bfloat16()
+    k = torch.randn(2, 500, 4, 128, device=DEV).bfloat16()
+    v = torch.randn(2, 500, 4, 128, device=DEV).bfloat16()
+    o = ops.attention(q, k, v, causal=True)
+    assert rel_err(o, _attn_ref(q, k, v, causal=True)) < 2e-2
+
+
+def test_attention_large_logits():
+    # exercises the deferred-rescale path: logits grow along the key axis
+    torch.manual_seed(8)
+    q = torch.randn(1, 256, 2, 128, device=DEV).bfloat16()
+    k = (torch.randn(1, 1024, 2, 128, device=DEV) * torch.linspace(0.2, 3, 1024, device=DEV)[None, :, None, None]
+         ).bfloat16()
+    v = torch.randn(1, 1024, 2, 128, device=DEV).bfloat16()
+    o = ops.attention(q, k, v)
+    assert rel_err(o, _attn_ref(q, k, v)) < 2e-2
