@@ -69,11 +69,13 @@ class BlockLoader:
         s = self.slots[self.plan.transfer_slot[transfer_label]]
         return s[e.offset:e.offset + e.nbytes].view(e.dtype).view(e.shape)
 
-    def bind(self, params_by_tid: dict[int, torch.nn.Parameter]) -> None:
+    def bind(self, params_by_tid: dict[int, torch.nn.Parameter], setter=None) -> None:
         for t, blk in self.plan.host_blocks.items():
             for e in blk.entries:
-                p = params_by_tid[e.tensor_id]
-                p.data = self.slot_view(t, e)
+                if setter is not None:
+                    setter(e.tensor_id, self.slot_view(t, e))
+                else:
+                    params_by_tid[e.tensor_id].data = self.slot_view(t, e)
 
     def host_views(self, params_by_tid: dict[int, torch.nn.Parameter]) -> None:
         """Rebind parameters to their packed host bytes (release with preserve_model)."""

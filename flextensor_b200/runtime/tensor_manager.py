@@ -480,7 +480,8 @@ class TensorManager:
             if not tids:
                 continue
             items = [(t, self.id_to_name[t], self.host[t]) for t in tids]
-            buf = self.shm_store.block_buffer(label, items) if self.shm_store is not None else None
+            buf = (self.shm_store.block_buffer(label, items, must_exist=self.load_from_shm)
+                   if self.shm_store is not None else None)
             if buf is not None and self.load_from_shm:
                 from flextensor_b200.core.host_store import PackedEntry, packed_layout
 
@@ -501,9 +502,25 @@ class TensorManager:
         engine = make_engine(self.device, max(slot_bytes, default=0) + 1,
                              timing=self.timing is not None, external_events=self.offload_timing == "cuda_graph")
         self.loader = BlockLoader(self.device, plan, engine, timing=self.timing)
-        self.loader.bind(self.params_by_tid)
+        self.loader.bind(self.params_by_tid, setter=self._set_param)
         self.loader.preload()
         self.phase = TMPhase.INFERENCE
+
+    def _set_param(self, tid: int, t: torch.Tensor) -> None:
+        """Point parameter ``tid`` at ``t``; a ``meta`` parameter (SHM follower) is replaced by a new one."""
+        p = self.params_by_tid[tid]
+        if not p.is_meta:
+            p.data = t
+            return
+        newp = nn.Parameter(t, requires_grad=False)
+        name = self.id_to_name[tid]
+        for n, q in list(self.model.named_parameters(remove_duplicate=False)):
+            if q is p:
+                mod_path, _, leaf = n.rpartition(".")
+                mod = self.model.get_submodule(mod_path) if mod_path else self.model
+                setattr(mod, leaf, newp)
+        self.params_by_tid[tid] = newp
+        _ = name
 
     def _release_host(self, tid: int) -> None:
         old = self.host.get(tid)

@@ -24,10 +24,14 @@ class ShmWeightStore:
         self._names: dict[str, str] = {}
         self._next = 0
 
-    def block_buffer(self, label: str, items: list[tuple[int, str, torch.Tensor]]) -> torch.Tensor:
+    def block_buffer(self, label: str, items: list[tuple[int, str, torch.Tensor]],
+                     must_exist: bool = False) -> torch.Tensor:
         _, total = packed_layout([tensor_nbytes(t) for _, _, t in items])
         name = weight_block_name(self.ns, self._next)
         self._next += 1
+        if must_exist and not shm_exists(name):
+            raise FileNotFoundError(f"SHM weight block {name} for {label!r} does not exist; the creator has not "
+                                    "published it (or already released it)")
         if shm_exists(name):
             seg = ShmSegment.attach(name)
             if seg.size < total:

@@ -136,11 +136,14 @@ class SharedTensorStore:
     def materialize_into(self, model: nn.Module, device: torch.device | str) -> None:
         for e in self.entries:
             src = self.tensor(e).to(device)
+            if device == "cpu" or str(device) == "cpu":
+                src = src.clone()  # never alias the shared mapping from a live module
+            obj = nn.Parameter(src, requires_grad=e["requires_grad"]) if e["kind"] == "parameter" else None
             for alias in e["aliases"]:
                 mod_path, _, leaf = alias.rpartition(".")
                 mod = model.get_submodule(mod_path) if mod_path else model
-                if e["kind"] == "parameter":
-                    setattr(mod, leaf, nn.Parameter(src, requires_grad=e["requires_grad"]))
+                if obj is not None:
+                    setattr(mod, leaf, obj)
                 else:
                     mod.register_buffer(leaf, src, persistent=bool(e["persistent"][0]) if e["persistent"] else True)
 
