@@ -34,4 +34,4 @@ def test_rope_table_splits():
     # first 22 pairs depend only on the frame index, the next 21 only on the row
     c = cos.view(2, 3, 4, 64)
     assert torch.allclose(c[:, :, :1, :22].expand(2, 3, 4, 22), c[..., :22])
-    assert torch.allclose(c[:, :1, :, 22:43].expand(2, 3, 4, 21), c[..., 22:43])
+    assert torch.allclose(c[:1, :, :1, 22:43].expand(2, 3, 4, 21), c[..., 22:43])
