@@ -218,7 +218,20 @@ class OffloadManager:
             with tm.trap(label):
                 return fn(*args, **kwargs)
 
-        mod.forward = patched_forward
+        def op_forward(*args, **kwargs):
+            # external_compile in INFERENCE: trap boundaries are opaque custom ops, so a
+            # caller's torch.compile of the unit keeps the prefetch schedule in its graph
+            tm = tm_ref._tm
+            if tm is None or tm_ref.phase != OffloadPhase.INFERENCE:
+                return patched_forward(*args, **kwargs)
+            mid = tm_ref.compiled_offload_manager_id
+            carrier = tm_ref._carrier
+            torch.ops.flextensor_b200.pre_compute(carrier, label, mid)
+            out = orig(*args, **kwargs)
+            torch.ops.flextensor_b200.post_compute(carrier, label, mid)
+            return out
+
+        mod.forward = op_forward if self.config.external_compile else patched_forward
 
     def _unpatch(self) -> None:
         for u in self.units:
@@ -314,6 +327,10 @@ class OffloadManager:
 
     def _enter_inference(self) -> None:
         self.phase = OffloadPhase.INFERENCE
+        if self.config.external_compile:
+            from flextensor_b200.runtime import custom_ops
+
+            self._carrier = custom_ops.carrier_for(self._tm.device)
         if self._compile_fn is not None:
             for u in self.units:
                 core = _UnitCore(self._orig_forwards[u.label])

@@ -174,3 +174,22 @@ def test_disabled_preloads():
     ref = m(x).detach().clone()
     mm = ft.offload(m, cfg(enabled=False))
     assert torch.equal(mm(x), ref)
+
+
+def test_custom_ops_external_compile_path():
+    from flextensor_b200.runtime import custom_ops  # noqa: F401  (registers the ops)
+
+    m, x = make()
+    ref = m(x).detach().clone()
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg(external_compile=True))
+    for _ in range(om.iters_before_inference):
+        mm(x)
+    assert om.phase.value == "inference"
+    for _ in range(3):
+        with torch.no_grad():
+            assert torch.equal(mm(x), ref)
+    # the boundary ops are registered with a fake impl (traceable by dynamo / opcheck)
+    t = torch.zeros(1)
+    torch.library.opcheck(torch.ops.flextensor_b200.pre_compute.default, (t, "nope", 0),
+                          test_utils=("test_schema", "test_faketensor"))
