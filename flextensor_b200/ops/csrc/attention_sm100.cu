@@ -197,7 +197,9 @@ __global__ void __launch_bounds__(192, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; j++) {
-      if (!mbar_wait(&sm.s_full, j & 1)) {
+      // tcgen05.ld/st are warp-collective (.sync.aligned): every branch that guards
+      // one must be warp-uniform, so wait results are combined with a vote.
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, j & 1))) {
         ok = false;
         break;
       }
@@ -222,16 +224,20 @@ __global__ void __launch_bounds__(192, 1)
       }
       // P_j may only overwrite the P buffer after PV_{j-1} finished; the same wait
       // makes it safe to rescale O.
-      if (j > 0 && !mbar_wait(&sm.o_done, (j - 1) & 1)) {
+      if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (j - 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
       float m_use = m;
-      if (mx > m + RESCALE_THRESHOLD || m == -INFINITY) {
-        m_use = mx;
-        if (j > 0 && m != -INFINITY) {
-          const float alpha = ex2(m - mx);
+      // Rescale decision is taken per warp: if any row's max grew past the threshold
+      // (or is still -inf), every row of the warp moves to its exact new max
+      // (alpha == 1 for rows whose max did not change).
+      const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
+      if (__any_sync(0xffffffffu, need)) {
+        m_use = fmaxf(m, mx);
+        if (j > 0) {
+          const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_use);
           l *= alpha;
 #pragma unroll
           for (int c = 0; c < AT_D / 32; c++) {
@@ -273,7 +279,7 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.p_full);
     }
-    if (ok && n_kv > 0 && mbar_wait(&sm.o_done, (n_kv - 1) & 1)) {
+    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done, (n_kv - 1) & 1))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * AT_D;

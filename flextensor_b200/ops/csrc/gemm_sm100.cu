@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int mt, nt;
       tile_coords(tile, p, mt, nt);
-      if (!mbar_wait(&tfull[acc], acc_ph)) break;
+      // tcgen05.ld below is warp-collective: leave the loop as a whole warp
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph))) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
 #pragma unroll 1
