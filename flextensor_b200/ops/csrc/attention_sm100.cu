@@ -1,19 +1,23 @@
 // Flash attention forward on 5th-generation tensor cores (sm_100a), head_dim 128, bf16.
 //
-// One CTA per (batch, query head, 128-query tile); 192 threads:
-//   warp 0     TMA: Q once (2 x [128 x 64] swizzled boxes), then K_j and V_j
-//              tiles of 128 keys into a 2-stage ring (3-D tensor maps, so keys
-//              past the sequence end are zero-filled, never read from the next batch).
-//   warp 1     TMEM owner + MMA issuer:  S = Q K_j^T  (M=128, N=128, K=128) into
-//              TMEM, then O += P_j V_j with P from shared memory (K-major) and
-//              V as an MN-major operand (no transpose pass).
-//   warps 2-5  softmax + epilogue, one query row per thread (TMEM lane = row):
-//              row max / exp2 / row sum entirely in registers, O rescaled in
-//              TMEM only when the running max grows by more than 2^8
-//              (stale-max trick: exp2 stays <= 256 and the final 1/l fixes it),
-//              P written back as bf16 in the 128-byte-swizzled layout the MMA reads.
-// Every mbarrier wait is bounded; a timeout sets the device error word and the
-// CTA unwinds (waits for its own MMAs, frees TMEM) instead of hanging.
+// One CTA per (batch, query head, 256 queries) = two 128-query tiles A and B
+// that ping-pong on the tensor core: while one tile's softmax warpgroup turns
+// S into P, the MMA warp runs the other tile's GEMMs. 320 threads:
+//   warps 0-3   softmax + epilogue of tile A (warp w owns TMEM lanes 32(w%4)..+31 = its query rows)
+//   warps 4-7   softmax + epilogue of tile B
+//   warp 8      TMEM owner + MMA issuer (one elected lane)
+//   warp 9      TMA producer: Q_A, Q_B once; K_j and V_j (128 keys) into two 2-stage rings
+//               (3-D tensor maps: keys past the sequence end read as zeros, never the next batch)
+// TMEM (512 columns): S_A | S_B | O_A | O_B, 128 fp32 columns each. P_X (bf16, two per
+// 32-bit column) is written by tcgen05.st over the first 64 columns of S_X and consumed by
+// the TS-form MMA (A operand from TMEM), so P never touches shared memory.
+// MMA issue order per KV block j:  PV_A(j) S_A(j+1) PV_B(j) S_B(j+1); S_X(j+1) reuses the
+// columns PV_X(j) reads as P, which tcgen05.mma's in-order execution makes safe.
+// Softmax per row (one thread = one row): pass 1 reads S from TMEM for the row max, pass 2
+// re-reads it to form P = exp2(s*scale*log2e - m) and the row sum; O is rescaled in TMEM only
+// when some row's max grew past 2^8 (stale-max trick; the final 1/l normalisation is exact).
+// Every branch around a warp-collective tcgen05.ld/st is warp-uniform (votes).
+// All waits are bounded; a timeout records the device error word and the CTA unwinds.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -28,12 +32,12 @@ FT_DEFINE_ERROR_READER(attn_device_error)
 
 namespace {
 
-constexpr int AT_M = 128;   // queries per CTA
-constexpr int AT_N = 128;   // keys per block
-constexpr int AT_D = 128;   // head dim
-constexpr int CHUNK = 128 * 64 * 2;  // one [128 rows x 64] bf16 swizzled box = 16 KB
-constexpr int STAGES = 2;
-constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr int TILE = 128;                 // queries per tile, keys per block
+constexpr int HD = 128;                   // head dim
+constexpr int CHUNK = 128 * 64 * 2;       // one [128 rows x 64 cols] bf16 swizzled box (16 KB)
+constexpr int KV_STAGES = 2;
+constexpr float RESCALE_THRESHOLD = 8.0f;
+constexpr int NTHREADS = 320;
 
 struct AttnArgs {
   int B, Sq, Sk, Hq, Hk;
@@ -41,16 +45,17 @@ struct AttnArgs {
   long long o_row, o_batch;
   float scale_log2;
   int causal;
-  int n_qtiles;
+  int n_qblocks;  // 256-query blocks per (b, h)
 };
 
 struct Smem {
-  uint8_t q[2 * CHUNK];
-  uint8_t k[STAGES][2 * CHUNK];
-  uint8_t v[STAGES][2 * CHUNK];
-  uint8_t p[2 * CHUNK];
-  uint64_t q_full, k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
-  uint64_t s_full, p_full, o_done, drain;
+  uint8_t q[2][2 * CHUNK];                // tile, d-half
+  uint8_t k[KV_STAGES][2 * CHUNK];
+  uint8_t v[KV_STAGES][2 * CHUNK];
+  uint64_t q_full;
+  uint64_t k_full[KV_STAGES], k_empty[KV_STAGES], v_full[KV_STAGES], v_empty[KV_STAGES];
+  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t drain;
   uint32_t tmem_base;
 };
 
@@ -60,264 +65,310 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
+}
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ bool spin_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(smem_u32(bar), parity)) {
+    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES / 4) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool key_ok(int kp, int qpos, int Sk, int causal) {
+  return kp < Sk && (!causal || kp <= qpos);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int qt = blockIdx.x % a.n_qtiles;
-  const int h = (blockIdx.x / a.n_qtiles) % a.Hq;
-  const int b = blockIdx.x / (a.n_qtiles * a.Hq);
+  const int qb = blockIdx.x % a.n_qblocks;
+  const int h = (blockIdx.x / a.n_qblocks) % a.Hq;
+  const int b = blockIdx.x / (a.n_qblocks * a.Hq);
   const int hk = h / (a.Hq / a.Hk);
-  const int q0 = qt * AT_M;
-  int n_kv = (a.Sk + AT_N - 1) / AT_N;
-  if (a.causal) n_kv = min(n_kv, (q0 + AT_M + AT_N - 1) / AT_N);
+  const int q0 = qb * 2 * TILE;
+  int n_kv = (a.Sk + TILE - 1) / TILE;
+  if (a.causal) n_kv = min(n_kv, (q0 + 2 * TILE + TILE - 1) / TILE);
+  const bool has_b = q0 + TILE < a.Sq;  // second tile has at least one real query
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < KV_STAGES; s++) {
       mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.v_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.p_full, 4);
-    mbar_init(&sm.o_done, 1);
+    for (int t = 0; t < 2; t++) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 4);
+      mbar_init(&sm.o_done[t], 1);
+    }
     mbar_init(&sm.drain, 1);
     fence_barrier_init();
   }
-  if (warp == 1) {
-    tmem_alloc(&sm.tmem_base, 256);
+  if (warp == 8) {
+    tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tS = sm.tmem_base;        // columns [0,128): S
-  const uint32_t tO = sm.tmem_base + 128;  // columns [128,256): O
+  const uint32_t tbase = sm.tmem_base;
 
-  if (warp == 0) {
+  if (warp == 9) {
+    // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(&sm.q_full, 2 * CHUNK);
-      tma_load_3d(sm.q, &tmQ, &sm.q_full, h * AT_D, q0, b);
-      tma_load_3d(sm.q + CHUNK, &tmQ, &sm.q_full, h * AT_D + 64, q0, b);
-      uint32_t pend = 1u << 8, pend_ph = 0;  // bit 8: q; bits 0..: stages
+      mbar_arrive_expect_tx(&sm.q_full, 4 * CHUNK);
+      for (int t = 0; t < 2; t++)
+        for (int c = 0; c < 2; c++)
+          tma_load_3d(sm.q[t] + c * CHUNK, &tmQ, &sm.q_full, h * HD + c * 64, q0 + t * TILE, b);
       bool ok = true;
+      uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
       for (int j = 0; j < n_kv && ok; j++) {
-        const int s = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
-        if (!mbar_wait(&sm.kv_empty[s], ph ^ 1)) {
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(&sm.k_empty[s], ph ^ 1)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&sm.k_full[s], 2 * CHUNK);
-        tma_load_3d(sm.k[s], &tmK, &sm.k_full[s], hk * AT_D, j * AT_N, b);
-        tma_load_3d(sm.k[s] + CHUNK, &tmK, &sm.k_full[s], hk * AT_D + 64, j * AT_N, b);
-        mbar_arrive_expect_tx(&sm.v_full[s], 2 * CHUNK);
-        tma_load_3d(sm.v[s], &tmV, &sm.v_full[s], hk * AT_D, j * AT_N, b);
-        tma_load_3d(sm.v[s] + CHUNK, &tmV, &sm.v_full[s], hk * AT_D + 64, j * AT_N, b);
-        pend |= 1u << s;
-        pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
-      }
-      if (!ok) {
-        const long long t0 = clock64();
-        auto left = [&] { return (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4; };
-        while (!mbar_try_wait(smem_u32(&sm.q_full), 0) && left()) {
+        for (int c = 0; c < 2; c++)
+          tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, j * TILE, b);
+        kpend |= 1u << s;
+        kph = (kph & ~(1u << s)) | (ph << s);
+        if (!mbar_wait(&sm.v_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
         }
-        for (int s = 0; s < STAGES; s++) {
-          if (!(pend >> s & 1)) continue;
-          while (!mbar_try_wait(smem_u32(&sm.k_full[s]), (pend_ph >> s) & 1) && left()) {
-          }
-          while (!mbar_try_wait(smem_u32(&sm.v_full[s]), (pend_ph >> s) & 1) && left()) {
-          }
+        mbar_arrive_expect_tx(&sm.v_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++)
+          tma_load_3d(sm.v[s] + c * CHUNK, &tmV, &sm.v_full[s], hk * HD + c * 64, j * TILE, b);
+        vpend |= 1u << s;
+        vph = (vph & ~(1u << s)) | (ph << s);
+      }
+      if (!ok) {  // unwinding: every issued load must land before the CTA exits
+        spin_drain(&sm.q_full, 0);
+        for (int s = 0; s < KV_STAGES; s++) {
+          if (kpend >> s & 1) spin_drain(&sm.k_full[s], (kph >> s) & 1);
+          if (vpend >> s & 1) spin_drain(&sm.v_full[s], (vph >> s) & 1);
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      constexpr uint32_t idS = umma_idesc_bf16_f32(AT_M, AT_N);
-      constexpr uint32_t idO = umma_idesc_bf16_f32(AT_M, AT_D, false, true);  // B (V) is MN-major
+      constexpr uint32_t idS = umma_idesc_bf16_f32(TILE, TILE);
+      constexpr uint32_t idO = umma_idesc_bf16_f32(TILE, HD, false, true);  // V is MN-major
       bool ok = mbar_wait(&sm.q_full, 0);
-      const uint32_t qa = smem_u32(sm.q);
-      for (int j = 0; ok && j < n_kv; j++) {
-        const int s = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
-        // S_j = Q K_j^T   (S buffer is free: softmax signalled p_full for j-1 before we got here)
-        if (!mbar_wait(&sm.k_full[s], ph)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      auto issue_S = [&](int t, int s) {
+        const uint32_t qa = smem_u32(sm.q[t]);
         const uint32_t ka = smem_u32(sm.k[s]);
 #pragma unroll
-        for (int kk = 0; kk < AT_D / 16; kk++) {
+        for (int kk = 0; kk < HD / 16; kk++) {
           const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-          umma_bf16_ss(tS, umma_desc_kmajor_sw128(qa + off), umma_desc_kmajor_sw128(ka + off), idS, kk > 0);
+          umma_bf16_ss(tbase + t * 128, umma_desc_kmajor_sw128(qa + off), umma_desc_kmajor_sw128(ka + off), idS,
+                       kk > 0);
         }
-        umma_commit(&sm.s_full);
-        // O += P_j V_j  once softmax published P_j
-        if (!mbar_wait(&sm.p_full, j & 1) || !mbar_wait(&sm.v_full[s], ph)) {
+        umma_commit(&sm.s_full[t]);
+      };
+      auto issue_PV = [&](int t, int s, int j) {
+        const uint32_t va = smem_u32(sm.v[s]);
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; kk++) {
+          umma_bf16_ts(tbase + 256 + t * 128, tbase + t * 128 + kk * 8,
+                       umma_desc_mnmajor_sw128(va + kk * 16 * 128, CHUNK), idO, (j | kk) != 0);
+        }
+        umma_commit(&sm.o_done[t]);
+      };
+      if (ok && n_kv > 0) {
+        ok = mbar_wait(&sm.k_full[0], 0);
+        if (ok) {
+          tc_fence_after();
+          issue_S(0, 0);
+          if (has_b) issue_S(1, 0);
+          umma_commit(&sm.k_empty[0]);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; j++) {
+        const int s = j % KV_STAGES, s1 = (j + 1) % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1, ph1 = ((j + 1) / KV_STAGES) & 1;
+        const bool more = j + 1 < n_kv;
+        if (!mbar_wait(&sm.v_full[s], ph) || !mbar_wait(&sm.p_full[0], j & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t pa = smem_u32(sm.p);
-        const uint32_t va = smem_u32(sm.v[s]);
-#pragma unroll
-        for (int kk = 0; kk < AT_N / 16; kk++) {
-          const uint32_t poff = (kk >> 2) * CHUNK + (kk & 3) * 32;  // keys 16kk.. in P (K-major)
-          const uint32_t voff = kk * 16 * 128;                       // 16 key rows of 128 B in V (MN-major)
-          umma_bf16_ss(tO, umma_desc_kmajor_sw128(pa + poff), umma_desc_mnmajor_sw128(va + voff, CHUNK), idO,
-                       (j | kk) != 0);
+        issue_PV(0, s, j);
+        if (more) {
+          if (!mbar_wait(&sm.k_full[s1], ph1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_S(0, s1);
         }
-        umma_commit(&sm.kv_empty[s]);
-        umma_commit(&sm.o_done);
+        if (has_b) {
+          if (!mbar_wait(&sm.p_full[1], j & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_PV(1, s, j);
+          if (more) issue_S(1, s1);
+        }
+        umma_commit(&sm.v_empty[s]);
+        if (more) umma_commit(&sm.k_empty[s1]);
       }
       if (!ok) {
         umma_commit(&sm.drain);
-        const long long t0 = clock64();
-        while (!mbar_try_wait(smem_u32(&sm.drain), 0) &&
-               (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
-        }
+        spin_drain(&sm.drain, 0);
       }
     }
   } else {
-    // softmax / epilogue warpgroup
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // row within the tile == TMEM lane
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int t = warp >> 2;           // tile
+    const int quad = warp & 3;         // TMEM lane quadrant
+    const int r = quad * 32 + lane;    // row in tile
+    const int qpos = q0 + t * TILE + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const int qpos = q0 + r;
+    const uint32_t tS = tbase + t * 128 + lane_off;
+    const uint32_t tO = tbase + 256 + t * 128 + lane_off;
+    const bool active = (t == 0) || has_b;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; j++) {
-      // tcgen05.ld/st are warp-collective (.sync.aligned): every branch that guards
-      // one must be warp-uniform, so wait results are combined with a vote.
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, j & 1))) {
+    for (int j = 0; active && j < n_kv; j++) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[AT_N];
+      const int kbase = j * TILE;
+      const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0 + t * TILE);
+      // pass 1: row max
+      float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < AT_N / 32; c++) {
-        uint32_t t[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, t);
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
         tmem_ld_wait();
+        if (masked) {
 #pragma unroll
-        for (int e = 0; e < 32; e++) sv[c * 32 + e] = __uint_as_float(t[e]) * a.scale_log2;
-      }
-      const int kbase = j * AT_N;
-      float mx = m;
+          for (int e = 0; e < 32; e++)
+            mx = fmaxf(mx, key_ok(kbase + c * 32 + e, qpos, a.Sk, a.causal) ? __uint_as_float(v[e]) : -INFINITY);
+        } else {
 #pragma unroll
-      for (int e = 0; e < AT_N; e++) {
-        const int kpos = kbase + e;
-        const bool valid = kpos < a.Sk && (!a.causal || kpos <= qpos);
-        if (!valid) sv[e] = -INFINITY;
-        mx = fmaxf(mx, sv[e]);
+          for (int e = 0; e < 32; e++) mx = fmaxf(mx, __uint_as_float(v[e]));
+        }
       }
-      // P_j may only overwrite the P buffer after PV_{j-1} finished; the same wait
-      // makes it safe to rescale O.
-      if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (j - 1) & 1))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float m_use = m;
-      // Rescale decision is taken per warp: if any row's max grew past the threshold
-      // (or is still -inf), every row of the warp moves to its exact new max
-      // (alpha == 1 for rows whose max did not change).
+      mx *= a.scale_log2;
       const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
       if (__any_sync(0xffffffffu, need)) {
-        m_use = fmaxf(m, mx);
+        const float m_new = fmaxf(m, mx);
         if (j > 0) {
-          const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_use);
+          // O_X is quiescent once PV_X(j-1) completed (its commit precedes S_X(j)'s)
+          if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
           l *= alpha;
 #pragma unroll
-          for (int c = 0; c < AT_D / 32; c++) {
-            uint32_t t[32];
-            tmem_ld_32x32b_x32(tO + lane_off + c * 32, t);
+          for (int c = 0; c < 4; c++) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tO + c * 32, v);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; e++) t[e] = __float_as_uint(__uint_as_float(t[e]) * alpha);
-            tmem_st_32x32b_x32(tO + lane_off + c * 32, t);
+            for (int e = 0; e < 32; e++) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_32x32b_x32(tO + c * 32, v);
           }
           tmem_st_wait();
         }
-        m = m_use;
+        m = m_new;
       }
-      const float msub = (m_use == -INFINITY) ? 0.f : m_use;
+      const float msub = (m == -INFINITY) ? 0.f : m;
+      // pass 2: P = exp2(s * scale - m), packed bf16x2 over the first 64 columns of S
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < 2; c++) {          // key halves -> P chunks
-        uint8_t* pbase = sm.p + c * CHUNK + r * 128;
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
 #pragma unroll
-        for (int u = 0; u < 8; u++) {        // 16-byte units of 8 keys
-          float pv[8];
-#pragma unroll
-          for (int e = 0; e < 8; e++) {
-            pv[e] = ex2(sv[c * 64 + u * 8 + e] - msub);
-            rs += pv[e];
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = ex2(fmaf(__uint_as_float(v[e]), a.scale_log2, -msub));
+          float p1 = ex2(fmaf(__uint_as_float(v[e + 1]), a.scale_log2, -msub));
+          if (masked) {
+            const int kp = kbase + c * 32 + e;
+            if (!key_ok(kp, qpos, a.Sk, a.causal)) p0 = 0.f;
+            if (!key_ok(kp + 1, qpos, a.Sk, a.causal)) p1 = 0.f;
           }
-          uint4 w;
-          w.x = pack_bf16x2(pv[0], pv[1]);
-          w.y = pack_bf16x2(pv[2], pv[3]);
-          w.z = pack_bf16x2(pv[4], pv[5]);
-          w.w = pack_bf16x2(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(pbase + ((u ^ (r & 7)) << 4)) = w;
+          rs += p0 + p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
         }
+        tmem_st_32x32b_x16(tS + c * 16, pk);
       }
       l += rs;
-      fence_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full);
+      if (lane == 0) mbar_arrive(&sm.p_full[t]);
     }
-    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done, (n_kv - 1) & 1))) {
+    // epilogue: O / l -> bf16
+    if (active && ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (n_kv - 1) & 1))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * AT_D;
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD;
 #pragma unroll
-      for (int c = 0; c < AT_D / 32; c++) {
-        uint32_t t[32];
-        tmem_ld_32x32b_x32(tO + lane_off + c * 32, t);
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tO + c * 32, v);
         tmem_ld_wait();
         if (qpos < a.Sq) {
 #pragma unroll
           for (int u = 0; u < 4; u++) {
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(t[u * 8 + 0]) * inv, __uint_as_float(t[u * 8 + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(t[u * 8 + 2]) * inv, __uint_as_float(t[u * 8 + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(t[u * 8 + 4]) * inv, __uint_as_float(t[u * 8 + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(t[u * 8 + 6]) * inv, __uint_as_float(t[u * 8 + 7]) * inv);
+            w.x = pack_bf16x2(__uint_as_float(v[u * 8 + 0]) * inv, __uint_as_float(v[u * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[u * 8 + 2]) * inv, __uint_as_float(v[u * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[u * 8 + 4]) * inv, __uint_as_float(v[u * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[u * 8 + 6]) * inv, __uint_as_float(v[u * 8 + 7]) * inv);
             *reinterpret_cast<uint4*>(out + c * 32 + u * 8) = w;
           }
         }
       }
-    } else if (n_kv == 0 && qpos < a.Sq) {
-      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * AT_D;
-      for (int d = 0; d < AT_D; d++) out[d] = __float2bfloat16(0.f);
+    } else if (active && n_kv == 0 && qpos < a.Sq) {
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD;
+      for (int d = 0; d < HD; d++) out[d] = __float2bfloat16(0.f);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 8) {
     tc_fence_after();
-    tmem_dealloc(sm.tmem_base, 256);
+    tmem_dealloc(tbase, 512);
   }
 }
 
 bool make_tmap_3d(CUtensorMap* map, const void* base, int H, int S, int B, long long row_stride,
                   long long batch_stride) {
   // dims (inner->outer): head*dim columns, sequence rows, batch; box 64 x 128 x 1, 128-byte swizzle
-  return make_tmap_3d_bf16(map, base, (uint64_t)H * AT_D, (uint64_t)S, (uint64_t)B, (uint64_t)row_stride,
+  return make_tmap_3d_bf16(map, base, (uint64_t)H * HD, (uint64_t)S, (uint64_t)B, (uint64_t)row_stride,
                            (uint64_t)batch_stride, 64, 128);
 }
 
@@ -342,7 +393,7 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
   a.o_batch = p.o_batch;
   a.scale_log2 = p.scale * 1.4426950408889634f;
   a.causal = p.causal ? 1 : 0;
-  a.n_qtiles = (p.Sq + AT_M - 1) / AT_M;
+  a.n_qblocks = (p.Sq + 2 * TILE - 1) / (2 * TILE);
   const int smem = (int)sizeof(Smem) + 1024;
   static bool attr = false;
   if (!attr) {
@@ -350,9 +401,9 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const long long grid = (long long)a.n_qtiles * p.Hq * p.B;
+  const long long grid = (long long)a.n_qblocks * p.Hq * p.B;
   if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-  attn_fwd_kernel<<<(int)grid, 192, smem, stream>>>(tq, tk, tv, a);
+  attn_fwd_kernel<<<(int)grid, NTHREADS, smem, stream>>>(tq, tk, tv, a);
   return cudaGetLastError();
 }
 
