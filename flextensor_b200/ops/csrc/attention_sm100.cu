@@ -13,8 +13,9 @@
 // the TS-form MMA (A operand from TMEM), so P never touches shared memory.
 // MMA issue order per KV block j:  PV_A(j) S_A(j+1) PV_B(j) S_B(j+1); S_X(j+1) reuses the
 // columns PV_X(j) reads as P, which tcgen05.mma's in-order execution makes safe.
-// Softmax per row (one thread = one row): pass 1 reads S from TMEM for the row max, pass 2
-// re-reads it to form P = exp2(s*scale*log2e - m) and the row sum; O is rescaled in TMEM only
+// Softmax per row (one thread = one row): pass 1 reads the S row from TMEM (two loads in
+// flight per wait) for the row max, pass 2 re-reads it to form P = exp2(s*scale*log2e - m)
+// and the row sum (tree reductions, no long dependency chains); O is rescaled in TMEM only
 // when some row's max grew past 2^8 (stale-max trick; the final 1/l normalisation is exact).
 // Every branch around a warp-collective tcgen05.ld/st is warp-uniform (votes).
 // All waits are bounded; a timeout records the device error word and the CTA unwinds.
@@ -258,22 +259,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       const int kbase = j * TILE;
       const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0 + t * TILE);
-      // pass 1: row max
-      float mx = -INFINITY;
+      // pass 1: row max, two halves of two in-flight TMEM loads each; the max is an 8-way
+      // tree so no 128-long dependency chain forms.
+      float mx8[8];
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
+      for (int i = 0; i < 8; i++) mx8[i] = -INFINITY;
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        uint32_t v[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; c++) tmem_ld_32x32b_x32(tS + (half * 2 + c) * 32, v[c]);
         tmem_ld_wait();
         if (masked) {
 #pragma unroll
-          for (int e = 0; e < 32; e++)
-            mx = fmaxf(mx, key_ok(kbase + c * 32 + e, qpos, a.Sk, a.causal) ? __uint_as_float(v[e]) : -INFINITY);
-        } else {
+          for (int c = 0; c < 2; c++)
 #pragma unroll
-          for (int e = 0; e < 32; e++) mx = fmaxf(mx, __uint_as_float(v[e]));
+            for (int e = 0; e < 32; e++)
+              if (!key_ok(kbase + (half * 2 + c) * 32 + e, qpos, a.Sk, a.causal))
+                v[c][e] = __float_as_uint(-INFINITY);
         }
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+#pragma unroll
+          for (int e = 0; e < 32; e++) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(v[c][e]));
       }
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       mx *= a.scale_log2;
       const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
       if (__any_sync(0xffffffffu, need)) {
@@ -289,40 +300,46 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           l *= alpha;
 #pragma unroll
           for (int c = 0; c < 4; c++) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tO + c * 32, v);
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tO + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; e++) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_32x32b_x32(tO + c * 32, v);
+            for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x32(tO + c * 32, o);
           }
-          tmem_st_wait();
         }
         m = m_new;
       }
       const float msub = (m == -INFINITY) ? 0.f : m;
-      // pass 2: P = exp2(s * scale - m), packed bf16x2 over the first 64 columns of S
-      float rs = 0.f;
+      // pass 2: P = exp2(s * scale - m), packed bf16x2 over the first 64 columns of S, in two halves
+      // of two in-flight loads; 4-way row sum. P columns written by half h were read by half h-1 or h.
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
+      for (int half = 0; half < 2; half++) {
+        uint32_t v[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; c++) tmem_ld_32x32b_x32(tS + (half * 2 + c) * 32, v[c]);
         tmem_ld_wait();
-        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2(fmaf(__uint_as_float(v[e]), a.scale_log2, -msub));
-          float p1 = ex2(fmaf(__uint_as_float(v[e + 1]), a.scale_log2, -msub));
-          if (masked) {
-            const int kp = kbase + c * 32 + e;
-            if (!key_ok(kp, qpos, a.Sk, a.causal)) p0 = 0.f;
-            if (!key_ok(kp + 1, qpos, a.Sk, a.causal)) p1 = 0.f;
+        for (int cc = 0; cc < 2; cc++) {
+          const int c = half * 2 + cc;
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float p0 = ex2(fmaf(__uint_as_float(v[cc][e]), a.scale_log2, -msub));
+            float p1 = ex2(fmaf(__uint_as_float(v[cc][e + 1]), a.scale_log2, -msub));
+            if (masked) {
+              const int kp = kbase + c * 32 + e;
+              if (!key_ok(kp, qpos, a.Sk, a.causal)) p0 = 0.f;
+              if (!key_ok(kp + 1, qpos, a.Sk, a.causal)) p1 = 0.f;
+            }
+            rs4[(e >> 1) & 3] += p0 + p1;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
           }
-          rs += p0 + p1;
-          pk[e >> 1] = pack_bf16x2(p0, p1);
+          tmem_st_32x32b_x16(tS + c * 16, pk);
         }
-        tmem_st_32x32b_x16(tS + c * 16, pk);
       }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l += rs;
       tmem_st_wait();
       tc_fence_before();

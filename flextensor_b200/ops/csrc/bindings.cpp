@@ -6,6 +6,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "ft_attn.h"
 #include "ft_ops.h"
 #include "ft_ops_norm.h"
@@ -77,6 +79,11 @@ void gemm(const Tensor& A, const Tensor& W, Tensor& C, const c10::optional<Tenso
   }
   p.num_sms = num_sms_for(A.get_device());
   p.force_bn = (int)force_bn;
+  static const bool pair_env = [] {
+    const char* e = std::getenv("FT_GEMM_2SM");
+    return e != nullptr && e[0] == '1';  // opt-in until the 2-SM kernel is validated on hardware
+  }();
+  p.pair_ok = pair_env;
   check_ok(ft::gemm_bf16(p, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
 }
 

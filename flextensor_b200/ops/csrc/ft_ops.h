@@ -30,7 +30,8 @@ struct GemmProblem {
   int gate_rows = 0;
   int epi = EPI_NONE;
   int num_sms = 0;
-  int force_bn = 0;
+  int force_bn = 0;   // 64/128/256: 1-SM tile width; 512: force the 2-SM 256x256 kernel
+  bool pair_ok = false;  // allow the 2-SM kernel when the shape suits it
 };
 
 cudaError_t gemm_bf16(const GemmProblem& g, cudaStream_t stream);

@@ -287,6 +287,225 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ------------------------------------------------------------------ 2-SM (CTA pair) variant
+// Cluster of 2 CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2 (M=256):
+// CTA r loads A rows [m0 + 128r, +128) and W rows [n0 + 128r, +128) into its own
+// shared memory; both halves' TMA bytes are counted on the leader's (rank 0) full
+// barrier; the leader's single MMA thread issues M=256 x N=256 x K=16 MMAs reading
+// both CTAs' tiles, and each CTA's TMEM receives its 128 rows x 256 columns.
+// Commits are multicast to both CTAs (stage free / accumulator ready); epilogue warps
+// of both CTAs arrive on the leader's accumulator-empty barrier.
+// Per CTA per k-block: 32 KB of shared-memory traffic for 2x the math of the 1-SM
+// 128x256 tile, which halves L2->SM bandwidth per FLOP.
+struct Gemm2Cfg {
+  static constexpr int BN = 256;  // pair tile N
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = BM * BK * 2;         // this CTA's 128 A rows
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's 128 W rows
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+};
+
+__device__ __forceinline__ void tile_coords_pair(int tile, const GemmArgs& p, int& mt2, int& nt) {
+  // mt2 indexes 256-row tiles
+  const int num_m2 = (p.num_m_tiles + 1) / 2;
+  const int per_group = 4 * p.num_n_tiles;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int first = g * 4;
+  const int gsz = min(4, num_m2 - first);
+  mt2 = first + r % gsz;
+  nt = r / gsz;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_bf16_tcgen05_2sm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          GemmArgs p) {
+  using Cfg = Gemm2Cfg;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int BN = Cfg::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_tiles = ((p.num_m_tiles + 1) / 2) * p.num_n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs (leader's copy is the one used)
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive / TMA completion
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      uint32_t pend = 0, pend_ph = 0;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        int mt2, nt;
+        tile_coords_pair(tile, p, mt2, nt);
+        const int arow = mt2 * 256 + (int)rank * 128;
+        const int brow = nt * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&empty[s], ph ^ 1)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, &full[s], kb * BK, arow);
+          tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, &full[s], kb * BK, brow);
+          pend |= 1u << s;
+          pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok && leader) {
+        for (int st = 0; st < STAGES; st++) {
+          if (!(pend >> st & 1)) continue;
+          const long long t0 = clock64();
+          while (!mbar_try_wait(smem_u32(&full[st]), (pend_ph >> st) & 1) &&
+                 (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(256, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++) {
+            umma_bf16_ss_pair(d, umma_desc_kmajor_sw128(a0 + k * 32), umma_desc_kmajor_sw128(b0 + k * 32), idesc,
+                              (kb | k) != 0);
+          }
+          umma_commit_pair(&empty[s], 0x3);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+      if (!ok) {
+        umma_commit_pair(drain, 0x1);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(smem_u32(drain), 0) &&
+               (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+      int mt2, nt;
+      tile_coords_pair(tile, p, mt2, nt);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph))) break;
+      tc_fence_after();
+      const int row = mt2 * 256 + (int)rank * 128 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nt * BN + c * 32;
+        if (row < p.M && col0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; e++) v[e] = __uint_as_float(r[e]);
+          epi_store32(p, row, col0, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no remote arrive / MMA may target a CTA that has left
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+static cudaError_t launch_gemm_2sm(const GemmArgs& a, const __nv_bfloat16* A, int lda, const __nv_bfloat16* W,
+                                   int ldw, int num_sms, cudaStream_t stream) {
+  using Cfg = Gemm2Cfg;
+  CUtensorMap tmA, tmB;
+  if (!make_tmap_2d_bf16(&tmA, A, a.K, a.M, lda, BK, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tmB, W, a.K, a.N, ldw, BK, Cfg::BN / 2)) return cudaErrorInvalidValue;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tcgen05_2sm, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int tiles = ((a.num_m_tiles + 1) / 2) * a.num_n_tiles;
+  int clusters = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  gemm_bf16_tcgen05_2sm<<<2 * clusters, 192, Cfg::SMEM, stream>>>(tmA, tmB, a);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ host side
 template <int BN>
 static cudaError_t launch_gemm(const GemmArgs& a, const __nv_bfloat16* A, int lda, const __nv_bfloat16* W, int ldw,
@@ -329,6 +548,13 @@ cudaError_t gemm_bf16(const GemmProblem& g, cudaStream_t stream) {
   if (a.bias != nullptr && (reinterpret_cast<uintptr_t>(a.bias) & 15)) return cudaErrorMisalignedAddress;
   int bn = g.N >= 256 ? 256 : (g.N > 64 ? 128 : 64);
   if (g.force_bn) bn = g.force_bn;
+  const bool pair = (g.force_bn == 512) || (g.force_bn == 0 && g.M >= 512 && g.N >= 256 && g.pair_ok);
+  if (pair) {
+    a.num_m_tiles = (g.M + BM - 1) / BM;
+    a.num_n_tiles = (g.N + 255) / 256;
+    a.num_tiles = a.num_m_tiles * a.num_n_tiles;
+    return launch_gemm_2sm(a, g.A, g.lda, g.W, g.ldw, g.num_sms > 0 ? g.num_sms : 148, stream);
+  }
   a.num_m_tiles = (g.M + BM - 1) / BM;
   a.num_n_tiles = (g.N + bn - 1) / bn;
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;

@@ -156,3 +156,19 @@ def test_attention_large_logits():
     v = torch.randn(1, 1024, 2, 128, device=DEV).bfloat16()
     o = ops.attention(q, k, v)
     assert rel_err(o, _attn_ref(q, k, v)) < 2e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 256, 64), (1000, 768, 512), (4096, 5120, 5120), (777, 384, 1024)])
+def test_gemm_pair_kernel(M, N, K):
+    """2-SM (cta_group::2, 256x256 tiles) kernel, forced."""
+    torch.manual_seed(9)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    b = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    res = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    gate = torch.randn(N, device=DEV, dtype=torch.float32)
+    ref = _lin_ref(x, w, b)
+    y = ops.linear(x, w, b, epi="gate_res", residual=res, gate=gate, force_bn=512)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    assert rel_err(y, res.float() + gate * ref) < 1e-2
