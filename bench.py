@@ -185,6 +185,7 @@ def make_config(ft, local: int, frac: float, profiling_iters: int):
         discovery_iters=1,
         load_strategy=ft.BudgetFillStrategy(n_blocks=2, threshold_mb=1.0, enable_layer_de=True,
                                             enable_tensor_de=False, seed=0),
+        offload_timing="eager",
     )
 
 
@@ -203,6 +204,15 @@ def import_arm(impl: str):
     import flextensor_b200 as ft  # noqa: PLC0415
 
     return ft, None
+
+
+def _launches(impl: str):
+    """Native kernels launched so far (our arm); the reference arm launches none of ours."""
+    if impl != "ours":
+        return None
+    from flextensor_b200.ops.api import launch_count
+
+    return launch_count()
 
 
 def main():
@@ -249,6 +259,7 @@ def main():
     torch.cuda.synchronize()
     torch.cuda.reset_peak_memory_stats(device)
 
+    launches0 = _launches(args.impl)
     clocks = ClockSampler(local)
     clocks.start()
     times = []
@@ -264,6 +275,7 @@ def main():
         torch.cuda.synchronize()
     barrier(pg)
     step_ms = [s.elapsed_time(e) for s, e in times]
+    launches = (_launches(args.impl) - launches0) // max(1, args.steps) if launches0 is not None else None
     peak_gb = torch.cuda.max_memory_allocated(device) / 1e9
     ms = sum(step_ms) / len(step_ms)
 
@@ -287,6 +299,18 @@ def main():
     ck = clocks.stop()
 
     hidden = None
+    try:
+        rep = om.collect_offload_timing()
+        if rep is not None and getattr(rep, "traps", None):
+            if hasattr(rep, "hidden_fraction"):
+                hidden = round(100.0 * rep.hidden_fraction, 2)
+            else:  # reference report: derive from its per-trap aggregates
+                tr = sum(t.transfer_ms["avg"] for t in rep.traps) if hasattr(rep.traps[0], "transfer_ms") else None
+                wt = sum(t.wait_ms["avg"] for t in rep.traps) if hasattr(rep.traps[0], "wait_ms") else None
+                if tr:
+                    hidden = round(100.0 * max(0.0, 1 - wt / tr), 2)
+    except Exception:  # noqa: BLE001
+        hidden = None
     try:
         tm = om.get_tensor_manager()
         st = tm.get_gpu_memory_usage()
@@ -321,7 +345,7 @@ def main():
         "clocks": ck,
         "e2e": None if e2e_max is None else {"value": round(e2e_max, 5), "unit": "s/step", "h2d_bytes_per_step": h2d,
                                               "d2h_bytes_per_step": d2h},
-        "gpu_launches": None,
+        "gpu_launches": launches,
         "config": {"model": MODEL if args.layers == 40 else f"{MODEL} [layers={args.layers}: NOT the headline]",
                    "global_batch": world, "seq_len": tokens, "parallelism": f"dp{world}",
                    "weight_budget": f"{int(RESIDENT_FRACTION * 100)}% of weight bytes on GPU (incl. ring slots)",

@@ -15,6 +15,18 @@ from flextensor_b200.ops import native
 
 EPI = {"none": 0, "bias": 1, "gelu": 2, "gate_res": 3, "res": 4}
 
+# Number of native kernel launches issued through these entry points (each call = one launch).
+_launches = 0
+
+
+def launch_count() -> int:
+    return _launches
+
+
+def _count() -> None:
+    global _launches
+    _launches += 1
+
 
 def _2d(t: torch.Tensor) -> torch.Tensor:
     return t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
@@ -42,6 +54,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     if e in (1, 2) and bias is None:
         e = EPI["none"] if e == 1 else e
     native.lib().gemm(a, weight, o2, bias, r2, gate, int(gate_rows), e, int(force_bn))
+    _count()
     return out
 
 
@@ -53,6 +66,7 @@ def layernorm_modulate(x: torch.Tensor, scale: torch.Tensor | None = None, shift
     if out is None:
         out = torch.empty_like(x)
     native.lib().ln_modulate(x2, _2d(out), weight, bias, scale, shift, int(mod_rows), float(eps))
+    _count()
     return out
 
 
@@ -62,6 +76,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None = None, *, eps: float =
     if out is None:
         out = torch.empty(x2.shape, dtype=x.dtype, device=x.device).view(x.shape)
     native.lib().rmsnorm(x2, _2d(out), weight, None, None, 0, 0, float(eps))
+    _count()
     return out
 
 
@@ -72,15 +87,17 @@ def qk_rmsnorm_rope(x: torch.Tensor, weight: torch.Tensor | None, cos: torch.Ten
     if out is None:
         out = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
     native.lib().rmsnorm(x2, _2d(out), weight, cos, sin, int(head_dim), int(seq_len), float(eps))
+    _count()
     return out
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
-              causal: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+              causal: bool = False, out: torch.Tensor | None = None, _diag_mode: int = 0) -> torch.Tensor:
     """Softmax attention on ``[B, S, H, 128]`` bf16 tensors (GQA when k/v have fewer heads)."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    native.lib().attention(q, k, v, out, float(scale), bool(causal))
+    native.lib().attention(q, k, v, out, float(scale), bool(causal), int(_diag_mode))
+    _count()
     return out

@@ -13,9 +13,9 @@
 // the TS-form MMA (A operand from TMEM), so P never touches shared memory.
 // MMA issue order per KV block j:  PV_A(j) S_A(j+1) PV_B(j) S_B(j+1); S_X(j+1) reuses the
 // columns PV_X(j) reads as P, which tcgen05.mma's in-order execution makes safe.
-// Softmax per row (one thread = one row): pass 1 reads the S row from TMEM (two loads in
-// flight per wait) for the row max, pass 2 re-reads it to form P = exp2(s*scale*log2e - m)
-// and the row sum (tree reductions, no long dependency chains); O is rescaled in TMEM only
+// Softmax per row (one thread = one row): one TMEM round trip brings the whole S row into
+// registers; row max (4 independent chains), P = exp2(s*scale*log2e - m) packed in place and the
+// row sum (4 partial sums) all happen in registers; O is rescaled in TMEM only
 // when some row's max grew past 2^8 (stale-max trick; the final 1/l normalisation is exact).
 // Every branch around a warp-collective tcgen05.ld/st is warp-uniform (votes).
 // All waits are bounded; a timeout records the device error word and the CTA unwinds.
@@ -47,6 +47,7 @@ struct AttnArgs {
   float scale_log2;
   int causal;
   int n_qblocks;  // 256-query blocks per (b, h)
+  int diag;
 };
 
 struct Smem {
@@ -67,6 +68,15 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
+}
+
+// stores words 0..15 of a 32-word register array (no reinterpret of the array: keeps it in registers)
+__device__ __forceinline__ void tmem_st_32x32b_x16_lo(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
@@ -257,89 +267,89 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       tc_fence_after();
+      if (a.diag == 2) {  // timing diagnostic: no softmax work at all
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[t]);
+        continue;
+      }
       const int kbase = j * TILE;
       const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0 + t * TILE);
-      // pass 1: row max, two halves of two in-flight TMEM loads each; the max is an 8-way
-      // tree so no 128-long dependency chain forms.
-      float mx8[8];
+      // Single pass over the S row: all 128 columns in flight in one TMEM round trip,
+      // 8-way tree max, exp2 in registers, P packed in place (pair i of chunk c -> word i),
+      // four 16-column TMEM stores. Registers: 128 for the row + a few scalars.
+      uint32_t v[4][32];
 #pragma unroll
-      for (int i = 0; i < 8; i++) mx8[i] = -INFINITY;
+      for (int c = 0; c < 4; c++) tmem_ld_32x32b_x32(tS + c * 32, v[c]);
+      tmem_ld_wait();
+      if (masked) {
 #pragma unroll
-      for (int half = 0; half < 2; half++) {
-        uint32_t v[2][32];
+        for (int c = 0; c < 4; c++)
 #pragma unroll
-        for (int c = 0; c < 2; c++) tmem_ld_32x32b_x32(tS + (half * 2 + c) * 32, v[c]);
-        tmem_ld_wait();
-        if (masked) {
-#pragma unroll
-          for (int c = 0; c < 2; c++)
-#pragma unroll
-            for (int e = 0; e < 32; e++)
-              if (!key_ok(kbase + (half * 2 + c) * 32 + e, qpos, a.Sk, a.causal))
-                v[c][e] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int c = 0; c < 2; c++)
-#pragma unroll
-          for (int e = 0; e < 32; e++) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(v[c][e]));
+          for (int e = 0; e < 32; e++)
+            if (!key_ok(kbase + c * 32 + e, qpos, a.Sk, a.causal)) v[c][e] = __float_as_uint(-INFINITY);
       }
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      mx *= a.scale_log2;
-      const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_new = fmaxf(m, mx);
-        if (j > 0) {
-          // O_X is quiescent once PV_X(j-1) completed (its commit precedes S_X(j)'s)
-          if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
-          l *= alpha;
+      float mx;
+      {
+        float m0 = __uint_as_float(v[0][0]), m1 = __uint_as_float(v[1][0]);
+        float m2 = __uint_as_float(v[2][0]), m3 = __uint_as_float(v[3][0]);
 #pragma unroll
-          for (int c = 0; c < 4; c++) {
-            uint32_t o[32];
-            tmem_ld_32x32b_x32(tO + c * 32, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st_32x32b_x32(tO + c * 32, o);
-          }
+        for (int e = 1; e < 32; e++) {
+          m0 = fmaxf(m0, __uint_as_float(v[0][e]));
+          m1 = fmaxf(m1, __uint_as_float(v[1][e]));
+          m2 = fmaxf(m2, __uint_as_float(v[2][e]));
+          m3 = fmaxf(m3, __uint_as_float(v[3][e]));
         }
+        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+      }
+      mx *= a.scale_log2;
+      // Rescale decision is warp-uniform (tcgen05.ld/st below are warp-collective): if any row's
+      // max grew past the threshold (or is still -inf), every row of the warp moves to its exact
+      // new max. O itself is rescaled after P is formed so the S row registers are dead by then.
+      const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
+      const bool rescale = __any_sync(0xffffffffu, need);
+      float alpha = 1.f;
+      if (rescale) {
+        const float m_new = fmaxf(m, mx);
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+        l *= alpha;
         m = m_new;
       }
       const float msub = (m == -INFINITY) ? 0.f : m;
-      // pass 2: P = exp2(s * scale - m), packed bf16x2 over the first 64 columns of S, in two halves
-      // of two in-flight loads; 4-way row sum. P columns written by half h were read by half h-1 or h.
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      float rsc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int half = 0; half < 2; half++) {
-        uint32_t v[2][32];
+      for (int c = 0; c < 4; c++) {
 #pragma unroll
-        for (int c = 0; c < 2; c++) tmem_ld_32x32b_x32(tS + (half * 2 + c) * 32, v[c]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-          const int c = half * 2 + cc;
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float p0 = ex2(fmaf(__uint_as_float(v[cc][e]), a.scale_log2, -msub));
-            float p1 = ex2(fmaf(__uint_as_float(v[cc][e + 1]), a.scale_log2, -msub));
-            if (masked) {
-              const int kp = kbase + c * 32 + e;
-              if (!key_ok(kp, qpos, a.Sk, a.causal)) p0 = 0.f;
-              if (!key_ok(kp + 1, qpos, a.Sk, a.causal)) p1 = 0.f;
-            }
-            rs4[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
+        for (int i = 0; i < 16; i++) {
+          float p0 = fmaf(__uint_as_float(v[c][2 * i]), a.scale_log2, -msub);
+          float p1 = fmaf(__uint_as_float(v[c][2 * i + 1]), a.scale_log2, -msub);
+          if (a.diag != 1) {  // diag 1: timing without exp2 (results invalid)
+            p0 = ex2(p0);
+            p1 = ex2(p1);
           }
-          tmem_st_32x32b_x16(tS + c * 16, pk);
+          rsc[c] += p0 + p1;
+          v[c][i] = pack_bf16x2(p0, p1);  // word i is no longer needed as input (2i >= i)
+        }
+        tmem_st_32x32b_x16_lo(tS + c * 16, v[c]);
+      }
+      const float rs = (rsc[0] + rsc[1]) + (rsc[2] + rsc[3]);
+      if (rescale && j > 0) {
+        // O_X is quiescent once PV_X(j-1) completed (its commit precedes S_X(j)'s)
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + c * 32, o);
         }
       }
-      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l += rs;
       tmem_st_wait();
       tc_fence_before();
@@ -411,6 +421,7 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
   a.scale_log2 = p.scale * 1.4426950408889634f;
   a.causal = p.causal ? 1 : 0;
   a.n_qblocks = (p.Sq + 2 * TILE - 1) / (2 * TILE);
+  a.diag = p.diag_mode;
   const int smem = (int)sizeof(Smem) + 1024;
   static bool attr = false;
   if (!attr) {

@@ -81,7 +81,7 @@ void gemm(const Tensor& A, const Tensor& W, Tensor& C, const c10::optional<Tenso
   p.force_bn = (int)force_bn;
   static const bool pair_env = [] {
     const char* e = std::getenv("FT_GEMM_2SM");
-    return e != nullptr && e[0] == '1';  // opt-in until the 2-SM kernel is validated on hardware
+    return e == nullptr || e[0] != '0';  // 2-SM kernel by default; FT_GEMM_2SM=0 disables it
   }();
   p.pair_ok = pair_env;
   check_ok(ft::gemm_bf16(p, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
@@ -163,7 +163,8 @@ void rmsnorm(const Tensor& x, Tensor& y, const c10::optional<Tensor>& weight, co
   check_ok(ft::rmsnorm(a, x.size(0), at::cuda::getCurrentCUDAStream()), "rmsnorm");
 }
 
-void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, double scale, bool causal) {
+void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, double scale, bool causal,
+               int64_t diag_mode) {
   for (const Tensor* p : {&q, &k, &v, const_cast<const Tensor*>(&o)}) {
     TORCH_CHECK(p->is_cuda() && p->scalar_type() == at::kBFloat16 && p->dim() == 4,
                 "attention tensors must be 4-D bf16 CUDA [B, S, H, D]");
@@ -196,6 +197,7 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
               "heads must be packed (stride 128 between heads)");
   p.scale = (float)scale;
   p.causal = causal;
+  p.diag_mode = (int)diag_mode;
   p.num_sms = num_sms_for(q.get_device());
   check_ok(ft::attention_fwd(p, at::cuda::getCurrentCUDAStream()), "attention_fwd");
 }
@@ -247,7 +249,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("y"), py::arg("weight") = py::none(), py::arg("cos") = py::none(),
         py::arg("sin") = py::none(), py::arg("head_dim") = 0, py::arg("seq_len") = 0, py::arg("eps") = 1e-6);
   m.def("attention", &attention, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("scale"),
-        py::arg("causal") = false);
+        py::arg("causal") = false, py::arg("diag_mode") = 0);
   m.def("device_error", &device_error, py::arg("reset") = false);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });

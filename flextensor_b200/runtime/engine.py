@@ -37,6 +37,8 @@ class TransferRecord:
     end: object = None
     wait_start: object = None
     wait_end: object = None
+    transfer_ms: float | None = None   # precomputed by the native engine
+    wait_ms: float | None = None
 
 
 class PyTransferEngine:

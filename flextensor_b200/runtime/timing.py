@@ -139,9 +139,13 @@ class OffloadTimingCollector:
                 # records are keyed by the compute label that reads the copy
                 r = out.setdefault(rec.key, TrapTimingRecord(rec.key))
                 r.transfer_bytes = rec.nbytes
-                if rec.start is not None and rec.end is not None:
+                if getattr(rec, "transfer_ms", None) is not None:
+                    r.transfer_ms = rec.transfer_ms
+                elif rec.start is not None and rec.end is not None:
                     r.transfer_ms = rec.start.elapsed_time(rec.end)
-                if rec.wait_start is not None and rec.wait_end is not None:
+                if getattr(rec, "wait_ms", None) is not None:
+                    r.wait_ms = rec.wait_ms
+                elif rec.wait_start is not None and rec.wait_end is not None:
                     r.wait_ms = rec.wait_start.elapsed_time(rec.wait_end)
             self._done.append(out)
         self._pending.clear()
