@@ -283,11 +283,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int c = 0; c < 4; c++) tmem_ld_32x32b_x32(tS + c * 32, v[c]);
       tmem_ld_wait();
       if (masked) {
+        // keys [kbase, kbase + lim) are visible to this row
+        const int lim = min(a.Sk, a.causal ? qpos + 1 : a.Sk) - kbase;
 #pragma unroll
         for (int c = 0; c < 4; c++)
 #pragma unroll
           for (int e = 0; e < 32; e++)
-            if (!key_ok(kbase + c * 32 + e, qpos, a.Sk, a.causal)) v[c][e] = __float_as_uint(-INFINITY);
+            if (c * 32 + e >= lim) v[c][e] = 0xff800000u;
       }
       float mx;
       {
@@ -321,12 +323,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int c = 0; c < 4; c++) {
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          float p0 = fmaf(__uint_as_float(v[c][2 * i]), a.scale_log2, -msub);
-          float p1 = fmaf(__uint_as_float(v[c][2 * i + 1]), a.scale_log2, -msub);
-          if (a.diag != 1) {  // diag 1: timing without exp2 (results invalid)
-            p0 = ex2(p0);
-            p1 = ex2(p1);
-          }
+          const float p0 = ex2(fmaf(__uint_as_float(v[c][2 * i]), a.scale_log2, -msub));
+          const float p1 = ex2(fmaf(__uint_as_float(v[c][2 * i + 1]), a.scale_log2, -msub));
           rsc[c] += p0 + p1;
           v[c][i] = pack_bf16x2(p0, p1);  // word i is no longer needed as input (2i >= i)
         }

@@ -1,0 +1,116 @@
+"""The streaming runtime on a GPU: native transfer engine, slot views, graphs, timing."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("CUDA device required", allow_module_level=True)
+
+import flextensor_b200 as ft  # noqa: E402
+from flextensor_b200.models.wan import WanDiT, init_wan_params_, tiny_config  # noqa: E402
+from flextensor_b200.ops import native  # noqa: E402
+from flextensor_b200.planner import NthLayerStrategy  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def tiny(impl="fused", layers=4):
+    cfg = tiny_config(num_layers=layers)
+    torch.manual_seed(0)
+    m = WanDiT(cfg, impl=impl).to(torch.bfloat16)
+    init_wan_params_(m, seed=0)
+    lat = torch.randn(1, cfg.in_channels, 2, 16, 16, device=DEV, dtype=torch.bfloat16)
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=DEV, dtype=torch.bfloat16)
+    ts = torch.tensor([321.0], device=DEV)
+    return m, (lat, ts, ctx)
+
+
+def cfg(**kw):
+    base = dict(include_patterns=["blocks.*"], skip_discovery=True, profiling_iters=1, num_blocks=2, min_blocks=2,
+                load_strategy=NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2, cyclic=True))
+    base.update(kw)
+    return ft.OffloadConfig(**base)
+
+
+def test_streamed_equals_resident_bitwise():
+    m, inp = tiny()
+    ref_m, _ = tiny()
+    ref_m = ref_m.to(DEV)
+    with torch.no_grad():
+        want = ref_m(*inp)
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg())
+    with torch.no_grad():
+        for _ in range(4):
+            assert torch.equal(mm(*inp), want)
+    tm = om.get_tensor_manager()
+    assert type(tm.loader.engine).__name__ == "NativeTransferEngine"
+    assert native.device_error(reset=True) == 0
+
+
+@pytest.mark.parametrize("mode", ["torch", "host_register"])
+def test_pinning_modes(mode):
+    m, inp = tiny(layers=2)
+    ref = tiny(layers=2)[0].to(DEV)
+    with torch.no_grad():
+        want = ref(*inp)
+    mm = ft.offload(m, cfg(pinned_memory_mode=mode))
+    with torch.no_grad():
+        for _ in range(3):
+            assert torch.equal(mm(*inp), want)
+    blocks = ft.get_offload_manager().get_tensor_manager().loader.plan.host_blocks.values()
+    assert all(b.data.is_pinned() for b in blocks)
+
+
+def test_cuda_graph_capture_of_streamed_forward():
+    m, inp = tiny()
+    ref = tiny()[0].to(DEV)
+    with torch.no_grad():
+        want = ref(*inp)
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg())
+    with torch.no_grad():
+        for _ in range(3):
+            mm(*inp)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g):
+                out = mm(*inp)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+
+
+def test_offload_timing_reports_hidden_fraction():
+    m, inp = tiny()
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg(offload_timing="eager"))
+    with torch.no_grad():
+        for _ in range(5):
+            mm(*inp)
+    rep = ft.collect_offload_timing()
+    assert rep is not None and rep.passes >= 3 and rep.traps
+    assert 0.0 <= rep.hidden_fraction <= 1.0
+    assert rep.total_transfer_ms > 0
+    print(ft.format_offload_timing_table(rep))
+
+
+def test_memory_budget_mode_plans_under_budget():
+    m, inp = tiny(layers=6)
+    total = sum(p.numel() * p.element_size() for p in m.parameters())
+    frac = 0.5 * total / torch.cuda.get_device_properties(0).total_memory
+    om = ft.get_offload_manager()
+    mm = om.offload(m, ft.OffloadConfig(include_patterns=["blocks.*"], skip_discovery=True, profiling_iters=2,
+                                        num_blocks=2, min_blocks=2, max_gpu_mem_fraction=frac,
+                                        load_strategy=ft.BudgetFillStrategy(n_blocks=2, enable_tensor_de=False,
+                                                                            seed=0, epoch=5)))
+    with torch.no_grad():
+        for _ in range(4):
+            mm(*inp)
+    assert om.phase.value == "inference"
