@@ -149,12 +149,19 @@ def build_model(impl: str, layers: int, device, seed: int):
         model = WanDiT(cfg, impl="fused" if impl == "ours" else "torch")
     model = model.to_empty(device=device).to(torch.bfloat16)
     init_wan_params_(model, seed=seed)
-    # weights start in (pinned) host memory, as a loaded checkpoint would
+    # weights start in pinned host memory, as a loaded checkpoint would: one pinned arena,
+    # each parameter a 256-byte aligned view (no per-tensor power-of-two rounding)
     with torch.no_grad():
-        for p in model.parameters():
-            h = torch.empty(p.shape, dtype=p.dtype, pin_memory=True)
+        params = list(model.parameters())
+        sizes = [(p.numel() * p.element_size() + 255) // 256 * 256 for p in params]
+        arena = torch.empty(sum(sizes), dtype=torch.uint8, pin_memory=True)
+        off = 0
+        for p, sz in zip(params, sizes):
+            n = p.numel() * p.element_size()
+            h = arena[off:off + n].view(p.dtype).view(p.shape)
             h.copy_(p.data, non_blocking=True)
             p.data = h
+            off += sz
         for name, b in model.named_buffers():
             b.data = b.data.cpu()
     torch.cuda.synchronize()

@@ -475,11 +475,28 @@ class TensorManager:
             self.phase = TMPhase.INFERENCE
             return
         host_blocks: dict[str, HostBlock] = {}
+        # One pinned arena for every packed block (a per-block pinned allocation would be rounded
+        # up to a power of two by the caching host allocator).
+        from flextensor_b200.core.host_store import alloc_host_bytes, packed_layout
+
+        arena, arena_off = None, 0
+        if self.shm_store is None:
+            need = sum(packed_layout([tensor_nbytes(self.host[t]) for t in load[l]])[1]
+                       for l in order if load.get(l))
+            if need:
+                arena = alloc_host_bytes(need, self.pinned_memory)
         for label in order:
             tids = load.get(label)
             if not tids:
                 continue
             items = [(t, self.id_to_name[t], self.host[t]) for t in tids]
+            if arena is not None:
+                sz = packed_layout([tensor_nbytes(h) for _, _, h in items])[1]
+                blk = pack_tensors(label, items, buffer=arena[arena_off:arena_off + sz], pinned=self.pinned_memory,
+                                   release_sources=self._release_host)
+                arena_off += sz
+                host_blocks[label] = blk
+                continue
             buf = (self.shm_store.block_buffer(label, items, must_exist=self.load_from_shm)
                    if self.shm_store is not None else None)
             if buf is not None and self.load_from_shm:
