@@ -192,7 +192,8 @@ class WanBlock(nn.Module):
         y = F.linear(o.reshape(B, seq_len, cfg.dim), a1.to_out.weight, a1.to_out.bias)
         x = (x.float() + y.float() * gate1).to(x.dtype)
         a2 = self.attn2
-        h = self.norm2(x.float()).to(x.dtype)
+        h = F.layer_norm(x.float(), (cfg.dim,), self.norm2.weight.float(), self.norm2.bias.float(),
+                         eps=cfg.eps).to(x.dtype)
         q = a2.norm_q(F.linear(h, a2.to_q.weight, a2.to_q.bias)).view(B, seq_len, H, Dh)
         L = ctx.shape[1]
         k = a2.norm_k(F.linear(ctx, a2.to_k.weight, a2.to_k.bias)).view(B, L, H, Dh)
