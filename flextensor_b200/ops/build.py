@@ -22,6 +22,7 @@ SOURCES = [
     "gemm_sm100.cu",
     "norm.cu",
     "attention_sm100.cu",
+    "p2p.cu",
 ]
 
 CUDA_FLAGS = [

@@ -206,7 +206,8 @@ int device_error(bool reset) {
   int e = ft::gemm_device_error(reset);
   int n = ft::norm_device_error(reset);
   int a = ft::attn_device_error(reset);
-  return e ? e : (n ? n : a);
+  int p = ft::p2p_device_error(reset);
+  return e ? e : (n ? n : (a ? a : p));
 }
 
 struct PyEngine {
@@ -228,6 +229,27 @@ struct PyEngine {
   void wait_ready(int key) { e->wait_ready(key, cs()); }
   void finish_use(int slot) { e->finish_use(slot, cs()); }
   void join() { e->join(cs()); }
+  void enable_striping(std::vector<uintptr_t> heaps, std::vector<uintptr_t> flags, std::vector<uintptr_t> acks,
+                       int rank, int n_slots, std::vector<uint64_t> slot_offsets, uintptr_t counters, int ctas) {
+    const int world = (int)heaps.size();
+    TORCH_CHECK(world >= 1 && world <= ft::kMaxRanks, "world size must be in [1, 8]");
+    TORCH_CHECK((int)flags.size() == world && (int)acks.size() == world, "per-rank pointer lists differ in length");
+    ft::PeerTable t;
+    for (int i = 0; i < world; i++) {
+      t.heap[i] = reinterpret_cast<uint8_t*>(heaps[i]);
+      t.flags[i] = reinterpret_cast<uint64_t*>(flags[i]);
+      t.acks[i] = reinterpret_cast<uint64_t*>(acks[i]);
+    }
+    t.rank = rank;
+    t.world = world;
+    t.n_slots = n_slots;
+    e->enable_striping(t, slot_offsets, reinterpret_cast<unsigned int*>(counters), ctas);
+  }
+  void submit_striped(int slot, const Tensor& src, int key) {
+    TORCH_CHECK(src.device().is_cpu() && src.is_contiguous(), "striped submit copies a contiguous host block");
+    c10::cuda::CUDAGuard g(device);
+    e->submit_striped(slot, src.data_ptr(), src.numel() * src.element_size(), key);
+  }
   void synchronize() { e->synchronize(); }
   std::vector<std::tuple<int, size_t, float, float>> take_samples() {
     std::vector<std::tuple<int, size_t, float, float>> out;
@@ -253,6 +275,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("device_error", &device_error, py::arg("reset") = false);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
+  m.def("device_malloc", [](size_t n) { return reinterpret_cast<uintptr_t>(ft::device_malloc(n)); });
+  m.def("device_free", [](uintptr_t p) { ft::device_free(reinterpret_cast<void*>(p)); });
+  m.def("ipc_handle", [](uintptr_t p) { return py::bytes(ft::ipc_handle(reinterpret_cast<void*>(p))); });
+  m.def("ipc_open", [](py::bytes h) { return reinterpret_cast<uintptr_t>(ft::ipc_open(std::string(h))); });
+  m.def("ipc_close", [](uintptr_t p) { ft::ipc_close(reinterpret_cast<void*>(p)); });
   py::class_<PyEngine>(m, "TransferEngine")
       .def(py::init<int, int, int, bool>())
       .def("begin", &PyEngine::begin)
@@ -260,6 +287,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("wait_ready", &PyEngine::wait_ready)
       .def("finish_use", &PyEngine::finish_use)
       .def("join", &PyEngine::join)
+      .def("enable_striping", &PyEngine::enable_striping)
+      .def("submit_striped", &PyEngine::submit_striped)
       .def("synchronize", &PyEngine::synchronize)
       .def("take_samples", &PyEngine::take_samples);
 }

@@ -1,0 +1,26 @@
+// Peer-memory data plane (p2p.cu) and symmetric-heap helpers (runtime.cpp).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ft {
+
+constexpr int kMaxRanks = 8;
+
+// Device pointers, valid in this process, into every rank's symmetric heap.
+struct PeerTable {
+  uint8_t* heap[kMaxRanks];   // base of rank p's heap (own heap at [rank])
+  uint64_t* flags[kMaxRanks]; // rank p's flag array [world][n_slots]: flags[src][slot] = last published epoch
+  uint64_t* acks[kMaxRanks];  // rank p's ack array  [world][n_slots]: acks[src][slot] = last epoch src finished reading
+  int rank = 0;
+  int world = 1;
+  int n_slots = 0;
+};
+
+cudaError_t p2p_publish(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s);
+cudaError_t p2p_wait_acks(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s);
+cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+                       uint64_t total_bytes, unsigned int* done_counter, int ctas, cudaStream_t s);
+int p2p_device_error(bool reset);
+
+}  // namespace ft

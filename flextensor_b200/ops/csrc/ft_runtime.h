@@ -3,7 +3,10 @@
 #include <cuda_runtime.h>
 
 #include <cstddef>
+#include <string>
 #include <vector>
+
+#include "ft_p2p.h"
 
 namespace ft {
 
@@ -17,6 +20,13 @@ struct TransferSample {
   float wait_ms = 0.f;
 };
 
+// Symmetric heap: cudaMalloc'd on this device, exported with CUDA IPC.
+void* device_malloc(size_t bytes);
+void device_free(void* p);
+std::string ipc_handle(void* p);
+void* ipc_open(const std::string& handle);
+void ipc_close(void* p);
+
 class TransferEngine {
  public:
   TransferEngine(int device, int n_slots, int n_keys, bool timing);
@@ -29,6 +39,11 @@ class TransferEngine {
   void synchronize();
   std::vector<TransferSample> take_samples();
   cudaStream_t copy_stream() const { return copy_; }
+  // Striped mode: slot `s` lives at heap offset slot_offsets[s] of every rank's symmetric heap;
+  // submit() then copies only this rank's stripe and gathers the others from peers.
+  void enable_striping(const PeerTable& t, const std::vector<uint64_t>& slot_offsets, unsigned int* counters,
+                       int gather_ctas);
+  void submit_striped(int slot, const void* host_src, size_t bytes, int key);
 
  private:
   int device_;
@@ -41,6 +56,12 @@ class TransferEngine {
   std::vector<cudaEvent_t> t_start_, t_end_, w_start_, w_end_;
   std::vector<size_t> bytes_;
   std::vector<char> t_valid_, w_valid_;
+  bool striped_ = false;
+  PeerTable peers_;
+  std::vector<uint64_t> slot_offsets_;
+  std::vector<uint64_t> epochs_;
+  unsigned int* counters_ = nullptr;
+  int gather_ctas_ = 32;
 };
 
 }  // namespace ft

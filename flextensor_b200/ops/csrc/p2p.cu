@@ -1,0 +1,125 @@
+// Peer-memory data plane for striped weight streaming (NVLink 5 / NVSwitch).
+//
+// Every rank owns a symmetric device heap (same layout on every rank, mapped into
+// every peer through CUDA IPC). A weight block is streamed as N stripes: rank r
+// copies stripe r host->device into its own slot, then
+//   publish  : one thread stores epoch into flags[r][slot] of EVERY rank
+//              (st.release.sys, so the stripe bytes are visible before the flag);
+//   gather   : CTAs wait (ld.acquire.sys, bounded) until flags[p][slot] >= epoch for each
+//              peer p, pull stripe p from p's slot with 16-byte loads over NVLink into the
+//              local slot, and the last CTA to finish stores epoch into acks[r][slot] of
+//              every peer (so p may overwrite its slot for the next epoch);
+//   wait_acks: before the next H2D into a slot, wait until every peer acked the previous
+//              epoch of that slot.
+// These kernels wait on OTHER GPUs only (never on another launch on the same GPU). No
+// TMA and no multicast is used: plain peer loads and stores. Every wait has a clock64
+// bound; on timeout the kernel records kErrPeerTimeout in the device error word and returns.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ft_p2p.h"
+#include "sm100_common.cuh"
+
+namespace ft {
+
+FT_DEFINE_ERROR_READER(p2p_device_error)
+
+namespace {
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ bool wait_geq(const uint64_t* p, uint64_t target) {
+  const long long t0 = clock64();
+  while (ld_acquire_sys(p) < target) {
+    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
+      record_error(kErrPeerTimeout);
+      return false;
+    }
+    if (error_raised()) return false;
+    __nanosleep(200);
+  }
+  return true;
+}
+
+__global__ void publish_kernel(PeerTable t, int slot, uint64_t epoch) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < t.world; p++) st_release_sys(t.flags[p] + (size_t)t.rank * t.n_slots + slot, epoch);
+  }
+}
+
+__global__ void wait_acks_kernel(PeerTable t, int slot, uint64_t epoch) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const uint64_t* mine = t.acks[t.rank];
+    for (int p = 0; p < t.world; p++) {
+      if (p == t.rank) continue;
+      if (!wait_geq(mine + (size_t)p * t.n_slots + slot, epoch)) return;
+    }
+  }
+}
+
+__global__ void gather_kernel(PeerTable t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+                              uint64_t total_bytes, unsigned int* done_counter) {
+  __shared__ int ok;
+  const uint64_t* myflags = t.flags[t.rank];
+  for (int pi = 1; pi < t.world; pi++) {
+    const int p = (t.rank + pi) % t.world;  // stagger peers so ranks do not all hit the same source
+    if (threadIdx.x == 0) ok = wait_geq(myflags + (size_t)p * t.n_slots + slot, epoch) ? 1 : 0;
+    __syncthreads();
+    if (!ok) return;
+    const uint64_t begin = (uint64_t)p * stripe_bytes;
+    const uint64_t end = begin + stripe_bytes < total_bytes ? begin + stripe_bytes : total_bytes;
+    if (begin >= end) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(t.heap[p] + slot_offset + begin);
+    uint4* dst = reinterpret_cast<uint4*>(t.heap[t.rank] + slot_offset + begin);
+    const uint64_t n16 = (end - begin) / 16;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (uint64_t)gridDim.x * blockDim.x) {
+      uint4 v = __ldcs(src + i);  // streaming: each peer byte is read exactly once
+      __stcg(dst + i, v);
+    }
+  }
+  // last CTA out acknowledges every peer's stripe for this epoch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(done_counter + slot, 1u);
+    if (prev == gridDim.x - 1) {
+      atomicExch(done_counter + slot, 0u);
+      for (int p = 0; p < t.world; p++) {
+        if (p == t.rank) continue;
+        st_release_sys(t.acks[p] + (size_t)t.rank * t.n_slots + slot, epoch);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t p2p_publish(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s) {
+  publish_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t p2p_wait_acks(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s) {
+  if (t.world <= 1 || epoch == 0) return cudaSuccess;
+  wait_acks_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+                       uint64_t total_bytes, unsigned int* done_counter, int ctas, cudaStream_t s) {
+  if (t.world <= 1) return cudaSuccess;
+  if ((slot_offset | stripe_bytes) & 15) return cudaErrorInvalidValue;
+  gather_kernel<<<ctas, 512, 0, s>>>(t, slot, epoch, slot_offset, stripe_bytes, total_bytes, done_counter);
+  return cudaGetLastError();
+}
+
+}  // namespace ft

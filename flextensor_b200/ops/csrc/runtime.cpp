@@ -12,6 +12,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -89,6 +91,37 @@ void host_unregister(void* ptr) {
   cudaError_t e = cudaHostUnregister(ptr);
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaHostUnregister failed: ") + cudaGetErrorString(e));
 }
+
+// ------------------------------------------------------------------ symmetric heap (CUDA IPC)
+void* device_malloc(size_t bytes) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaMemset failed: ") + cudaGetErrorString(e));
+  return p;
+}
+
+void device_free(void* p) { cudaFree(p); }
+
+std::string ipc_handle(void* p) {
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaIpcGetMemHandle failed: ") + cudaGetErrorString(e));
+  return std::string(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+void* ipc_open(const std::string& handle) {
+  if (handle.size() != sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaIpcOpenMemHandle failed: ") + cudaGetErrorString(e));
+  return p;
+}
+
+void ipc_close(void* p) { cudaIpcCloseMemHandle(p); }
 
 // ------------------------------------------------------------------ transfer engine
 #define FT_CHECK(x)                                                                                \
@@ -196,6 +229,43 @@ void TransferEngine::join(cudaStream_t compute) {
 }
 
 void TransferEngine::synchronize() { FT_CHECK(cudaStreamSynchronize(copy_)); }
+
+void TransferEngine::enable_striping(const PeerTable& t, const std::vector<uint64_t>& slot_offsets,
+                                     unsigned int* counters, int gather_ctas) {
+  peers_ = t;
+  slot_offsets_ = slot_offsets;
+  epochs_.assign(slot_offsets.size(), 0);
+  counters_ = counters;
+  gather_ctas_ = gather_ctas;
+  striped_ = t.world > 1;
+}
+
+void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes, int key) {
+  if (!striped_) throw std::runtime_error("submit_striped without enable_striping");
+  if (slot_recorded_[slot]) FT_CHECK(cudaStreamWaitEvent(copy_, slot_free_[slot], 0));
+  const uint64_t epoch = ++epochs_[slot];
+  const bool t = timing_ && !capturing_;
+  if (t) FT_CHECK(cudaEventRecord(t_start_[key], copy_));
+  // peers must have finished reading this slot's previous contents (our stripe) before we overwrite it
+  FT_CHECK(p2p_wait_acks(peers_, slot, epoch - 1, copy_));
+  const int W = peers_.world, r = peers_.rank;
+  const uint64_t stripe = ((bytes + W - 1) / W + 255) / 256 * 256;
+  const uint64_t b0 = std::min<uint64_t>((uint64_t)r * stripe, bytes);
+  const uint64_t b1 = std::min<uint64_t>(b0 + stripe, bytes);
+  uint8_t* dst = peers_.heap[r] + slot_offsets_[slot];
+  if (b1 > b0)
+    FT_CHECK(cudaMemcpyAsync(dst + b0, static_cast<const uint8_t*>(host_src) + b0, b1 - b0, cudaMemcpyHostToDevice,
+                             copy_));
+  FT_CHECK(p2p_publish(peers_, slot, epoch, copy_));
+  FT_CHECK(p2p_gather(peers_, slot, epoch, slot_offsets_[slot], stripe, bytes, counters_, gather_ctas_, copy_));
+  FT_CHECK(cudaEventRecord(ready_[key], copy_));
+  ready_recorded_[key] = 1;
+  if (t) {
+    FT_CHECK(cudaEventRecord(t_end_[key], copy_));
+    bytes_[key] = bytes;
+    t_valid_[key] = 1;
+  }
+}
 
 std::vector<TransferSample> TransferEngine::take_samples() {
   std::vector<TransferSample> out;

@@ -1,0 +1,134 @@
+"""Striped host streaming across the GPUs of one node.
+
+With N ranks each running a replica of the same offloaded model, every ring slot
+lives in a symmetric heap. When a trap's weights are prefetched, rank r copies
+only stripe r (1/N of the packed host block) over its own PCIe link, then a pull
+kernel gathers the other N-1 stripes from the peers' slots over NVLink (see
+``ops/csrc/p2p.cu``). Host-link bytes per rank drop N-fold, so the node's
+aggregate PCIe bandwidth -- and, with the shared-memory store, one host copy of
+the weights -- serves all ranks.
+
+Enable before ``offload()``::
+
+    flextensor_b200.parallel.enable_striped_streaming()      # default process group
+
+or set ``FT_STRIPED_STREAMING=1`` (the TensorManager then uses the default group).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from flextensor_b200.config import _register_env_var
+from flextensor_b200.ops import native
+from flextensor_b200.parallel.symm import SymmetricHeap
+
+_register_env_var("FT_STRIPED_STREAMING")
+
+_STATE = {"enabled": False, "group": None}
+HEADER_ALIGN = 4096
+SLOT_ALIGN = 4096
+
+
+def enable_striped_streaming(group=None) -> None:
+    _STATE["enabled"] = True
+    _STATE["group"] = group
+
+
+def disable_striped_streaming() -> None:
+    _STATE["enabled"] = False
+    _STATE["group"] = None
+
+
+def striping_group():
+    """The group to stripe over, or ``None`` when striping is off / single process."""
+    import torch.distributed as dist
+
+    on = _STATE["enabled"] or os.environ.get("FT_STRIPED_STREAMING", "0") not in ("", "0", "false", "False")
+    if not on or not dist.is_available() or not dist.is_initialized():
+        return None
+    g = _STATE["group"]
+    return g if dist.get_world_size(g) > 1 else None
+
+
+class StripedTransferEngine:
+    """Native engine in striped mode; owns the symmetric heap that backs the ring slots."""
+
+    def __init__(self, device: torch.device, slot_bytes: dict[int, int], group=None, timing: bool = False,
+                 gather_ctas: int = 32, max_keys: int = 4096):
+        self.device = torch.device(device)
+        n_slots = max(slot_bytes) + 1 if slot_bytes else 1
+        import torch.distributed as dist
+
+        world = dist.get_world_size(group)
+        hdr = world * n_slots * 8 * 2 + n_slots * 4
+        hdr = (hdr + HEADER_ALIGN - 1) // HEADER_ALIGN * HEADER_ALIGN
+        offs, cur = [0] * n_slots, hdr
+        for s in range(n_slots):
+            offs[s] = cur
+            cur += (slot_bytes.get(s, 0) + SLOT_ALIGN - 1) // SLOT_ALIGN * SLOT_ALIGN
+        self.heap = SymmetricHeap(cur, group, self.device.index or 0)
+        self.slot_offsets = offs
+        self.slot_bytes = slot_bytes
+        self.n_slots = n_slots
+        flags = [p for p in self.heap.ptrs]
+        acks = [p + world * n_slots * 8 for p in self.heap.ptrs]
+        counters = self.heap.base + 2 * world * n_slots * 8
+        self._keys: dict[str, int] = {}
+        self._names: list[str] = []
+        self._e = native.lib().TransferEngine(self.device.index or 0, n_slots, max_keys, bool(timing))
+        self._e.enable_striping(list(self.heap.ptrs), flags, acks, self.heap.rank, n_slots, offs, counters,
+                                gather_ctas)
+        self.timing = timing
+        dist.barrier(group=group)  # every rank's heap is open before anyone publishes into it
+
+    # slots are views of the symmetric heap
+    def slot_tensor(self, slot: int, nbytes: int) -> torch.Tensor:
+        return self.heap.view(self.slot_offsets[slot], max(nbytes, 256))
+
+    def _k(self, key: str) -> int:
+        k = self._keys.get(key)
+        if k is None:
+            k = len(self._names)
+            self._keys[key] = k
+            self._names.append(key)
+        return k
+
+    def begin(self) -> None:
+        self._e.begin()
+
+    def submit(self, slot: int, dst: torch.Tensor, src: torch.Tensor, key: str) -> None:
+        self._e.submit_striped(int(slot), src, self._k(key))
+
+    def wait_ready(self, key: str) -> None:
+        k = self._keys.get(key)
+        if k is not None:
+            self._e.wait_ready(k)
+
+    def finish_use(self, slot: int) -> None:
+        self._e.finish_use(int(slot))
+
+    def join(self) -> None:
+        self._e.join()
+
+    def synchronize(self) -> None:
+        self._e.synchronize()
+
+    def reset(self) -> None:
+        self._e.synchronize()
+
+    def take_records(self):
+        from flextensor_b200.runtime.engine import TransferRecord
+
+        out = []
+        for key, nbytes, tms, wms in self._e.take_samples():
+            r = TransferRecord(self._names[key], nbytes)
+            r.transfer_ms, r.wait_ms = tms, wms
+            out.append(r)
+        return out
+
+    def close(self) -> None:
+        self._e.synchronize()
+        self.heap.close()

@@ -58,8 +58,10 @@ class BlockLoader:
         self.last = plan.order[-1] if plan.order else None
         self.c2t = {c: t for t, c in plan.t2c.items()}
         self.compute_slot = {c: plan.transfer_slot[t] for t, c in plan.t2c.items()}
+        alloc = getattr(engine, "slot_tensor", None)
         self.slots: dict[int, torch.Tensor] = {
-            s: torch.empty(max(n, 256), dtype=torch.uint8, device=self.device) for s, n in plan.slot_bytes.items()
+            s: (alloc(s, n) if alloc is not None else torch.empty(max(n, 256), dtype=torch.uint8, device=self.device))
+            for s, n in plan.slot_bytes.items()
         }
         self._pass_active = False
         self._closed = False
@@ -156,6 +158,9 @@ class BlockLoader:
             self.engine.synchronize()
         finally:
             self.slots.clear()
+            close = getattr(self.engine, "close", None)
+            if close is not None:
+                close()
 
 
 class TensorStrategyLoader:

@@ -441,6 +441,7 @@ class TensorManager:
         self.memory_stats = self.benchmark_memory_transfers(max_label)
         budget = self._gpu_budget()
         result = self.strategy.compute(self.layer_stats, self.memory_stats, budget)
+        result = self._agree_on_plan(result)
         self.strategy_result = result
         self._build_from_result(result)
         if self.enable_diagnostics:
@@ -448,6 +449,27 @@ class TensorManager:
 
             log_plan(self)
         return self.model
+
+    def _agree_on_plan(self, result: StrategyResult) -> StrategyResult:
+        """With striped streaming every rank must run rank 0's plan (same slots, same epochs)."""
+        if self.device.type != "cuda":
+            return result
+        from flextensor_b200.parallel.striped import striping_group
+
+        group = striping_group()
+        if group is None:
+            return result
+        import torch.distributed as dist
+
+        box = [result, self.layer_stats] if dist.get_rank(group) == 0 else [None, None]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(box, src=src, group=group)
+        plan, stats = box
+        # rebind tensor ids by name (ids are positional and identical for identical models)
+        if [l.label for l in stats] != [l.label for l in self.layer_stats]:
+            raise RuntimeError("striped streaming needs identical offload units on every rank")
+        self.layer_stats = stats
+        return plan
 
     # ---------------------------------------------------------------- plan -> runtime
     def _build_from_result(self, result: StrategyResult) -> None:
@@ -516,8 +538,16 @@ class TensorManager:
         preload = [t for t in host_blocks if idx[t2c[t]] <= idx[t]]
         plan = SlotPlan(order=order, transfer_slot=slot_of, t2c={t: t2c[t] for t in host_blocks},
                         slot_bytes=slot_bytes, host_blocks=host_blocks, preload=preload)
-        engine = make_engine(self.device, max(slot_bytes, default=0) + 1,
-                             timing=self.timing is not None, external_events=self.offload_timing == "cuda_graph")
+        engine = None
+        if self.device.type == "cuda":
+            from flextensor_b200.parallel.striped import StripedTransferEngine, striping_group
+
+            group = striping_group()
+            if group is not None:
+                engine = StripedTransferEngine(self.device, slot_bytes, group, timing=self.timing is not None)
+        if engine is None:
+            engine = make_engine(self.device, max(slot_bytes, default=0) + 1,
+                                 timing=self.timing is not None, external_events=self.offload_timing == "cuda_graph")
         self.loader = BlockLoader(self.device, plan, engine, timing=self.timing)
         self.loader.bind(self.params_by_tid, setter=self._set_param)
         self.loader.preload()
