@@ -308,14 +308,9 @@ def main():
     hidden = None
     try:
         rep = om.collect_offload_timing()
-        if rep is not None and getattr(rep, "traps", None):
-            if hasattr(rep, "hidden_fraction"):
-                hidden = round(100.0 * rep.hidden_fraction, 2)
-            else:  # reference report: derive from its per-trap aggregates
-                tr = sum(t.transfer_ms["avg"] for t in rep.traps) if hasattr(rep.traps[0], "transfer_ms") else None
-                wt = sum(t.wait_ms["avg"] for t in rep.traps) if hasattr(rep.traps[0], "wait_ms") else None
-                if tr:
-                    hidden = round(100.0 * max(0.0, 1 - wt / tr), 2)
+        if rep is not None and getattr(rep, "total_transfer_sum", 0) > 0:
+            # both runtimes: wait = time the compute stream stalled on a copy
+            hidden = round(100.0 * max(0.0, 1.0 - rep.total_wait_sum / rep.total_transfer_sum), 2)
     except Exception:  # noqa: BLE001
         hidden = None
     try:

@@ -432,7 +432,7 @@ class OffloadManager:
         self._manual_update_state = manual_update_state
         tm = self._tm
         rep = tm.collect_offload_timing() if tm is not None else None
-        if tm is None or rep is None or not rep.traps:
+        if tm is None or rep is None or not rep.per_trap:
             self._replan_status = StrategyReplanStatus.FAILED
             return 0
         budgets = rep.compute_budgets_by_profile_label()

@@ -26,67 +26,137 @@ import torch
 MAX_PASSES = 1024
 
 
-@dataclass
+@dataclass(frozen=True, slots=True)
 class TrapTimingRecord:
+    """One trap in one forward pass (ms); ``wait_ms == 0`` means the copy was fully hidden."""
+
     label: str
-    compute_ms: float = 0.0
     transfer_ms: float = 0.0
+    compute_ms: float = 0.0
     wait_ms: float = 0.0
     transfer_bytes: int = 0
 
 
-@dataclass
+@dataclass(frozen=True, slots=True)
 class OffloadTimingSnapshot:
-    label: str
-    samples: int
-    compute_ms: dict[str, float]
-    transfer_ms: dict[str, float]
-    wait_ms: dict[str, float]
-    transfer_bytes: int
+    """One forward pass; totals are derived from ``per_trap``."""
 
-
-def _agg(v: list[float]) -> dict[str, float]:
-    if not v:
-        return {"min": 0.0, "max": 0.0, "avg": 0.0, "std": 0.0}
-    return {"min": min(v), "max": max(v), "avg": sum(v) / len(v), "std": statistics.pstdev(v) if len(v) > 1 else 0.0}
-
-
-@dataclass
-class OffloadTimingReport:
-    passes: int
-    traps: list[OffloadTimingSnapshot] = field(default_factory=list)
-
-    @property
-    def total_transfer_ms(self) -> float:
-        return sum(t.transfer_ms["avg"] for t in self.traps)
+    per_trap: tuple = ()
 
     @property
     def total_wait_ms(self) -> float:
-        return sum(t.wait_ms["avg"] for t in self.traps)
+        return sum(r.wait_ms for r in self.per_trap)
+
+    @property
+    def total_transfer_ms(self) -> float:
+        return sum(r.transfer_ms for r in self.per_trap)
 
     @property
     def total_compute_ms(self) -> float:
-        return sum(t.compute_ms["avg"] for t in self.traps)
+        return sum(r.compute_ms for r in self.per_trap)
+
+
+@dataclass(frozen=True, slots=True)
+class TrapTimingStats:
+    """One trap aggregated over passes."""
+
+    label: str
+    compute_min: float = 0.0
+    compute_max: float = 0.0
+    compute_avg: float = 0.0
+    compute_median: float = 0.0
+    compute_std: float = 0.0
+    transfer_min: float = 0.0
+    transfer_max: float = 0.0
+    transfer_avg: float = 0.0
+    transfer_median: float = 0.0
+    transfer_std: float = 0.0
+    wait_min: float = 0.0
+    wait_max: float = 0.0
+    wait_avg: float = 0.0
+    wait_median: float = 0.0
+    wait_std: float = 0.0
+    transfer_bytes: int = 0
+
+    def compute_budget_ms(self, *, conservative: bool = False) -> float:
+        """Compute window used as the transfer budget by a replan (median; min when conservative)."""
+        order = (self.compute_min, self.compute_median, self.compute_avg) if conservative else (
+            self.compute_median, self.compute_avg, self.compute_min)
+        for v in order:
+            if v and v > 0:
+                return float(v)
+        return 0.0
+
+
+def _stats(vals: list[float]) -> tuple[float, float, float, float, float]:
+    if not vals:
+        return (0.0, 0.0, 0.0, 0.0, 0.0)
+    return (min(vals), max(vals), sum(vals) / len(vals), statistics.median(vals),
+            statistics.pstdev(vals) if len(vals) > 1 else 0.0)
+
+
+@dataclass(slots=True)
+class OffloadTimingReport:
+    """Per-trap aggregates (``per_trap``) and the raw passes (``passes``)."""
+
+    per_trap: tuple = ()
+    passes: tuple = ()
+
+    @property
+    def num_passes(self) -> int:
+        return len(self.passes)
+
+    @property
+    def traps(self) -> tuple:
+        return self.per_trap
+
+    @property
+    def total_compute_sum(self) -> float:
+        return sum(s.total_compute_ms for s in self.passes)
+
+    @property
+    def total_transfer_sum(self) -> float:
+        return sum(s.total_transfer_ms for s in self.passes)
+
+    @property
+    def total_wait_sum(self) -> float:
+        return sum(s.total_wait_ms for s in self.passes)
+
+    @property
+    def total_compute_avg(self) -> float:
+        return self.total_compute_sum / self.num_passes if self.num_passes else 0.0
+
+    @property
+    def total_transfer_avg(self) -> float:
+        return self.total_transfer_sum / self.num_passes if self.num_passes else 0.0
+
+    @property
+    def total_wait_avg(self) -> float:
+        return self.total_wait_sum / self.num_passes if self.num_passes else 0.0
 
     @property
     def hidden_fraction(self) -> float:
-        tr = self.total_transfer_ms
-        return 1.0 if tr <= 0 else max(0.0, 1.0 - self.total_wait_ms / tr)
+        """Share of host->device copy time that did not stall compute."""
+        tr = self.total_transfer_sum
+        return 1.0 if tr <= 0 else max(0.0, 1.0 - self.total_wait_sum / tr)
 
-    def compute_budgets_by_profile_label(self) -> dict[str, float]:
-        """Mean compute ms per trap (input to a replan from production timings)."""
-        return {t.label: t.compute_ms["avg"] for t in self.traps}
+    def compute_budgets_by_profile_label(self, profile_labels=None, *, conservative: bool = False) -> dict[str, float]:
+        """Compute window (ms) per trap label, the input of a replan from production timings."""
+        by = {t.label: t.compute_budget_ms(conservative=conservative) for t in self.per_trap}
+        if profile_labels is None:
+            return by
+        return {l: by[l] for l in profile_labels if l in by and by[l] > 0}
 
 
 def format_offload_timing_table(report: OffloadTimingReport | None) -> str:
-    if report is None or not report.traps:
+    if report is None or not report.per_trap:
         return "(no offload timing samples)"
-    rows = [f"{'trap':<32} {'n':>5} {'compute ms':>11} {'transfer ms':>12} {'wait ms':>9} {'MB':>9}"]
-    for t in report.traps:
-        rows.append(f"{t.label[:32]:<32} {t.samples:>5} {t.compute_ms['avg']:>11.3f} {t.transfer_ms['avg']:>12.3f} "
-                    f"{t.wait_ms['avg']:>9.3f} {t.transfer_bytes / 2**20:>9.1f}")
-    rows.append(f"{'TOTAL':<32} {report.passes:>5} {report.total_compute_ms:>11.3f} {report.total_transfer_ms:>12.3f} "
-                f"{report.total_wait_ms:>9.3f}  hidden={report.hidden_fraction * 100:.1f}%")
+    rows = [f"{'trap':<32} {'compute ms':>11} {'transfer ms':>12} {'wait ms':>9} {'MB':>9}"]
+    for t in report.per_trap:
+        rows.append(f"{t.label[:32]:<32} {t.compute_avg:>11.3f} {t.transfer_avg:>12.3f} {t.wait_avg:>9.3f} "
+                    f"{t.transfer_bytes / 2**20:>9.1f}")
+    rows.append(f"{'TOTAL / pass':<32} {report.total_compute_avg:>11.3f} {report.total_transfer_avg:>12.3f} "
+                f"{report.total_wait_avg:>9.3f}  passes={report.num_passes} hidden={report.hidden_fraction * 100:.1f}%")
     return "\n".join(rows)
 
 
@@ -96,7 +166,7 @@ class OffloadTimingCollector:
         self.external = mode == "cuda_graph"
         self.enabled = self.device.type == "cuda" and mode != "off"
         self._pending: list[tuple[dict, list]] = []
-        self._done: deque[dict[str, TrapTimingRecord]] = deque(maxlen=MAX_PASSES)
+        self._done: deque[OffloadTimingSnapshot] = deque(maxlen=MAX_PASSES)
         self._cur: dict | None = None
 
     def _ev(self):
@@ -130,24 +200,24 @@ class OffloadTimingCollector:
             return
         torch.cuda.synchronize(self.device)
         for comp, recs in self._pending:
-            out: dict[str, TrapTimingRecord] = {}
+            vals: dict[str, dict] = {}
             for label, (a, b) in comp.items():
-                r = out.setdefault(label, TrapTimingRecord(label))
+                d = vals.setdefault(label, {})
                 if a is not None and b is not None:
-                    r.compute_ms = a.elapsed_time(b)
+                    d["compute_ms"] = a.elapsed_time(b)
             for rec in recs:
                 # records are keyed by the compute label that reads the copy
-                r = out.setdefault(rec.key, TrapTimingRecord(rec.key))
-                r.transfer_bytes = rec.nbytes
+                d = vals.setdefault(rec.key, {})
+                d["transfer_bytes"] = rec.nbytes
                 if getattr(rec, "transfer_ms", None) is not None:
-                    r.transfer_ms = rec.transfer_ms
+                    d["transfer_ms"] = rec.transfer_ms
                 elif rec.start is not None and rec.end is not None:
-                    r.transfer_ms = rec.start.elapsed_time(rec.end)
+                    d["transfer_ms"] = rec.start.elapsed_time(rec.end)
                 if getattr(rec, "wait_ms", None) is not None:
-                    r.wait_ms = rec.wait_ms
+                    d["wait_ms"] = rec.wait_ms
                 elif rec.wait_start is not None and rec.wait_end is not None:
-                    r.wait_ms = rec.wait_start.elapsed_time(rec.wait_end)
-            self._done.append(out)
+                    d["wait_ms"] = rec.wait_start.elapsed_time(rec.wait_end)
+            self._done.append(OffloadTimingSnapshot(tuple(TrapTimingRecord(l, **d) for l, d in vals.items())))
         self._pending.clear()
 
     def reset(self) -> None:
@@ -158,17 +228,16 @@ class OffloadTimingCollector:
         if not self.enabled:
             return None
         self._resolve()
-        if not self._done:
-            return OffloadTimingReport(passes=0)
+        passes = tuple(self._done)
         labels: list[str] = []
-        for p in self._done:
-            for l in p:
-                if l not in labels:
-                    labels.append(l)
-        traps = []
+        for p in passes:
+            for r in p.per_trap:
+                if r.label not in labels:
+                    labels.append(r.label)
+        per = []
         for l in labels:
-            rs = [p[l] for p in self._done if l in p]
-            traps.append(OffloadTimingSnapshot(
-                l, len(rs), _agg([r.compute_ms for r in rs]), _agg([r.transfer_ms for r in rs]),
-                _agg([r.wait_ms for r in rs]), max(r.transfer_bytes for r in rs)))
-        return OffloadTimingReport(passes=len(self._done), traps=traps)
+            rs = [r for p in passes for r in p.per_trap if r.label == l]
+            c, t, w = _stats([r.compute_ms for r in rs]), _stats([r.transfer_ms for r in rs]), _stats(
+                [r.wait_ms for r in rs])
+            per.append(TrapTimingStats(l, *c, *t, *w, transfer_bytes=max(r.transfer_bytes for r in rs)))
+        return OffloadTimingReport(per_trap=tuple(per), passes=passes)

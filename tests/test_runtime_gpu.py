@@ -95,9 +95,9 @@ def test_offload_timing_reports_hidden_fraction():
         for _ in range(5):
             mm(*inp)
     rep = ft.collect_offload_timing()
-    assert rep is not None and rep.passes >= 3 and rep.traps
+    assert rep is not None and rep.num_passes >= 3 and rep.per_trap
     assert 0.0 <= rep.hidden_fraction <= 1.0
-    assert rep.total_transfer_ms > 0
+    assert rep.total_transfer_sum > 0
     print(ft.format_offload_timing_table(rep))
 
 
