@@ -92,12 +92,13 @@ def qk_rmsnorm_rope(x: torch.Tensor, weight: torch.Tensor | None, cos: torch.Ten
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
-              causal: bool = False, out: torch.Tensor | None = None, _diag_mode: int = 0) -> torch.Tensor:
+              causal: bool = False, out: torch.Tensor | None = None, _diag_mode: int = 0,
+              _trace: torch.Tensor | None = None) -> torch.Tensor:
     """Softmax attention on ``[B, S, H, 128]`` bf16 tensors (GQA when k/v have fewer heads)."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    native.lib().attention(q, k, v, out, float(scale), bool(causal), int(_diag_mode))
+    native.lib().attention(q, k, v, out, float(scale), bool(causal), int(_diag_mode), _trace)
     _count()
     return out

@@ -48,6 +48,7 @@ struct AttnArgs {
   int causal;
   int n_qblocks;  // 256-query blocks per (b, h)
   int diag;
+  unsigned long long* trace;  // debug: clock64 timeline of CTA 0 (null in production)
 };
 
 struct Smem {
@@ -106,6 +107,11 @@ __device__ __forceinline__ bool spin_drain(uint64_t* bar, uint32_t parity) {
     if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES / 4) return false;
   }
   return true;
+}
+
+// debug timeline: slot layout [event][j] with 64 blocks max per event kind
+__device__ __forceinline__ void trace_at(const AttnArgs& a, int ev, int j) {
+  if (a.trace != nullptr && blockIdx.x == 0 && j < 64) a.trace[ev * 64 + j] = clock64();
 }
 
 __device__ __forceinline__ bool key_ok(int kp, int qpos, int Sk, int causal) {
@@ -239,6 +245,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         tc_fence_after();
+        trace_at(a, 0, j);
         issue_PV(0, s, j);
         if (more) {
           if (!mbar_wait(&sm.k_full[s1], ph1)) {
@@ -246,6 +253,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           }
           tc_fence_after();
+          trace_at(a, 1, j);
           issue_S(0, s1);
         }
         if (has_b) {
@@ -254,6 +262,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           }
           tc_fence_after();
+          trace_at(a, 2, j);
           issue_PV(1, s, j);
           if (more) issue_S(1, s1);
         }
@@ -283,6 +292,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       tc_fence_after();
+      if (r == 0) trace_at(a, 4 + 4 * t, j);
       if (a.diag == 2) {  // timing diagnostic: no softmax work at all
         tc_fence_before();
         __syncwarp();
@@ -298,6 +308,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; c++) tmem_ld_32x32b_x32(tS + c * 32, v[c]);
       tmem_ld_wait();
+      if (r == 0) trace_at(a, 5 + 4 * t, j);
       if (masked) {
         // keys [kbase, kbase + lim) are visible to this row
         const int lim = min(a.Sk, a.causal ? qpos + 1 : a.Sk) - kbase;
@@ -355,6 +366,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_st_32x32b_x16_lo(tS + c * 16, v[c]);
       }
       const float rs = (rsc[0] + rsc[1]) + (rsc[2] + rsc[3]);
+      if (r == 0) trace_at(a, 6 + 4 * t, j);
       if (rescale && j > 0) {
         // O_X is quiescent once PV_X(j-1) completed (its commit precedes S_X(j)'s)
         if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
@@ -377,6 +389,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.p_full[t]);
+      if (r == 0) trace_at(a, 7 + 4 * t, j);
     }
     // epilogue: O / l -> bf16
     if (active && ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (n_kv - 1) & 1))) {
@@ -444,6 +457,7 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
   a.causal = p.causal ? 1 : 0;
   a.n_qblocks = (p.Sq + 2 * TILE - 1) / (2 * TILE);
   a.diag = p.diag_mode;
+  a.trace = reinterpret_cast<unsigned long long*>(p.trace);
   const int smem = (int)sizeof(Smem) + 1024;
   static bool attr = false;
   if (!attr) {

@@ -164,7 +164,7 @@ void rmsnorm(const Tensor& x, Tensor& y, const c10::optional<Tensor>& weight, co
 }
 
 void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, double scale, bool causal,
-               int64_t diag_mode) {
+               int64_t diag_mode, const c10::optional<Tensor>& trace) {
   for (const Tensor* p : {&q, &k, &v, const_cast<const Tensor*>(&o)}) {
     TORCH_CHECK(p->is_cuda() && p->scalar_type() == at::kBFloat16 && p->dim() == 4,
                 "attention tensors must be 4-D bf16 CUDA [B, S, H, D]");
@@ -198,6 +198,11 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
   p.scale = (float)scale;
   p.causal = causal;
   p.diag_mode = (int)diag_mode;
+  if (trace && trace->defined()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->numel() >= 12 * 64,
+                "trace must be a CUDA int64 tensor with >= 768 entries");
+    p.trace = trace->data_ptr();
+  }
   p.num_sms = num_sms_for(q.get_device());
   check_ok(ft::attention_fwd(p, at::cuda::getCurrentCUDAStream()), "attention_fwd");
 }
@@ -271,7 +276,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("y"), py::arg("weight") = py::none(), py::arg("cos") = py::none(),
         py::arg("sin") = py::none(), py::arg("head_dim") = 0, py::arg("seq_len") = 0, py::arg("eps") = 1e-6);
   m.def("attention", &attention, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("scale"),
-        py::arg("causal") = false, py::arg("diag_mode") = 0);
+        py::arg("causal") = false, py::arg("diag_mode") = 0, py::arg("trace") = py::none());
   m.def("device_error", &device_error, py::arg("reset") = false);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });

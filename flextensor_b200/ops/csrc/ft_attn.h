@@ -15,7 +15,8 @@ struct AttnProblem {
   long long q_batch = 0, k_batch = 0, v_batch = 0, o_batch = 0;  // element stride between batches
   float scale = 1.f;
   bool causal = false;
-  int diag_mode = 0;  // timing diagnostics only: 1 = no exp2, 2 = no softmax work (results invalid)
+  int diag_mode = 0;
+  void* trace = nullptr;  // debug only: uint64[12*64] clock64 timeline of CTA 0  // timing diagnostics only: 1 = no exp2, 2 = no softmax work (results invalid)
   int num_sms = 0;
 };
 
