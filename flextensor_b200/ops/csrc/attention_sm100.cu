@@ -57,7 +57,7 @@ struct Smem {
   uint8_t v[KV_STAGES][2 * CHUNK];
   uint64_t q_full;
   uint64_t k_full[KV_STAGES], k_empty[KV_STAGES], v_full[KV_STAGES], v_empty[KV_STAGES];
-  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t s_full[2], p_half[2], p_full[2], o_done[2];
   uint64_t drain;
   uint32_t tmem_base;
 };
@@ -68,7 +68,7 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// exp2 on the FMA pipe, used for a quarter of the probabilities so the 16/clk MUFU pipe is
+// exp2 on the FMA pipe, used for 3/8 of the probabilities so the 16/clk MUFU pipe is
 // not the softmax bottleneck. Cody-Waite range reduction x = r + f with r = rint(x) (the
 // 1.5*2^23 magic-add rounding), 2^f on f in [-1/2, 1/2] by a cubic fitted for this kernel by
 // weighted least squares on relative error (max rel. error 7.5e-5, far below bf16's 3.9e-3),
@@ -82,6 +82,31 @@ __device__ __forceinline__ float exp2_fma(float x) {
   const int ri = __float_as_int(t) - 0x4B400000;
   const float y = __int_as_float(__float_as_int(p) + (ri << 23));
   return x <= -126.f ? 0.f : y;
+}
+
+// Blackwell packed fp32 pairs and 3-input max (halve the softmax's FFMA / FADD / FMNMX count)
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -144,6 +169,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int t = 0; t < 2; t++) {
       mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_half[t], 4);
       mbar_init(&sm.p_full[t], 4);
       mbar_init(&sm.o_done[t], 1);
     }
@@ -218,14 +244,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         umma_commit(&sm.s_full[t]);
       };
-      auto issue_PV = [&](int t, int s, int j) {
+      // O += P V over keys [16*k0, 16*k1); P (bf16 pairs) sits in the first 64 columns of S
+      auto issue_PV_part = [&](int t, int s, int j, int k0, int k1) {
         const uint32_t va = smem_u32(sm.v[s]);
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; kk++) {
+        for (int kk = k0; kk < k1; kk++) {
           umma_bf16_ts(tbase + 256 + t * 128, tbase + t * 128 + kk * 8,
                        umma_desc_mnmajor_sw128(va + kk * 16 * 128, CHUNK), idO, (j | kk) != 0);
         }
+      };
+      // P arrives in two halves: the first four PV steps start while the softmax is still
+      // producing keys 64..127
+      auto issue_PV = [&](int t, int s, int j) -> bool {
+        if (!mbar_wait(&sm.p_half[t], j & 1)) return false;
+        tc_fence_after();
+        issue_PV_part(t, s, j, 0, TILE / 32);
+        if (!mbar_wait(&sm.p_full[t], j & 1)) return false;
+        tc_fence_after();
+        issue_PV_part(t, s, j, TILE / 32, TILE / 16);
         umma_commit(&sm.o_done[t]);
+        return true;
       };
       if (ok && n_kv > 0) {
         ok = mbar_wait(&sm.k_full[0], 0);
@@ -240,13 +278,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int s = j % KV_STAGES, s1 = (j + 1) % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1, ph1 = ((j + 1) / KV_STAGES) & 1;
         const bool more = j + 1 < n_kv;
-        if (!mbar_wait(&sm.v_full[s], ph) || !mbar_wait(&sm.p_full[0], j & 1)) {
+        if (!mbar_wait(&sm.v_full[s], ph)) {
           ok = false;
           break;
         }
-        tc_fence_after();
         trace_at(a, 0, j);
-        issue_PV(0, s, j);
+        if (!issue_PV(0, s, j)) {
+          ok = false;
+          break;
+        }
         if (more) {
           if (!mbar_wait(&sm.k_full[s1], ph1)) {
             ok = false;
@@ -257,13 +297,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           issue_S(0, s1);
         }
         if (has_b) {
-          if (!mbar_wait(&sm.p_full[1], j & 1)) {
+          trace_at(a, 2, j);
+          if (!issue_PV(1, s, j)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          trace_at(a, 2, j);
-          issue_PV(1, s, j);
           if (more) issue_S(1, s1);
         }
         umma_commit(&sm.v_empty[s]);
@@ -323,11 +361,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float m0 = __uint_as_float(v[0][0]), m1 = __uint_as_float(v[1][0]);
         float m2 = __uint_as_float(v[2][0]), m3 = __uint_as_float(v[3][0]);
 #pragma unroll
-        for (int e = 1; e < 32; e++) {
-          m0 = fmaxf(m0, __uint_as_float(v[0][e]));
-          m1 = fmaxf(m1, __uint_as_float(v[1][e]));
-          m2 = fmaxf(m2, __uint_as_float(v[2][e]));
-          m3 = fmaxf(m3, __uint_as_float(v[3][e]));
+        for (int e = 0; e < 32; e += 2) {
+          m0 = max3(m0, __uint_as_float(v[0][e]), __uint_as_float(v[0][e + 1]));
+          m1 = max3(m1, __uint_as_float(v[1][e]), __uint_as_float(v[1][e + 1]));
+          m2 = max3(m2, __uint_as_float(v[2][e]), __uint_as_float(v[2][e + 1]));
+          m3 = max3(m3, __uint_as_float(v[3][e]), __uint_as_float(v[3][e + 1]));
         }
         mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
       }
@@ -345,45 +383,66 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         m = m_new;
       }
       const float msub = (m == -INFINITY) ? 0.f : m;
-      float rsc[4] = {0.f, 0.f, 0.f, 0.f};
+      unsigned long long rsc[4] = {0ull, 0ull, 0ull, 0ull};  // packed (even, odd) partial row sums
+      const unsigned long long scale2 = f2pack(a.scale_log2, a.scale_log2);
+      const unsigned long long negm2 = f2pack(-msub, -msub);
 #pragma unroll
       for (int c = 0; c < 4; c++) {
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          const float x0 = fmaf(__uint_as_float(v[c][2 * i]), a.scale_log2, -msub);
-          const float x1 = fmaf(__uint_as_float(v[c][2 * i + 1]), a.scale_log2, -msub);
+          const unsigned long long x2 =
+              fma2(f2pack(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), scale2, negm2);
+          float x0, x1;
+          f2unpack(x2, x0, x1);
           float p0, p1;
-          if ((i & 3) == 3) {  // 1 pair in 4 on the FMA pipe
+          if ((i & 7) == 2 || (i & 7) == 5 || (i & 7) == 7) {  // 3 pairs in 8 on the FMA pipe
             p0 = exp2_fma(x0);
             p1 = exp2_fma(x1);
           } else {
             p0 = ex2(x0);
             p1 = ex2(x1);
           }
-          rsc[c] += p0 + p1;
+          rsc[i & 3] = add2(rsc[i & 3], f2pack(p0, p1));
           v[c][i] = pack_bf16x2(p0, p1);  // word i is no longer needed as input (2i >= i)
         }
         tmem_st_32x32b_x16_lo(tS + c * 16, v[c]);
+        if (c == 1) {
+          // O must be rescaled before ANY of this block's PV steps run, i.e. before p_half.
+          // Chunks 0-1 are stored, so their registers are free for the O round trip here.
+          if (rescale && j > 0) {
+            // O_X is quiescent once PV_X(j-1) completed (its commit precedes S_X(j)'s)
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int oc = 0; oc < 4; oc++) {
+              uint32_t o[32];
+              tmem_ld_32x32b_x32(tO + oc * 32, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st_32x32b_x32(tO + oc * 32, o);
+            }
+          }
+          // keys 0..63 done: let the MMA warp start on them
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_half[t]);
+        }
       }
-      const float rs = (rsc[0] + rsc[1]) + (rsc[2] + rsc[3]);
+      float rs;
+      {
+        float a0, a1, b0, b1, c0, c1, d0, d1;
+        f2unpack(add2(rsc[0], rsc[1]), a0, a1);
+        f2unpack(add2(rsc[2], rsc[3]), b0, b1);
+        rs = (a0 + a1) + (b0 + b1);
+        (void)c0, (void)c1, (void)d0, (void)d1;
+      }
       if (r == 0) trace_at(a, 6 + 4 * t, j);
-      if (rescale && j > 0) {
-        // O_X is quiescent once PV_X(j-1) completed (its commit precedes S_X(j)'s)
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(tO + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st_32x32b_x32(tO + c * 32, o);
-        }
-      }
+      if (!ok) break;
       l += rs;
       tmem_st_wait();
       tc_fence_before();

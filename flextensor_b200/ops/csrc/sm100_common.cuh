@@ -98,18 +98,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t phase)
   return ok != 0;
 }
 
-// Bounded wait for the barrier phase with parity `phase` to complete.
+// Bounded wait for the barrier phase with parity `phase` to complete. The hot loop is
+// try_wait only (it suspends in hardware until the phase completes or a short time
+// limit passes); the clock bound and the global error word are checked every 256 spins,
+// so a completed phase is noticed without a long-latency global load in the way.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, phase)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(a, phase)) return true;
-    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
-      record_error(kErrWaitTimeout);
-      return false;
+    if ((it & 255u) == 0u) {
+      if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
+        record_error(kErrWaitTimeout);
+        return false;
+      }
+      if (error_raised()) return false;
     }
-    if (error_raised()) return false;
   }
 }
 
