@@ -138,7 +138,10 @@ def barrier(pg):
 
 
 # ----------------------------------------------------------------------------- model + runtime per arm
-def build_model(impl: str, layers: int, device, seed: int):
+def build_model(impl: str, layers: int, device, seed: int, on_device: bool = False):
+    """Random-init Wan-14B-shape DiT. ``on_device``: weights stay on the GPU they were initialised
+    on (multi-GPU runs: eight host copies of 28 GB would not fit the host), else they move to
+    one pinned host arena as a loaded checkpoint would."""
     import torch
 
     sys.path.insert(0, ROOT)
@@ -149,6 +152,11 @@ def build_model(impl: str, layers: int, device, seed: int):
         model = WanDiT(cfg, impl="fused" if impl == "ours" else "torch")
     model = model.to_empty(device=device).to(torch.bfloat16)
     init_wan_params_(model, seed=seed)
+    if on_device:
+        torch.cuda.synchronize()
+        model.eval()
+        model.requires_grad_(False)
+        return model, cfg
     # weights start in pinned host memory, as a loaded checkpoint would: one pinned arena,
     # each parameter a 256-byte aligned view (no per-tensor power-of-two rounding)
     with torch.no_grad():
@@ -168,6 +176,30 @@ def build_model(impl: str, layers: int, device, seed: int):
     model.eval()
     model.requires_grad_(False)
     return model, cfg
+
+
+def host_ram_check(impl: str, layers: int, world: int):
+    """None when the N-rank run fits the host's RAM, else the reason it cannot run.
+
+    Our arm holds 1/N of the streamed bytes per rank in pinned memory (stripe-only host
+    store). The reference arm has no striping: every process keeps a whole pinned copy of
+    its offloaded weights (~75% of 28.6 GB) plus packing transients."""
+    import psutil
+
+    from flextensor_b200.models.wan import WAN_14B, WanConfig
+
+    cfg = WanConfig(**{**WAN_14B.__dict__, "num_layers": layers})
+    d, f = cfg.dim, cfg.ffn_dim
+    per_block = 2 * (4 * d * d + 4 * d * d + 2 * d * f)  # bf16: self-attn + cross-attn + FFN
+    streamed = per_block * cfg.num_layers * (1.0 - RESIDENT_FRACTION)
+    per_rank = streamed / world if impl == "ours" else streamed * 1.15
+    need = per_rank * world + world * 4e9  # + ~4 GB host per CUDA/torch process
+    avail = psutil.virtual_memory().available
+    if need > 0.85 * avail:
+        return (f"host RAM: {world} ranks x {per_rank / 1e9:.1f} GB pinned weights + process overhead = "
+                f"{need / 1e9:.0f} GB > 85% of {avail / 1e9:.0f} GB available "
+                f"({'stripe-only' if impl == 'ours' else 'one full host copy per process, no striping'})")
+    return None
 
 
 def weight_budget_fraction(model, device) -> float:
@@ -213,13 +245,25 @@ def import_arm(impl: str):
     return ft, None
 
 
-def _launches(impl: str):
-    """Native kernels launched so far (our arm); the reference arm launches none of ours."""
+def _launches(impl: str, om=None):
+    """Native kernels launched so far (our arm: compute ops + the striped engine's p2p
+    kernels); the reference arm launches none of ours."""
     if impl != "ours":
         return None
     from flextensor_b200.ops.api import launch_count
 
-    return launch_count()
+    n = launch_count()
+    eng = _engine(om)
+    if eng is not None and hasattr(eng, "kernel_launches"):
+        n += eng.kernel_launches()
+    return n
+
+
+def _engine(om):
+    try:
+        return om.get_tensor_manager().loader.engine
+    except Exception:  # noqa: BLE001
+        return None
 
 
 def main():
@@ -234,7 +278,20 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": why}))
         return
     torch.manual_seed(1234 + rank)
-    model, cfg = build_model(args.impl, args.layers, device, seed=rank)
+    if world > 1:
+        why = host_ram_check(args.impl, args.layers, world)
+        if why is not None:
+            if rank == 0:
+                print(json.dumps({"impl": args.impl, "n_gpus": world, "unavailable": why}))
+            pg.destroy_process_group()
+            return
+        if args.impl == "ours":
+            # N replicas of ONE model: each rank streams 1/N of every block over its own host
+            # link and pulls the rest from its peers over NVLink; its host keeps only that stripe
+            from flextensor_b200.parallel import enable_striped_streaming
+
+            enable_striped_streaming()
+    model, cfg = build_model(args.impl, args.layers, device, seed=0, on_device=world > 1)
     frac, total_w, block_w, other_w = weight_budget_fraction(model, device)
     config = make_config(ft, local, frac, args.profiling_iters)
     om = ft.get_offload_manager()
@@ -266,7 +323,7 @@ def main():
     torch.cuda.synchronize()
     torch.cuda.reset_peak_memory_stats(device)
 
-    launches0 = _launches(args.impl)
+    launches0 = _launches(args.impl, om)
     clocks = ClockSampler(local)
     clocks.start()
     times = []
@@ -282,8 +339,11 @@ def main():
         torch.cuda.synchronize()
     barrier(pg)
     step_ms = [s.elapsed_time(e) for s, e in times]
-    launches = (_launches(args.impl) - launches0) // max(1, args.steps) if launches0 is not None else None
-    peak_gb = torch.cuda.max_memory_allocated(device) / 1e9
+    launches = (_launches(args.impl, om) - launches0) // max(1, args.steps) if launches0 is not None else None
+    # ring slots in the symmetric heap (striped runs) live outside torch's allocator: add them
+    eng = _engine(om) if args.impl == "ours" else None
+    heap_bytes = getattr(eng, "device_bytes", 0) if eng is not None else 0
+    peak_gb = (torch.cuda.max_memory_allocated(device) + heap_bytes) / 1e9
     ms = sum(step_ms) / len(step_ms)
 
     # end to end through the public call: H2D inputs from pinned host, forward, D2H result
@@ -316,7 +376,7 @@ def main():
     try:
         tm = om.get_tensor_manager()
         st = tm.get_gpu_memory_usage()
-        blocks_gb = st.blocks_bytes / 1e9
+        blocks_gb = max(st.blocks_bytes, heap_bytes) / 1e9
         resident_gb = st.unmapped_tensors_bytes / 1e9
     except Exception:  # noqa: BLE001
         blocks_gb = resident_gb = None
@@ -349,7 +409,9 @@ def main():
                                               "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "config": {"model": MODEL if args.layers == 40 else f"{MODEL} [layers={args.layers}: NOT the headline]",
-                   "global_batch": world, "seq_len": tokens, "parallelism": f"dp{world}",
+                   "global_batch": world, "seq_len": tokens,
+                   "parallelism": f"dp{world}" + (" + striped host streaming (1/N per rank, NVLink gather)"
+                                                  if world > 1 and args.impl == "ours" else ""),
                    "weight_budget": f"{int(RESIDENT_FRACTION * 100)}% of weight bytes on GPU (incl. ring slots)",
                    "l2": "flushed (256 MB write) before every timed step",
                    "denoise_steps_timed": args.steps},

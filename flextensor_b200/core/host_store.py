@@ -142,14 +142,62 @@ class HostBlock:
     data: torch.Tensor
     entries: list[PackedEntry] = field(default_factory=list)
     shm_name: str | None = None
+    total: int | None = None                  # packed size when ``data`` holds only one stripe
+    stripe: tuple[int, int] | None = None     # [b0, b1) of the packed bytes held in ``data``
 
     @property
     def nbytes(self) -> int:
-        return self.data.numel()
+        """Size of the whole packed block (what a device slot holds)."""
+        return self.total if self.total is not None else self.data.numel()
+
+    @property
+    def stripe_only(self) -> bool:
+        return self.stripe is not None
 
     def view(self, e: PackedEntry, base: torch.Tensor | None = None) -> torch.Tensor:
+        if base is None and self.stripe is not None:
+            raise RuntimeError(f"host block {self.label!r} holds one stripe; whole tensors live on the device only")
         buf = self.data if base is None else base
         return buf[e.offset:e.offset + e.nbytes].view(e.dtype).view(e.shape)
+
+
+def stripe_len(total: int, world: int) -> int:
+    """Stripe length of a packed block: ceil(total / world) rounded up to 256 bytes (the native
+    engine and the gather kernel use the same rule)."""
+    return ((total + world - 1) // world + 255) // 256 * 256
+
+
+def stripe_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    s = stripe_len(total, world)
+    b0 = min(rank * s, total)
+    return b0, min(b0 + s, total)
+
+
+def pack_tensors_stripe(label: str, items: list[tuple[int, str, torch.Tensor]], rank: int, world: int,
+                        pinned: bool = True, release_sources=None, buffer: torch.Tensor | None = None) -> HostBlock:
+    """Pack only stripe ``rank`` of ``world`` of a label's block into host memory.
+
+    The layout (offsets, total) is the one :func:`pack_tensors` would produce, so every rank
+    agrees on it; each rank keeps ``stripe_len(total)`` bytes, and the full block only ever
+    exists in the device slot after the peers' stripes were gathered. Sources may live on the
+    device (copied D2H slice by slice) or on the host.
+    """
+    sizes = [tensor_nbytes(t) for _, _, t in items]
+    offs, total = packed_layout(sizes)
+    b0, b1 = stripe_range(total, rank, world)
+    data = buffer if buffer is not None else alloc_host_bytes(max(b1 - b0, 256), pinned)
+    if data.numel() < b1 - b0:
+        raise ValueError(f"stripe buffer for {label!r} holds {data.numel()} bytes, needs {b1 - b0}")
+    blk = HostBlock(label, data, total=total, stripe=(b0, b1))
+    for (tid, name, t), off, n in zip(items, offs, sizes):
+        blk.entries.append(PackedEntry(tid, name, off, n, t.dtype, tuple(t.shape)))
+        lo, hi = max(off, b0), min(off + n, b1)
+        if hi > lo:
+            src = t.detach().contiguous().reshape(-1).view(torch.uint8)[lo - off:hi - off]
+            data[lo - b0:hi - b0].copy_(src)
+        if release_sources is not None:
+            release_sources(tid)
+    return blk
 
 
 def pack_tensors(label: str, items: list[tuple[int, str, torch.Tensor]], buffer: torch.Tensor | None = None,

@@ -250,10 +250,24 @@ struct PyEngine {
     t.n_slots = n_slots;
     e->enable_striping(t, slot_offsets, reinterpret_cast<unsigned int*>(counters), ctas);
   }
-  void submit_striped(int slot, const Tensor& src, int key) {
+  // total_bytes < 0: src is the whole packed block. Otherwise src holds only this rank's
+  // stripe of a packed block of total_bytes bytes.
+  void submit_striped(int slot, const Tensor& src, int key, int64_t total_bytes) {
     TORCH_CHECK(src.device().is_cpu() && src.is_contiguous(), "striped submit copies a contiguous host block");
     c10::cuda::CUDAGuard g(device);
-    e->submit_striped(slot, src.data_ptr(), src.numel() * src.element_size(), key);
+    const size_t held = src.numel() * src.element_size();
+    if (total_bytes < 0) {
+      e->submit_striped(slot, src.data_ptr(), held, key, false);
+    } else {
+      TORCH_CHECK(held >= e->stripe_bytes((size_t)total_bytes), "stripe buffer holds ", held, " bytes, needs ",
+                  e->stripe_bytes((size_t)total_bytes));
+      e->submit_striped(slot, src.data_ptr(), (size_t)total_bytes, key, true);
+    }
+  }
+  size_t stripe_bytes(size_t total) const { return e->stripe_bytes(total); }
+  void drain_striped() {
+    c10::cuda::CUDAGuard g(device);
+    e->drain_striped();
   }
   void synchronize() { e->synchronize(); }
   std::vector<std::tuple<int, size_t, float, float>> take_samples() {
@@ -293,7 +307,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("finish_use", &PyEngine::finish_use)
       .def("join", &PyEngine::join)
       .def("enable_striping", &PyEngine::enable_striping)
-      .def("submit_striped", &PyEngine::submit_striped)
+      .def("submit_striped", &PyEngine::submit_striped, py::arg("slot"), py::arg("src"), py::arg("key"),
+           py::arg("total_bytes") = -1)
+      .def("stripe_bytes", &PyEngine::stripe_bytes)
+      .def("drain_striped", &PyEngine::drain_striped)
+      .def("kernel_launches", [](const PyEngine& p) { return p.e->kernel_launches(); })
       .def("synchronize", &PyEngine::synchronize)
       .def("take_samples", &PyEngine::take_samples);
 }

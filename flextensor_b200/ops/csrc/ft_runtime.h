@@ -43,7 +43,17 @@ class TransferEngine {
   // submit() then copies only this rank's stripe and gathers the others from peers.
   void enable_striping(const PeerTable& t, const std::vector<uint64_t>& slot_offsets, unsigned int* counters,
                        int gather_ctas);
-  void submit_striped(int slot, const void* host_src, size_t bytes, int key);
+  // host_src is the whole packed block, or (stripe_only) just this rank's stripe of it.
+  void submit_striped(int slot, const void* host_src, size_t bytes, int key, bool stripe_only);
+  // Wait (bounded, on the copy stream) until every peer acknowledged the latest epoch of every
+  // slot, i.e. finished reading this rank's stripes; then synchronize. Call before freeing the heap.
+  void drain_striped();
+  // Kernels this engine launched (striped publish / wait / gather), for launch accounting.
+  uint64_t kernel_launches() const { return kernel_launches_; }
+  // Bytes of the stripe this rank holds for a packed block of `total` bytes (0 past the end).
+  size_t stripe_bytes(size_t total) const;
+  // Stripe length for a packed block of `total` bytes: ceil(total / world) rounded up to 256.
+  size_t stripe_len(size_t total) const;
 
  private:
   int device_;
@@ -57,6 +67,7 @@ class TransferEngine {
   std::vector<size_t> bytes_;
   std::vector<char> t_valid_, w_valid_;
   bool striped_ = false;
+  uint64_t kernel_launches_ = 0;
   PeerTable peers_;
   std::vector<uint64_t> slot_offsets_;
   std::vector<uint64_t> epochs_;

@@ -26,6 +26,8 @@ FT_DEFINE_ERROR_READER(p2p_device_error)
 
 namespace {
 
+constexpr int kGatherThreads = 256;
+
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -66,10 +68,15 @@ __global__ void wait_acks_kernel(PeerTable t, int slot, uint64_t epoch) {
   }
 }
 
-__global__ void gather_kernel(PeerTable t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
-                              uint64_t total_bytes, unsigned int* done_counter) {
+// Small CTAs with a low register cap (launch bounds: 5 x 256 threads per SM) so a gather CTA
+// fits beside one resident CTA of the persistent GEMM / attention kernels on the same SM and
+// the NVLink pull overlaps compute instead of queueing it. Four 16-byte loads in flight per thread.
+__global__ void __launch_bounds__(kGatherThreads, 5)
+gather_kernel(PeerTable t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+              uint64_t total_bytes, unsigned int* done_counter) {
   __shared__ int ok;
   const uint64_t* myflags = t.flags[t.rank];
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (int pi = 1; pi < t.world; pi++) {
     const int p = (t.rank + pi) % t.world;  // stagger peers so ranks do not all hit the same source
     if (threadIdx.x == 0) ok = wait_geq(myflags + (size_t)p * t.n_slots + slot, epoch) ? 1 : 0;
@@ -81,10 +88,16 @@ __global__ void gather_kernel(PeerTable t, int slot, uint64_t epoch, uint64_t sl
     const uint4* src = reinterpret_cast<const uint4*>(t.heap[p] + slot_offset + begin);
     uint4* dst = reinterpret_cast<uint4*>(t.heap[t.rank] + slot_offset + begin);
     const uint64_t n16 = (end - begin) / 16;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (uint64_t)gridDim.x * blockDim.x) {
-      uint4 v = __ldcs(src + i);  // streaming: each peer byte is read exactly once
-      __stcg(dst + i, v);
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n16; i += 4 * stride) {  // streaming: each peer byte is read exactly once
+      const uint4 v0 = __ldcs(src + i), v1 = __ldcs(src + i + stride);
+      const uint4 v2 = __ldcs(src + i + 2 * stride), v3 = __ldcs(src + i + 3 * stride);
+      __stcg(dst + i, v0);
+      __stcg(dst + i + stride, v1);
+      __stcg(dst + i + 2 * stride, v2);
+      __stcg(dst + i + 3 * stride, v3);
     }
+    for (; i < n16; i += stride) __stcg(dst + i, __ldcs(src + i));
   }
   // last CTA out acknowledges every peer's stripe for this epoch
   __syncthreads();
@@ -117,8 +130,8 @@ cudaError_t p2p_wait_acks(const PeerTable& t, int slot, uint64_t epoch, cudaStre
 cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
                        uint64_t total_bytes, unsigned int* done_counter, int ctas, cudaStream_t s) {
   if (t.world <= 1) return cudaSuccess;
-  if ((slot_offset | stripe_bytes) & 15) return cudaErrorInvalidValue;
-  gather_kernel<<<ctas, 512, 0, s>>>(t, slot, epoch, slot_offset, stripe_bytes, total_bytes, done_counter);
+  if ((slot_offset | stripe_bytes | total_bytes) & 15) return cudaErrorInvalidValue;
+  gather_kernel<<<ctas, kGatherThreads, 0, s>>>(t, slot, epoch, slot_offset, stripe_bytes, total_bytes, done_counter);
   return cudaGetLastError();
 }
 

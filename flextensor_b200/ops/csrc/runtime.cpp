@@ -240,7 +240,25 @@ void TransferEngine::enable_striping(const PeerTable& t, const std::vector<uint6
   striped_ = t.world > 1;
 }
 
-void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes, int key) {
+void TransferEngine::drain_striped() {
+  if (!striped_) return;
+  for (size_t slot = 0; slot < epochs_.size(); slot++)
+    if (epochs_[slot] > 0) FT_CHECK(p2p_wait_acks(peers_, (int)slot, epochs_[slot], copy_));
+  FT_CHECK(cudaStreamSynchronize(copy_));
+}
+
+size_t TransferEngine::stripe_len(size_t total) const {
+  const size_t W = (size_t)std::max(1, peers_.world);
+  return ((total + W - 1) / W + 255) / 256 * 256;
+}
+
+size_t TransferEngine::stripe_bytes(size_t total) const {
+  const size_t s = stripe_len(total);
+  const size_t b0 = std::min<size_t>((size_t)peers_.rank * s, total);
+  return std::min<size_t>(b0 + s, total) - b0;
+}
+
+void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes, int key, bool stripe_only) {
   if (!striped_) throw std::runtime_error("submit_striped without enable_striping");
   if (slot_recorded_[slot]) FT_CHECK(cudaStreamWaitEvent(copy_, slot_free_[slot], 0));
   const uint64_t epoch = ++epochs_[slot];
@@ -248,14 +266,15 @@ void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes
   if (t) FT_CHECK(cudaEventRecord(t_start_[key], copy_));
   // peers must have finished reading this slot's previous contents (our stripe) before we overwrite it
   FT_CHECK(p2p_wait_acks(peers_, slot, epoch - 1, copy_));
-  const int W = peers_.world, r = peers_.rank;
-  const uint64_t stripe = ((bytes + W - 1) / W + 255) / 256 * 256;
+  kernel_launches_ += (epoch > 1) ? 3 : 2;  // [wait_acks], publish, gather
+  const int r = peers_.rank;
+  const uint64_t stripe = stripe_len(bytes);
   const uint64_t b0 = std::min<uint64_t>((uint64_t)r * stripe, bytes);
   const uint64_t b1 = std::min<uint64_t>(b0 + stripe, bytes);
   uint8_t* dst = peers_.heap[r] + slot_offsets_[slot];
   if (b1 > b0)
-    FT_CHECK(cudaMemcpyAsync(dst + b0, static_cast<const uint8_t*>(host_src) + b0, b1 - b0, cudaMemcpyHostToDevice,
-                             copy_));
+    FT_CHECK(cudaMemcpyAsync(dst + b0, static_cast<const uint8_t*>(host_src) + (stripe_only ? 0 : b0), b1 - b0,
+                             cudaMemcpyHostToDevice, copy_));
   FT_CHECK(p2p_publish(peers_, slot, epoch, copy_));
   FT_CHECK(p2p_gather(peers_, slot, epoch, slot_offsets_[slot], stripe, bytes, counters_, gather_ctas_, copy_));
   FT_CHECK(cudaEventRecord(ready_[key], copy_));

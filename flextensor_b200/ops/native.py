@@ -15,6 +15,7 @@ import threading
 import torch
 
 from flextensor_b200.ops.build import MODULE_NAME, built_library
+from flextensor_b200.instrumentation.core import instrumentable
 
 _lock = threading.Lock()
 _mod = None
@@ -71,6 +72,7 @@ def device_error(reset: bool = False) -> int:
     return lib().device_error(reset)
 
 
+@instrumentable
 class NativeTransferEngine:
     """C++ ring-slot engine; same interface as ``PyTransferEngine`` (string keys mapped to ints)."""
 

@@ -24,6 +24,7 @@ import torch
 from flextensor_b200.config import _register_env_var
 from flextensor_b200.ops import native
 from flextensor_b200.parallel.symm import SymmetricHeap
+from flextensor_b200.instrumentation.core import instrumentable
 
 _register_env_var("FT_STRIPED_STREAMING")
 
@@ -49,15 +50,16 @@ def striping_group():
     on = _STATE["enabled"] or os.environ.get("FT_STRIPED_STREAMING", "0") not in ("", "0", "false", "False")
     if not on or not dist.is_available() or not dist.is_initialized():
         return None
-    g = _STATE["group"]
+    g = _STATE["group"] if _STATE["group"] is not None else dist.group.WORLD
     return g if dist.get_world_size(g) > 1 else None
 
 
+@instrumentable
 class StripedTransferEngine:
     """Native engine in striped mode; owns the symmetric heap that backs the ring slots."""
 
     def __init__(self, device: torch.device, slot_bytes: dict[int, int], group=None, timing: bool = False,
-                 gather_ctas: int = 32, max_keys: int = 4096):
+                 gather_ctas: int = 16, max_keys: int = 4096):
         self.device = torch.device(device)
         n_slots = max(slot_bytes) + 1 if slot_bytes else 1
         import torch.distributed as dist
@@ -69,6 +71,7 @@ class StripedTransferEngine:
         for s in range(n_slots):
             offs[s] = cur
             cur += (slot_bytes.get(s, 0) + SLOT_ALIGN - 1) // SLOT_ALIGN * SLOT_ALIGN
+        self.group = group
         self.heap = SymmetricHeap(cur, group, self.device.index or 0)
         self.slot_offsets = offs
         self.slot_bytes = slot_bytes
@@ -100,7 +103,20 @@ class StripedTransferEngine:
         self._e.begin()
 
     def submit(self, slot: int, dst: torch.Tensor, src: torch.Tensor, key: str) -> None:
+        """``src`` is the whole packed host block; this rank copies its stripe of it."""
         self._e.submit_striped(int(slot), src, self._k(key))
+
+    def kernel_launches(self) -> int:
+        return int(self._e.kernel_launches())
+
+    @property
+    def device_bytes(self) -> int:
+        """Device memory held outside torch's allocator (the symmetric heap)."""
+        return self.heap.nbytes if self.heap is not None else 0
+
+    def submit_stripe(self, slot: int, stripe: torch.Tensor, key: str, total_bytes: int) -> None:
+        """``stripe`` holds only this rank's stripe of a packed block of ``total_bytes``."""
+        self._e.submit_striped(int(slot), stripe, self._k(key), int(total_bytes))
 
     def wait_ready(self, key: str) -> None:
         k = self._keys.get(key)
@@ -130,5 +146,23 @@ class StripedTransferEngine:
         return out
 
     def close(self) -> None:
-        self._e.synchronize()
-        self.heap.close()
+        """Free the heap once no peer can still read or write it.
+
+        Peers read this rank's stripes and write flags/acks into its heap; the heap is an
+        IPC export, so it may only be freed after (1) every peer acknowledged the latest
+        stripe of every slot (bounded device-side wait) and (2) all ranks reached close
+        (a barrier on the striping group, so no peer publishes into a freed heap)."""
+        if self.heap is None:
+            return
+        import torch.distributed as dist
+
+        try:
+            self._e.drain_striped()
+        finally:
+            err = native.device_error(reset=False)
+            if dist.is_initialized():
+                dist.barrier(group=self.group)
+            self.heap.close()
+            self.heap = None
+        if err:
+            raise RuntimeError(f"striped streaming: device wait timed out (error word {err}) before the heap was freed")

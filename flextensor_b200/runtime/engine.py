@@ -27,6 +27,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
+from flextensor_b200.instrumentation.core import instrumentable
 
 
 @dataclass
@@ -41,6 +42,7 @@ class TransferRecord:
     wait_ms: float | None = None
 
 
+@instrumentable
 class PyTransferEngine:
     """Reference engine; exact on CPU (synchronous copies), event-ordered on CUDA."""
 

@@ -31,6 +31,7 @@ from dataclasses import dataclass, field
 import torch
 
 from flextensor_b200.core.host_store import HostBlock, PackedEntry
+from flextensor_b200.instrumentation.core import instrumentable
 
 logger = logging.getLogger(__name__)
 
@@ -45,6 +46,7 @@ class SlotPlan:
     preload: list[str] = field(default_factory=list)  # transfer labels to issue at construction
 
 
+@instrumentable
 class BlockLoader:
     kind = "block"
 
@@ -80,10 +82,25 @@ class BlockLoader:
                     params_by_tid[e.tensor_id].data = self.slot_view(t, e)
 
     def host_views(self, params_by_tid: dict[int, torch.nn.Parameter]) -> None:
-        """Rebind parameters to their packed host bytes (release with preserve_model)."""
-        for blk in self.plan.host_blocks.values():
+        """Rebind parameters to their packed host bytes (release with preserve_model).
+
+        A stripe-only block (striped streaming) has no whole copy on the host: its
+        parameters are copied out of the device slot into fresh host tensors, one slot
+        load at a time, before the slots go away.
+        """
+        for t, blk in self.plan.host_blocks.items():
+            if not blk.stripe_only:
+                for e in blk.entries:
+                    params_by_tid[e.tensor_id].data = blk.view(e)
+                continue
+            slot = self.plan.transfer_slot[t]
+            self.engine.begin()
+            self._issue(t)
+            self.engine.wait_ready(self.plan.t2c[t])
+            self.engine.join()
             for e in blk.entries:
-                params_by_tid[e.tensor_id].data = blk.view(e)
+                params_by_tid[e.tensor_id].data = self.slot_view(t, e).to("cpu")
+            self.engine.finish_use(slot)
 
     @property
     def blocks_bytes(self) -> int:
@@ -92,9 +109,12 @@ class BlockLoader:
     # -------------------------------------------------------------- schedule
     def _issue(self, t: str) -> None:
         blk = self.plan.host_blocks[t]
-        n = blk.data.numel()
+        n = blk.nbytes
         slot = self.plan.transfer_slot[t]
-        self.engine.submit(slot, self.slots[slot][:n], blk.data, self.plan.t2c[t])
+        if blk.stripe_only:
+            self.engine.submit_stripe(slot, blk.data, self.plan.t2c[t], n)
+        else:
+            self.engine.submit(slot, self.slots[slot][:n], blk.data, self.plan.t2c[t])
 
     def preload(self) -> None:
         if not self.plan.preload:
@@ -163,6 +183,7 @@ class BlockLoader:
                 close()
 
 
+@instrumentable
 class TensorStrategyLoader:
     """Per-tensor streaming: device buffers come from the caching allocator."""
 

@@ -161,6 +161,10 @@ class OffloadManager:
 
     def _make_tm(self) -> TensorManager:
         c = self.config
+        if c.enable_instrumentation:
+            from flextensor_b200.instrumentation import get_registry
+
+            get_registry().enabled = True
         shm_store = None
         if c.shm_enabled:
             from flextensor_b200.shm.store import ShmWeightStore
@@ -335,10 +339,20 @@ class OffloadManager:
             for u in self.units:
                 core = _UnitCore(self._orig_forwards[u.label])
                 self._compiled[u.label] = self._compile_fn(core)
-        if self.config.enable_instrumentation:
-            from flextensor_b200.instrumentation import dump_to_directory
+        self._dump_instrumentation()
 
-            dump_to_directory(self, self.config.instrumentation_output_dir)
+    def _dump_instrumentation(self) -> None:
+        c = self.config
+        if not c.enable_instrumentation or not c.instrumentation_output_dir or self._tm is None:
+            return
+        from flextensor_b200.instrumentation import dump_to_directory
+
+        try:
+            stats = self._tm.get_memory_transfer_stats()
+            dump_to_directory(c.instrumentation_output_dir, extra={
+                "memory_transfer_stats": {str(k): v for k, v in (stats or {}).items()}})
+        except Exception:  # noqa: BLE001 - a failed dump never blocks inference
+            LOGGER.warning("instrumentation dump failed; continuing", exc_info=True)
 
     @_error_boundary
     def update_state(self, *, replay_generation: int = -1) -> None:

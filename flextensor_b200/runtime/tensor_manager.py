@@ -48,6 +48,7 @@ from flextensor_b200.runtime.loaders import BlockLoader, SlotPlan, TensorStrateg
 from flextensor_b200.runtime.timing import OffloadTimingCollector
 from flextensor_b200.runtime.units import Unit
 from flextensor_b200.types import GPUMemoryUsage
+from flextensor_b200.instrumentation.core import instrumentable
 
 logger = logging.getLogger(__name__)
 
@@ -90,6 +91,7 @@ class _ForeignReadMode(TorchFunctionMode):
         return func(*args, **kwargs)
 
 
+@instrumentable
 class TensorManager:
     """Owns tensors, traps, plan and loader for one model."""
 
@@ -161,6 +163,7 @@ class TensorManager:
         self.unmapped_bytes = 0
         self.load_from_shm = False
         self._state_restored_from_profile = False
+        self._stripe = None
 
     # ================================================================== model / units
     def set_model(self, model: nn.Module) -> None:
@@ -222,10 +225,33 @@ class TensorManager:
                 b.data = b.data.to(self.device)
 
     # ================================================================== phases
+    def _striping(self):
+        """(group, rank, world) when striped streaming applies to this manager, else None."""
+        if self.device.type != "cuda" or self.loader_type == "strategy" or self.shm_store is not None:
+            return None
+        from flextensor_b200.parallel.striped import striping_group
+
+        g = striping_group()
+        if g is None:
+            return None
+        import torch.distributed as dist
+
+        return g, dist.get_rank(g), dist.get_world_size(g)
+
     def initialize_warmup(self) -> nn.Module:
         assert self.model is not None, "set_model first"
+        self._stripe = self._striping()
         with torch.no_grad():
             for tid in self.owner:
+                p = self.params_by_tid[tid]
+                if self._stripe is not None and p.device == self.device:
+                    # Striped streaming: the host keeps only this rank's stripe of each packed
+                    # block, so weights that start on the device stay there until the plan is
+                    # built and are then packed stripe by stripe (no full host copy per rank).
+                    self._orig_device.setdefault(tid, p.device)
+                    p.requires_grad_(False)
+                    self.host[tid] = p.data
+                    continue
                 self._to_host(tid)
             self._move_non_unit_to_device()
         self.phase = TMPhase.DISCOVERY
@@ -501,15 +527,39 @@ class TensorManager:
         # up to a power of two by the caching host allocator).
         from flextensor_b200.core.host_store import alloc_host_bytes, packed_layout
 
+        stripe = getattr(self, "_stripe", None)
+        if stripe is not None:
+            from flextensor_b200.core.host_store import pack_tensors_stripe, stripe_range
+
+            _, rank, world = stripe
+            spans = {}
+            for label in order:
+                if load.get(label):
+                    tot = packed_layout([tensor_nbytes(self.host[t]) for t in load[label]])[1]
+                    b0, b1 = stripe_range(tot, rank, world)
+                    spans[label] = (b1 - b0 + 255) // 256 * 256
+            arena = alloc_host_bytes(max(sum(spans.values()), 256), self.pinned_memory)
+            off = 0
+            with torch.no_grad():
+                for label in order:
+                    if label not in spans:
+                        continue
+                    items = [(t, self.id_to_name[t], self.host[t]) for t in load[label]]
+                    host_blocks[label] = pack_tensors_stripe(
+                        label, items, rank, world, pinned=self.pinned_memory,
+                        buffer=arena[off:off + spans[label]])
+                    off += spans[label]
+                    for t, _, h in items:  # drop the device source; the stripe + slot hold it now
+                        self.host[t] = torch.empty(h.shape, dtype=h.dtype, device="meta")
         arena, arena_off = None, 0
-        if self.shm_store is None:
+        if self.shm_store is None and stripe is None:
             need = sum(packed_layout([tensor_nbytes(self.host[t]) for t in load[l]])[1]
                        for l in order if load.get(l))
             if need:
                 arena = alloc_host_bytes(need, self.pinned_memory)
         for label in order:
             tids = load.get(label)
-            if not tids:
+            if not tids or label in host_blocks:
                 continue
             items = [(t, self.id_to_name[t], self.host[t]) for t in tids]
             if arena is not None:
@@ -534,7 +584,7 @@ class TensorManager:
         slot_of = {l: l2b.get(l, i % max(2, self.blocks)) for i, l in enumerate(host_blocks)}
         slot_bytes: dict[int, int] = {}
         for l, b in slot_of.items():
-            slot_bytes[b] = max(slot_bytes.get(b, 0), host_blocks[l].data.numel())
+            slot_bytes[b] = max(slot_bytes.get(b, 0), host_blocks[l].nbytes)
         preload = [t for t in host_blocks if idx[t2c[t]] <= idx[t]]
         plan = SlotPlan(order=order, transfer_slot=slot_of, t2c={t: t2c[t] for t in host_blocks},
                         slot_bytes=slot_bytes, host_blocks=host_blocks, preload=preload)
@@ -543,13 +593,15 @@ class TensorManager:
             from flextensor_b200.parallel.striped import StripedTransferEngine, striping_group
 
             group = striping_group()
-            if group is not None:
+            if group is not None and self.loader_type != "strategy":
                 engine = StripedTransferEngine(self.device, slot_bytes, group, timing=self.timing is not None)
         if engine is None:
             engine = make_engine(self.device, max(slot_bytes, default=0) + 1,
                                  timing=self.timing is not None, external_events=self.offload_timing == "cuda_graph")
         self.loader = BlockLoader(self.device, plan, engine, timing=self.timing)
         self.loader.bind(self.params_by_tid, setter=self._set_param)
+        if stripe is not None:
+            torch.cuda.empty_cache()  # the device copies that were packed into stripes are free now
         self.loader.preload()
         self.phase = TMPhase.INFERENCE
 
@@ -592,7 +644,7 @@ class TensorManager:
                     alloc.setdefault(self.loader.plan.transfer_slot[l], []).append(l)
             l2b = dict(self.loader.plan.transfer_slot)
             bsz = {b: int(n) for b, n in self.loader.plan.slot_bytes.items()}
-            lsz = {l: int(b.data.numel()) for l, b in self.loader.plan.host_blocks.items()}
+            lsz = {l: int(b.nbytes) for l, b in self.loader.plan.host_blocks.items()}
             t2c = dict(self.loader.plan.t2c)
         else:
             alloc, l2b, bsz = {}, {}, {}

@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, on_device):
     import datetime
 
     import torch.distributed as dist
@@ -49,6 +49,8 @@ def _worker(rank, world, port, q):
     ts = torch.tensor([77.0], device=dev)
     with torch.no_grad():
         want = ref(lat, ts, ctx)
+    if on_device:
+        m = m.to(dev)  # device-resident source: the host keeps only this rank's stripe
     enable_striped_streaming()
     om = ft.get_offload_manager()
     mm = om.offload(m, ft.OffloadConfig(gpu_device=rank, include_patterns=["blocks.*"], skip_discovery=True,
@@ -59,28 +61,36 @@ def _worker(rank, world, port, q):
         for _ in range(5):
             ok &= bool(torch.equal(mm(lat, ts, ctx), want))
     torch.cuda.synchronize()
-    engine = type(om.get_tensor_manager().loader.engine).__name__
+    loader = om.get_tensor_manager().loader
+    engine = type(loader.engine).__name__
+    stripe_only = all(b.stripe_only for b in loader.plan.host_blocks.values()) and bool(loader.plan.host_blocks)
     err = native.device_error(reset=True)
     dist.barrier()
-    om.release()
+    om.release()  # preserve_model: every parameter comes back to the host, whole
+    want_sd = {k: v.cpu() for k, v in ref.state_dict().items()}
+    restored = all(torch.equal(v.cpu(), want_sd[k]) for k, v in m.state_dict().items())
+    dist.barrier()
     dist.destroy_process_group()
-    q.put((rank, ok, engine, err))
+    q.put((rank, ok, engine, err, stripe_only == on_device, restored))
 
 
-def test_striped_streaming_two_ranks():
+@pytest.mark.parametrize("on_device", [False, True], ids=["host_source", "device_source_stripe_only"])
+def test_striped_streaming_two_ranks(on_device):
     import torch.multiprocessing as mp
 
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q, on_device)) for r in range(world)]
     for p in ps:
         p.start()
     res = sorted(q.get(timeout=300) for _ in ps)
     for p in ps:
         p.join(60)
-    for rank, ok, engine, err in res:
+    for rank, ok, engine, err, stripe_mode_ok, restored in res:
         assert engine == "StripedTransferEngine"
         assert err == 0
         assert ok, f"rank {rank} output differs from the resident model"
+        assert stripe_mode_ok, f"rank {rank}: host blocks stripe-only={not on_device} unexpectedly"
+        assert restored, f"rank {rank}: release() did not give back the original weights"
