@@ -285,8 +285,16 @@ class OffloadManager:
         self._hook = model.register_forward_hook(self._post_forward, prepend=True)
         if self._pending_state is not None:
             st, self._pending_state = self._pending_state, None
-            tm.initialize_warmup()
-            tm.restore_state(st, model)
+            adopt, self._pending_adopt = getattr(self, "_pending_adopt", False), False
+            if adopt:
+                # model already loaded (e.g. by a serving engine): move only what the plan
+                # moves, in a capacity-safe order, then build the loader without profiling
+                plan = tm.plan_state_adoption(model, st)
+                tm.execute_state_adoption(model, plan)
+                tm.restore_adopted_state(model, st)
+            else:
+                tm.initialize_warmup()
+                tm.restore_state(st, model)
             self._enter_inference()
             return model
         tm.initialize_warmup()
@@ -306,13 +314,19 @@ class OffloadManager:
 
     @_error_boundary
     def offload_from_state(self, model: nn.Module, state: TensorManagerState, config: OffloadConfig | None = None,
-                           *, allow_strategy_replan: bool = True) -> nn.Module:
+                           *, allow_strategy_replan: bool = True, adopt: bool = False) -> nn.Module:
+        """Apply a saved plan without discovery or profiling.
+
+        ``adopt=True``: ``model`` is already placed (typically all on the GPU); its storages
+        are migrated to the plan's placement in a capacity-checked order instead of first
+        moving every offloadable tensor to the host."""
         if config is not None:
             self.set_config(config)
         if state.loader_type != self.config.transfer_mode:
             raise ValueError(f"state loader_type {state.loader_type!r} != config transfer_mode "
                              f"{self.config.transfer_mode!r}")
         self._pending_state = state
+        self._pending_adopt = adopt
         return self.offload(model)
 
     def offload_block(self, name: str):

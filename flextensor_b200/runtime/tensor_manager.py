@@ -238,12 +238,19 @@ class TensorManager:
 
         return g, dist.get_rank(g), dist.get_world_size(g)
 
-    def initialize_warmup(self) -> nn.Module:
+    def initialize_warmup(self, keep_on_device: set[int] | None = None) -> nn.Module:
+        """Move every offloadable tensor to the host and everything else to the device.
+
+        ``keep_on_device``: tensor ids a restored plan keeps resident; they go straight to
+        the device instead of making a host round trip (state adoption)."""
         assert self.model is not None, "set_model first"
         self._stripe = self._striping()
         with torch.no_grad():
             for tid in self.owner:
                 p = self.params_by_tid[tid]
+                if keep_on_device is not None and tid in keep_on_device:
+                    self._to_device(tid)
+                    continue
                 if self._stripe is not None and p.device == self.device:
                     # Striped streaming: the host keeps only this rank's stripe of each packed
                     # block, so weights that start on the device stay there until the plan is
@@ -692,8 +699,53 @@ class TensorManager:
     def load_profile(self, profile_directory: str, model: nn.Module) -> None:
         self.restore_state(self.load_state(profile_directory), model)
 
-    def restore_state(self, state: TensorManagerState, model: nn.Module | None = None) -> None:
-        """Adopt a saved plan: rebind ids by name, then build the loader directly (no profiling)."""
+    # ------------------------------------------------------------------ state adoption
+    def plan_state_adoption(self, model: nn.Module, state: TensorManagerState, *,
+                            host_reserve_bytes: int = 4 << 30, gpu_reserve_bytes: int = 1 << 30):
+        """Read-only plan for moving ``model``'s storages to where ``state`` wants them.
+
+        Capacity is what is free now minus the reserves (host: psutil available; GPU: free
+        plus torch's cached-but-unused bytes). Raises RuntimeError when no order fits."""
+        import psutil
+
+        from flextensor_b200.core.placement import (MemoryCapacity, capture_model_state, plan_state_transition,
+                                                    target_from_profile)
+
+        if state.loader_type != self.loader_type:
+            raise ValueError(f"Saved state uses loader_type='{state.loader_type}' but TensorManager is configured "
+                             f"with loader_type='{self.loader_type}'. Re-profile or use a matching transfer mode.")
+        for nm, v in (("host_reserve_bytes", host_reserve_bytes), ("gpu_reserve_bytes", gpu_reserve_bytes)):
+            if type(v) is not int or v < 0:
+                raise ValueError(f"{nm} must be a non-negative integer")
+        if self.device.type != "cuda":
+            raise ValueError("state adoption plans placement onto a CUDA device")
+        free, _ = torch.cuda.mem_get_info(self.device)
+        cached = torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
+        cap = MemoryCapacity(host_bytes=max(0, psutil.virtual_memory().available - host_reserve_bytes),
+                             gpu_bytes=max(0, free + cached - gpu_reserve_bytes))
+        pinning = "none" if not self.pinned_memory else (
+            "in_place" if self.pinner.mode == "host_register" else "copy")
+        current = capture_model_state(model)
+        target, spec = target_from_profile(current, state, target_device=f"cuda:{self.device.index}",
+                                           pinning=pinning, use_shm=self.shm_store is not None)
+        return plan_state_transition(current, target, transition=spec, capacity=cap)
+
+    def execute_state_adoption(self, model: nn.Module, plan) -> None:
+        """Carry out a plan from :meth:`plan_state_adoption` (before any graph capture)."""
+        from flextensor_b200.core.placement import execute_transition
+
+        with torch.no_grad():
+            execute_transition(model, plan, pin=self.pinner.pin if self.pinned_memory else None)
+
+    def restore_adopted_state(self, model: nn.Module, state: TensorManagerState) -> None:
+        """Build the saved plan's loader on a model whose placement was already adopted."""
+        self.restore_state(state, model, adopted=True)
+
+    def restore_state(self, state: TensorManagerState, model: nn.Module | None = None, *,
+                      adopted: bool = False) -> None:
+        """Adopt a saved plan: rebind ids by name, then build the loader directly (no profiling).
+
+        ``adopted``: tensors the plan keeps resident are not sent through the host first."""
         if model is not None and model is not self.model:
             self.set_model(model)
         name_to_tid = self.name_to_id
@@ -712,7 +764,9 @@ class TensorManager:
                                  load_time_ms=t.load_time_ms) for t in v] for k, v in state.load_strategy.items()})
         self._state_restored_from_profile = True
         if self.phase == TMPhase.NONE:
-            self.initialize_warmup()
+            streamed = {t for ts in load.values() for t in ts}
+            keep = {t for t in self.owner if t not in streamed} if adopted else None
+            self.initialize_warmup(keep_on_device=keep)
         self._build_runtime([s.label for s in state.stats], load, dict(state.transfer_to_compute_map),
                             dict(state.label_to_block_id))
         self.state = state

@@ -114,3 +114,33 @@ def test_memory_budget_mode_plans_under_budget():
         for _ in range(4):
             mm(*inp)
     assert om.phase.value == "inference"
+
+
+def test_state_adoption_into_gpu_loaded_model():
+    """A saved plan adopted into a model that already sits on the GPU (serving-engine path):
+    only the streamed storages move to the host, in a capacity-checked order."""
+    m, inp = tiny()
+    with torch.no_grad():
+        want = tiny()[0].to(DEV)(*inp)
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg())
+    with torch.no_grad():
+        for _ in range(om.iters_before_inference):
+            mm(*inp)
+    state = om.get_tensor_manager().export_state()
+    ft.release()
+    streamed = {s.name for v in state.load_strategy.values() for s in v}
+
+    fresh = tiny()[0].to(DEV)
+    tm_plan = ft.get_offload_manager("adopt")
+    mm2 = tm_plan.offload_from_state(fresh, state, cfg(), adopt=True)
+    assert tm_plan.phase.value == "inference"
+    with torch.no_grad():
+        for _ in range(3):
+            assert torch.equal(mm2(*inp), want)
+    host = tm_plan.get_tensor_manager().host
+    names = tm_plan.get_tensor_manager().id_to_name
+    assert {names[t] for t in host} == streamed
+    tm = tm_plan.get_tensor_manager()
+    assert all(p.device == DEV for t, p in tm.params_by_tid.items() if names[t] not in streamed)
+    ft.release("adopt")
