@@ -138,10 +138,16 @@ def barrier(pg):
 
 
 # ----------------------------------------------------------------------------- model + runtime per arm
-def build_model(impl: str, layers: int, device, seed: int, on_device: bool = False):
-    """Random-init Wan-14B-shape DiT. ``on_device``: weights stay on the GPU they were initialised
-    on (multi-GPU runs: eight host copies of 28 GB would not fit the host), else they move to
-    one pinned host arena as a loaded checkpoint would."""
+def build_model(impl: str, layers: int, device, seed: int, placement: str = "pinned_arena"):
+    """Random-init Wan-14B-shape DiT (initialised on the GPU, then placed).
+
+    ``placement``:
+      * ``pinned_arena`` -- one pinned host arena, each parameter a view (a loaded checkpoint);
+      * ``device``       -- weights stay on the GPU (our multi-GPU runs: the runtime packs each
+        rank's stripe straight from the GPU, so no rank ever holds a whole host copy);
+      * ``pageable``     -- one pageable host tensor per parameter (the reference's multi-GPU
+        runs: it pins and packs them and frees each source as it goes, which keeps N host
+        copies within the host's RAM where a pinned arena per rank would not)."""
     import torch
 
     sys.path.insert(0, ROOT)
@@ -152,8 +158,15 @@ def build_model(impl: str, layers: int, device, seed: int, on_device: bool = Fal
         model = WanDiT(cfg, impl="fused" if impl == "ours" else "torch")
     model = model.to_empty(device=device).to(torch.bfloat16)
     init_wan_params_(model, seed=seed)
-    if on_device:
+    if placement in ("device", "pageable"):
+        with torch.no_grad():
+            if placement == "pageable":
+                for p in model.parameters():
+                    p.data = p.data.cpu()
+                for _, b in model.named_buffers():
+                    b.data = b.data.cpu()
         torch.cuda.synchronize()
+        torch.cuda.empty_cache()
         model.eval()
         model.requires_grad_(False)
         return model, cfg
@@ -192,11 +205,12 @@ def host_ram_check(impl: str, layers: int, world: int):
     d, f = cfg.dim, cfg.ffn_dim
     per_block = 2 * (4 * d * d + 4 * d * d + 2 * d * f)  # bf16: self-attn + cross-attn + FFN
     streamed = per_block * cfg.num_layers * (1.0 - RESIDENT_FRACTION)
-    per_rank = streamed / world if impl == "ours" else streamed * 1.15
+    total = per_block * cfg.num_layers
+    per_rank = streamed / world if impl == "ours" else total * 1.1
     need = per_rank * world + world * 4e9  # + ~4 GB host per CUDA/torch process
     avail = psutil.virtual_memory().available
     if need > 0.85 * avail:
-        return (f"host RAM: {world} ranks x {per_rank / 1e9:.1f} GB pinned weights + process overhead = "
+        return (f"host RAM: {world} ranks x {per_rank / 1e9:.1f} GB host weights + process overhead = "
                 f"{need / 1e9:.0f} GB > 85% of {avail / 1e9:.0f} GB available "
                 f"({'stripe-only' if impl == 'ours' else 'one full host copy per process, no striping'})")
     return None
@@ -291,7 +305,8 @@ def main():
             from flextensor_b200.parallel import enable_striped_streaming
 
             enable_striped_streaming()
-    model, cfg = build_model(args.impl, args.layers, device, seed=0, on_device=world > 1)
+    placement = "pinned_arena" if world == 1 else ("device" if args.impl == "ours" else "pageable")
+    model, cfg = build_model(args.impl, args.layers, device, seed=0, placement=placement)
     frac, total_w, block_w, other_w = weight_budget_fraction(model, device)
     config = make_config(ft, local, frac, args.profiling_iters)
     om = ft.get_offload_manager()
