@@ -50,11 +50,14 @@ class SlotPlan:
 class BlockLoader:
     kind = "block"
 
-    def __init__(self, device: torch.device, plan: SlotPlan, engine, timing=None):
+    def __init__(self, device: torch.device, plan: SlotPlan, engine, timing=None, prefetch_policy=None):
+        from flextensor_b200.runtime.prefetch_policy import PiecewisePrefetchPolicy
+
         self.device = torch.device(device)
         self.plan = plan
         self.engine = engine
         self.timing = timing
+        self.policy = prefetch_policy if prefetch_policy is not None else PiecewisePrefetchPolicy()
         self.order = plan.order
         self.first = plan.order[0] if plan.order else None
         self.last = plan.order[-1] if plan.order else None
@@ -115,6 +118,7 @@ class BlockLoader:
             self.engine.submit_stripe(slot, blk.data, self.plan.t2c[t], n)
         else:
             self.engine.submit(slot, self.slots[slot][:n], blk.data, self.plan.t2c[t])
+        self.policy.on_schedule(t, self.plan.t2c[t])
 
     def preload(self) -> None:
         if not self.plan.preload:
@@ -147,6 +151,7 @@ class BlockLoader:
                 self.timing.on_pass_start()
         if label in self.compute_slot:
             self.engine.wait_ready(label)
+            self.policy.on_wait(label)
         if label in self.plan.transfer_slot:
             self._issue(label)
         if self.timing is not None:
@@ -164,8 +169,16 @@ class BlockLoader:
         if self._pass_active:
             self.engine.join()
             self._pass_active = False
+            self.policy.on_piece_join(at_last_layer=True)
             if self.timing is not None:
                 self.timing.on_pass_end(self.engine)
+
+    def piece_join(self) -> None:
+        """A piecewise CUDA-graph boundary inside the forward: join the copy stream into the
+        compute stream (capture needs it) and report prefetches this forces to complete."""
+        if self._pass_active:
+            self.engine.join()
+            self.policy.on_piece_join(at_last_layer=False)
 
     def sync_prev_onload(self) -> None:
         self.engine.synchronize()

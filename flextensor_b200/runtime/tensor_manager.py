@@ -111,6 +111,7 @@ class TensorManager:
         offload_timing: str = "off",
         enable_diagnostics: bool = False,
         shm_store: Any = None,
+        piecewise_prefetch: str = "warn",
         _compute_transfer_gap: int | None = None,
         _direct_mode: bool = True,
         _use_trace_tensor: bool = False,
@@ -134,6 +135,8 @@ class TensorManager:
         self.offload_timing = offload_timing
         self.enable_diagnostics = enable_diagnostics
         self.shm_store = shm_store
+        self.piecewise_prefetch = piecewise_prefetch
+        self.rearrange = bool(_rearrange_transfers)
         self.compute_transfer_gap = _compute_transfer_gap
         self.phase = TMPhase.NONE
 
@@ -464,16 +467,23 @@ class TensorManager:
     def initialize_inference(self) -> nn.Module:
         self._staging = None
         rows = [r for r in self.collector.get_layer_stats() if r.label in self.unit_tids]
-        untimed = [r.label for r in rows if r.duration is None]
-        if untimed:
-            logger.warning("traps never timed during profiling (kept resident): %s", untimed)
+        from flextensor_b200.runtime.profiling_quality import report_profiling_quality
+
+        report_profiling_quality(self.collector, verbose=self.enable_diagnostics)
         tstats = self._tensor_statistics()
         tstats = {t: s for t, s in tstats.items() if t in self.owner}
         self.layer_stats = compute_layer_statistics(rows, tstats)
+        if self.remove_layers_operations:
+            from flextensor_b200.planner.operations import remove_layers_compound
+
+            ops = [o for o in self.remove_layers_operations if o.get("op") == "remove"]
+            self.layer_stats = remove_layers_compound(self.layer_stats, ops)
         max_label = max((sum(t.size_bytes for t in l.tensors) for l in self.layer_stats), default=1 << 20)
         self.memory_stats = self.benchmark_memory_transfers(max_label)
         budget = self._gpu_budget()
         result = self.strategy.compute(self.layer_stats, self.memory_stats, budget)
+        if self.rearrange and result.strategy_map and self.loader_type != "strategy":
+            result = self._rearranged(result)
         result = self._agree_on_plan(result)
         self.strategy_result = result
         self._build_from_result(result)
@@ -482,6 +492,18 @@ class TensorManager:
 
             log_plan(self)
         return self.model
+
+    def _rearranged(self, result: StrategyResult) -> StrategyResult:
+        """Move transfers to the latest earlier trap that hides them (free traps only)."""
+        from flextensor_b200.planner.common import build_block_data, calculate_transfer_to_compute_map
+        from flextensor_b200.planner.interpolator import create_interpolator_from_benchmarks
+        from flextensor_b200.planner.operations import rearrange_transfers
+
+        interp = create_interpolator_from_benchmarks(self.memory_stats) if self.memory_stats else None
+        t2c = calculate_transfer_to_compute_map(self.layer_stats, result.strategy_map)
+        plan, _ = rearrange_transfers(result.strategy_map, t2c, self.layer_stats, interp,
+                                      gap=self.compute_transfer_gap or 1)
+        return StrategyResult(plan, build_block_data(plan, self.layer_stats, self.blocks))
 
     def _agree_on_plan(self, result: StrategyResult) -> StrategyResult:
         """With striped streaming every rank must run rank 0's plan (same slots, same epochs)."""
@@ -605,7 +627,10 @@ class TensorManager:
         if engine is None:
             engine = make_engine(self.device, max(slot_bytes, default=0) + 1,
                                  timing=self.timing is not None, external_events=self.offload_timing == "cuda_graph")
-        self.loader = BlockLoader(self.device, plan, engine, timing=self.timing)
+        from flextensor_b200.runtime.prefetch_policy import PiecewisePrefetchPolicy
+
+        self.loader = BlockLoader(self.device, plan, engine, timing=self.timing,
+                                  prefetch_policy=PiecewisePrefetchPolicy.from_mode(self.piecewise_prefetch))
         self.loader.bind(self.params_by_tid, setter=self._set_param)
         if stripe is not None:
             torch.cuda.empty_cache()  # the device copies that were packed into stripes are free now
