@@ -1,0 +1,109 @@
+"""FlexTensor worker for vLLM (V1 engine).
+
+``load_model``: read the OffloadConfig (``FT_*`` environment / ``FT_CONFIG_FILE``); when
+enabled, install :class:`FlexTensorBootstrapOffloader` so decoder layers are built and loaded
+into host memory, let vLLM load the model, then hand it to the FlexTensor runtime:
+
+* with a saved profile (``profile_storage_dir`` holding ``profile.json``) the plan is applied
+  directly;
+* otherwise the plan is computed without forward passes (``OffloadManager.offload_static``:
+  per-layer durations estimated from the measured host->device time of each layer's bytes)
+  under ``max_gpu_mem_fraction`` when set.
+
+Units are patched in place, so vLLM keeps calling its own model object. vLLM then sizes the
+KV cache with the ring slots already allocated. Selection of compile/graph behaviour follows
+vLLM's: under vLLM's compile mode the trap boundaries are the opaque custom ops
+``flextensor_b200::pre_compute`` / ``post_compute`` (``external_compile``); CUDA-graph
+replays use device-event timing (``offload_timing="cuda_graph"`` when timing is on).
+Parity: ``src/flextensor/contrib/vllm/v2/worker.py:235-616``. Rejected like the reference:
+expert parallelism / EPLB, and the shared-memory path with TP or PP > 1.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+
+import torch
+
+from flextensor_b200.config import _register_env_var, load_config
+from flextensor_b200.contrib.vllm.offloader import FlexTensorBootstrapOffloader
+from flextensor_b200.contrib.vllm.patterns import resolve_vllm_patterns
+
+LOGGER = logging.getLogger("vllm.flextensor_b200.worker")
+MANAGER_NAME = "vllm"
+_register_env_var("FT_VLLM_USE_V2_WORKER")
+
+from vllm.v1.worker.gpu_worker import Worker  # noqa: E402
+
+
+class FlexTensorWorkerError(RuntimeError):
+    pass
+
+
+def _validate(vllm_config, cfg) -> None:
+    par = vllm_config.parallel_config
+    if getattr(par, "enable_expert_parallel", False) or getattr(par, "enable_eplb", False):
+        raise FlexTensorWorkerError("expert parallelism / EPLB is not supported with FlexTensor offloading")
+    if cfg.shm_enabled and (par.tensor_parallel_size > 1 or par.pipeline_parallel_size > 1):
+        raise FlexTensorWorkerError("the shared-memory weight store needs tensor_parallel_size == "
+                                    "pipeline_parallel_size == 1")
+    if cfg.transfer_mode == "strategy":
+        raise FlexTensorWorkerError("the vLLM worker needs a block transfer_mode")
+
+
+class FlexTensorOffloadWorker(Worker):
+    def load_model(self, *args, **kwargs) -> None:
+        if self.device.index is None:
+            raise FlexTensorWorkerError(f"worker device needs an explicit index, got {self.device}")
+        cfg = load_config(gpu_device=self.device.index)
+        if not cfg.enabled:
+            super().load_model(*args, **kwargs)
+            return
+        if kwargs.get("load_dummy_weights"):
+            raise FlexTensorWorkerError("load_dummy_weights=True is not supported")
+        _validate(self.vllm_config, cfg)
+        inc, exc = resolve_vllm_patterns(cfg)
+        from vllm.config import CompilationMode, CUDAGraphMode
+
+        comp = self.vllm_config.compilation_config
+        external_compile = comp.mode == CompilationMode.VLLM_COMPILE
+        graphs = comp.cudagraph_mode is not None and comp.cudagraph_mode != CUDAGraphMode.NONE
+        timing = cfg.offload_timing
+        if timing != "off":
+            timing = "cuda_graph" if graphs else "eager"
+        cfg = cfg.model_copy(update={"include_patterns": inc, "exclude_patterns": exc,
+                                     "external_compile": external_compile, "offload_timing": timing})
+
+        from vllm.model_executor.offloader.base import NoopOffloader, get_offloader, set_offloader
+
+        prev = get_offloader()
+        if not isinstance(prev, NoopOffloader):
+            raise FlexTensorWorkerError(f"another vLLM offloader is active: {type(prev).__name__}")
+        boot = FlexTensorBootstrapOffloader()
+        set_offloader(boot)
+        import flextensor_b200 as ft
+
+        om = ft.get_offload_manager(MANAGER_NAME)
+        try:
+            super().load_model(*args, **kwargs)
+            raw = self.model_runner.get_model()
+            before = torch.cuda.memory_allocated(self.device)
+            prof = cfg.profile_storage_dir
+            if prof and os.path.exists(os.path.join(prof, "profile.json")):
+                om.set_config(cfg)
+                om.load_profile(prof)
+                om.offload(raw, cfg)
+            else:
+                om.offload_static(raw, cfg)
+            boot.manager = om
+            self.model_runner.model_memory_usage += torch.cuda.memory_allocated(self.device) - before
+            LOGGER.info("FlexTensor took over %s: %.2f GB staged on host, ring slots %.2f GB",
+                        type(raw).__name__, boot.staged_bytes / 1e9,
+                        om.get_gpu_memory_usage().blocks_bytes / 1e9)
+        except Exception:
+            try:
+                om.release()
+            finally:
+                set_offloader(prev)
+            raise

@@ -329,6 +329,31 @@ class OffloadManager:
         self._pending_adopt = adopt
         return self.offload(model)
 
+    @_error_boundary
+    def offload_static(self, model: nn.Module, config: OffloadConfig | None = None, *,
+                       durations_ms: dict[str, float] | None = None) -> nn.Module:
+        """Plan and build the runtime with no discovery or profiling forward passes.
+
+        For models that cannot run a plain forward outside their engine (serving engines that
+        need attention metadata per call). Traps are the selected units and each trap reads
+        exactly its unit's parameters. Trap durations come from ``durations_ms`` or, by
+        default, from a conservative estimate: every unit computes for as long as its own
+        weights take to copy host->device (measured), so a plan that hides each transfer
+        behind one trap's compute is feasible by construction. A real profile can replace
+        the estimate later (``request_strategy_replan`` / a saved profile)."""
+        c = (config or self.config).model_copy(update={"skip_discovery": True})
+        model = self.offload(model, c)
+        tm = self._tm
+        if self.phase != OffloadPhase.PROFILING:
+            return model  # disabled, or nothing matched
+        est = tm.estimate_unit_durations() if durations_ms is None else dict(durations_ms)
+        for label in tm.labels:
+            if label in est:
+                tm.collector.record_duration(label, float(est[label]))
+        tm.initialize_inference()
+        self._enter_inference()
+        return model
+
     def offload_block(self, name: str):
         """Manual trap: ``with om.offload_block("blk"): ...`` (discovered by tensor reads)."""
         if self._skip_discovery_honored:

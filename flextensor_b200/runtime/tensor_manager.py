@@ -436,6 +436,12 @@ class TensorManager:
         del src, dst
         return out
 
+    def estimate_unit_durations(self) -> dict[str, float]:
+        """Per-unit duration estimate: the measured H2D time of the unit's own bytes."""
+        sizes = {l: self._trap_bytes(l) for l in self.labels}
+        ms = self._benchmark_sizes(sorted({max(n, 1) for n in sizes.values()}), reps=3)
+        return {l: ms[max(n, 1)] for l, n in sizes.items()}
+
     def get_memory_transfer_stats(self) -> dict[int, float] | None:
         return self.memory_stats
 
