@@ -207,6 +207,31 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
   check_ok(ft::attention_fwd(p, at::cuda::getCurrentCUDAStream()), "attention_fwd");
 }
 
+// Direct call of the striped gather with a caller-owned counter buffer (tests and tools).
+void p2p_gather_raw(std::vector<uint64_t> heaps, std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank,
+                    int n_slots, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+                    uint64_t total_bytes, const Tensor& counters, int ctas) {
+  const int world = (int)heaps.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kMaxRanks && flags.size() == heaps.size() && acks.size() == heaps.size(),
+              "one heap/flag/ack pointer per rank, at most ", ft::kMaxRanks);
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= n_slots,
+              "counters: int32 CUDA tensor with one entry per slot");
+  ft::PeerTable t;
+  for (int p = 0; p < world; p++) {
+    t.heap[p] = reinterpret_cast<uint8_t*>(heaps[p]);
+    t.flags[p] = reinterpret_cast<uint64_t*>(flags[p]);
+    t.acks[p] = reinterpret_cast<uint64_t*>(acks[p]);
+  }
+  t.rank = rank;
+  t.world = world;
+  t.n_slots = n_slots;
+  c10::cuda::CUDAGuard g(counters.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  const cudaError_t e = ft::p2p_gather(t, slot, epoch, slot_offset, stripe_bytes, total_bytes,
+                                       reinterpret_cast<unsigned int*>(counters.data_ptr<int>()), ctas, s);
+  TORCH_CHECK(e == cudaSuccess, "p2p_gather: ", cudaGetErrorString(e));
+}
+
 int device_error(bool reset) {
   int e = ft::gemm_device_error(reset);
   int n = ft::norm_device_error(reset);
@@ -292,6 +317,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention", &attention, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("scale"),
         py::arg("causal") = false, py::arg("diag_mode") = 0, py::arg("trace") = py::none());
   m.def("device_error", &device_error, py::arg("reset") = false);
+  m.def("p2p_gather_raw", &p2p_gather_raw);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
   m.def("device_malloc", [](size_t n) { return reinterpret_cast<uintptr_t>(ft::device_malloc(n)); });

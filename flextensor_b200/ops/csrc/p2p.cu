@@ -136,3 +136,87 @@ cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t sl
 }
 
 }  // namespace ft
+
+// ======================================================================================
+// No-allocation C entry point for the striped gather.
+//
+// This entry point has no counterpart in the reference (which has no native code). It serves
+// callers that must not allocate device memory on the call path: code driving the gather from
+// plain C or from a foreign runtime with no torch allocator at hand, and engines whose device
+// memory is planned up front, where an allocation on the call path could fail or fragment the
+// pool mid-run.
+//
+// The gather's only scratch is one arrival counter per ring slot (the last CTA out acknowledges
+// the peers and re-zeroes it). Here those counters live in the file-scope device array
+// `g_gather_noalloc_counters` (kGatherNoAllocMaxSlots = 256 counters, 1 KiB) instead of a
+// caller buffer, so a call allocates nothing: no cudaMalloc / cudaFree, no library call that
+// allocates. Slot indices or slot counts beyond 256 are rejected with cudaErrorInvalidValue.
+//
+// Device address: in host code `g_gather_noalloc_counters` names only a host-side stand-in
+// for the symbol, so the kernel never receives it directly. The first call on each device
+// (with that device current) looks the address up with cudaGetSymbolAddress, checks the
+// result and caches it; make that first call on a device before any stream capture begins.
+//
+// Every call on a device shares the one array, and the array keeps whatever the previous call
+// left. The counter of the slot in use is therefore cleared (cudaMemsetAsync on the caller's
+// stream) before each launch, so a call that timed out earlier cannot leave a stale count.
+// Calls whose executions overlap on the GPU (several streams, or several host threads on one
+// device) race on the shared counters and must be serialised by the caller.
+// ======================================================================================
+namespace ft {
+namespace {
+
+constexpr int kGatherNoAllocMaxSlots = 256;
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) unsigned int g_gather_noalloc_counters[kGatherNoAllocMaxSlots];
+
+unsigned int* noalloc_counters_for_current_device(cudaError_t* err) {
+  static unsigned int* cache[kNoAllocMaxDevices] = {};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_gather_noalloc_counters);
+    if (*err != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<unsigned int*>(p);
+  }
+  return cache[dev];
+}
+
+}  // namespace
+}  // namespace ft
+
+// Arguments: per-rank device pointers (heap base, flag array, ack array) for `world` ranks,
+// this rank's index, slots per heap, the slot to gather, its epoch, the slot's byte offset in
+// every heap, the stripe length, the packed block size, the grid size and a cudaStream_t.
+// Returns a cudaError_t value (cudaSuccess = 0).
+extern "C" int ft_p2p_gather_noalloc(const uint64_t* heap_ptrs, const uint64_t* flag_ptrs,
+                                     const uint64_t* ack_ptrs, int world, int rank, int n_slots, int slot,
+                                     uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+                                     uint64_t total_bytes, int ctas, void* stream) {
+  using namespace ft;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return (int)cudaErrorInvalidValue;
+  if (n_slots < 1 || n_slots > ft::kGatherNoAllocMaxSlots || slot < 0 || slot >= n_slots) return (int)cudaErrorInvalidValue;
+  if (ctas < 1 || !heap_ptrs || !flag_ptrs || !ack_ptrs) return (int)cudaErrorInvalidValue;
+  cudaError_t err = cudaSuccess;
+  unsigned int* counters = noalloc_counters_for_current_device(&err);
+  if (counters == nullptr) return (int)err;
+  PeerTable t;
+  for (int p = 0; p < world; p++) {
+    t.heap[p] = reinterpret_cast<uint8_t*>(heap_ptrs[p]);
+    t.flags[p] = reinterpret_cast<uint64_t*>(flag_ptrs[p]);
+    t.acks[p] = reinterpret_cast<uint64_t*>(ack_ptrs[p]);
+  }
+  t.rank = rank;
+  t.world = world;
+  t.n_slots = n_slots;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  err = cudaMemsetAsync(counters + slot, 0, sizeof(unsigned int), s);
+  if (err != cudaSuccess) return (int)err;
+  return (int)p2p_gather(t, slot, epoch, slot_offset, stripe_bytes, total_bytes, counters, ctas, s);
+}
