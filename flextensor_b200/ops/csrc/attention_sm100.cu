@@ -23,6 +23,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "ft_attn.h"
 #include "ft_ops.h"
 #include "sm100_common.cuh"
@@ -38,7 +40,10 @@ constexpr int HD = 128;                   // head dim
 constexpr int CHUNK = 128 * 64 * 2;       // one [128 rows x 64 cols] bf16 swizzled box (16 KB)
 constexpr int KV_STAGES = 2;
 constexpr float RESCALE_THRESHOLD = 8.0f;
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 320;            // plain attention: 10 warps
+constexpr int NTHREADS_CP = 352;         // context-parallel: + warp 10, the K/V gather warp
+constexpr int CP_PIECE = 12288;          // bytes per gather step (peer -> smem -> local HBM)
+constexpr int CP_MAX_KV_BLOCKS = 1024;   // 128-key blocks (131072 keys)
 
 struct AttnArgs {
   int B, Sq, Sk, Hq, Hk;
@@ -51,7 +56,7 @@ struct AttnArgs {
   unsigned long long* trace;  // debug: clock64 timeline of CTA 0 (null in production)
 };
 
-struct Smem {
+struct SmemBase {
   uint8_t q[2][2 * CHUNK];                // tile, d-half
   uint8_t k[KV_STAGES][2 * CHUNK];
   uint8_t v[KV_STAGES][2 * CHUNK];
@@ -60,6 +65,35 @@ struct Smem {
   uint64_t s_full[2], p_half[2], p_full[2], o_done[2];
   uint64_t drain;
   uint32_t tmem_base;
+};
+struct SmemCP : SmemBase {
+  alignas(128) uint8_t stage[2][CP_PIECE];  // gather staging (peer -> here -> local HBM)
+  uint64_t stage_full[2];
+  int n_order;
+  uint16_t order[CP_MAX_KV_BLOCKS];         // KV block processing order (own shard first)
+};
+template <bool CP>
+using SmemT = typename std::conditional<CP, SmemCP, SmemBase>::type;
+
+// Context-parallel extension: this rank's queries attend over the K/V of all ranks. Each rank
+// writes its K/V rows (K|V interleaved per token) into its own copy of the full-sequence
+// buffer and publishes an epoch flag; inside this kernel, warp 10 of every CTA pulls peers'
+// rows into the local buffer (claiming 12 KB pieces from a per-peer ticket counter, so any
+// resident CTA can finish a chunk and no CTA waits on a CTA that is not running), and the TMA
+// producer waits for a peer's chunk to be complete before loading its keys. KV blocks are
+// processed own-shard first, then peers in the order they are gathered.
+struct CpArgs {
+  int rank, world, shard_rows;
+  long long row_bytes, batch_bytes, shard_bytes;  // per token row / batch / one rank's rows of a batch
+  const uint8_t* peer_kv[kCpMaxRanks];             // each rank's full-sequence K|V buffer (own at [rank])
+  uint8_t* local_kv;
+  const uint64_t* flags;                           // flags[q * flag_stride]: epoch rank q published
+  int flag_stride;
+  uint64_t* peer_acks[kCpMaxRanks];                // where to tell rank p we finished reading its rows
+  uint64_t epoch;
+  unsigned int* claim;                             // [world], zero at launch
+  unsigned int* done;                              // [world], zero at launch
+  int pieces_per_batch, batches;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -143,11 +177,111 @@ __device__ __forceinline__ bool key_ok(int kp, int qpos, int Sk, int causal) {
   return kp < Sk && (!causal || kp <= qpos);
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1)
+__device__ bool cp_wait_flag(const uint64_t* f, uint64_t epoch) {
+  const long long t0 = clock64();
+  while (ld_acquire_sys_u64(f) < epoch) {
+    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
+      record_error(kErrPeerTimeout);
+      return false;
+    }
+    if (error_raised()) return false;
+    __nanosleep(128);
+  }
+  return true;
+}
+
+__device__ bool cp_wait_done(const unsigned int* d, unsigned int target) {
+  const long long t0 = clock64();
+  while (ld_acquire_gpu_u32(d) < target) {
+    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
+      record_error(kErrWaitTimeout);
+      return false;
+    }
+    if (error_raised()) return false;
+    __nanosleep(64);
+  }
+  fence_proxy_async_global();  // the rows were written by bulk (async-proxy) stores of other CTAs
+  return true;
+}
+
+// KV blocks in gather order: a block is processed once every rank whose rows it holds is
+// local; blocks needing only this rank's rows come first.
+__device__ void cp_build_order(SmemCP& sm, const CpArgs& c, int Sk) {
+  int n = 0;
+  for (int d = 0; d < c.world; d++) {
+    const int p = (c.rank + d) % c.world;
+    const int first = p * c.shard_rows / TILE, last = ((p + 1) * c.shard_rows - 1) / TILE;
+    for (int kb = first; kb <= last; kb++) {
+      const int lo = kb * TILE / c.shard_rows, hi = min(kb * TILE + TILE - 1, Sk - 1) / c.shard_rows;
+      int md = 0;
+      for (int q = lo; q <= hi; q++) md = max(md, (q - c.rank + c.world) % c.world);
+      if (md == d && n < CP_MAX_KV_BLOCKS) sm.order[n++] = (uint16_t)kb;
+    }
+  }
+  sm.n_order = n;
+}
+
+// Warp 10 (one lane): claim 12 KB pieces of peers' rows and move them peer -> smem -> local
+// HBM with bulk copies, two pieces in flight; the CTA that completes a peer's chunk tells the
+// peer it may overwrite those rows.
+__device__ void cp_gather(SmemCP& sm, const CpArgs& c) {
+  const unsigned int npieces = (unsigned int)(c.pieces_per_batch * c.batches);
+  uint32_t ph[2] = {0, 0};
+  int issued = 0, pend_p = -1;
+  bool ok = true;
+  auto finish = [&](int p) {  // the store of a piece of chunk p has been performed
+    fence_proxy_async_global();
+    const unsigned int old = atom_add_release_gpu_u32(c.done + p, 1u);
+    if (old + 1 == npieces) {
+      __threadfence_system();
+      st_release_sys_u64(c.peer_acks[p], c.epoch);
+    }
+  };
+  for (int d = 1; d < c.world && ok; d++) {
+    const int p = (c.rank + d) % c.world;
+    bool flagged = false;
+    for (;;) {
+      const unsigned int idx = atomicAdd(c.claim + p, 1u);
+      if (idx >= npieces) break;
+      if (!flagged) {
+        if (!cp_wait_flag(c.flags + (size_t)p * c.flag_stride, c.epoch)) {
+          ok = false;
+          break;
+        }
+        flagged = true;
+      }
+      const int b = idx / c.pieces_per_batch;
+      const long long off = (long long)(idx % c.pieces_per_batch) * CP_PIECE;
+      const uint32_t n = (uint32_t)min((long long)CP_PIECE, c.shard_bytes - off);
+      const long long at = (long long)b * c.batch_bytes + (long long)p * c.shard_bytes + off;
+      const int st = issued & 1;
+      mbar_arrive_expect_tx(&sm.stage_full[st], n);
+      bulk_load_g2s(sm.stage[st], c.peer_kv[p] + at, n, &sm.stage_full[st]);
+      if (!mbar_wait(&sm.stage_full[st], ph[st])) {
+        ok = false;
+        break;
+      }
+      ph[st] ^= 1;
+      bulk_store_s2g(c.local_kv + at, sm.stage[st], n);
+      bulk_commit();
+      issued++;
+      if (pend_p >= 0) {
+        bulk_wait<1>();  // the previous piece's store is performed
+        finish(pend_p);
+      }
+      pend_p = p;
+    }
+  }
+  bulk_wait<0>();
+  if (ok && pend_p >= 0) finish(pend_p);
+}
+
+template <bool CP>
+__global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+                    const __grid_constant__ CUtensorMap tmV, AttnArgs a, const __grid_constant__ CpArgs cp) {
   extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SmemT<CP>& sm = *reinterpret_cast<SmemT<CP>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   const int qb = blockIdx.x % a.n_qblocks;
@@ -174,6 +308,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&sm.o_done[t], 1);
     }
     mbar_init(&sm.drain, 1);
+    if constexpr (CP) {
+      mbar_init(&sm.stage_full[0], 1);
+      mbar_init(&sm.stage_full[1], 1);
+      cp_build_order(sm, cp, a.Sk);
+    }
     fence_barrier_init();
   }
   if (warp == 8) {
@@ -185,7 +324,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tbase = sm.tmem_base;
 
-  if (warp == 9) {
+  if (CP && warp == 10) {
+    // ------------------------------------------------------------------ K/V gather (CP only)
+    if constexpr (CP) {
+      if (lane == 0) cp_gather(sm, cp);
+    }
+  } else if (warp == 9) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
@@ -197,16 +341,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tma_load_3d(sm.q[t] + c * CHUNK, &tmQ, &sm.q_full, h * HD + c * 64, q0 + t * TILE, b);
       bool ok = true;
       uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
+      uint32_t ready = 0;  // CP: peers whose rows are complete in the local buffer
       for (int j = 0; j < n_kv && ok; j++) {
         const int s = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
+        int kb = j;
+        if constexpr (CP) {
+          kb = sm.order[j];
+          const unsigned int npieces = (unsigned int)(cp.pieces_per_batch * cp.batches);
+          const int lo = kb * TILE / cp.shard_rows, hi = min(kb * TILE + TILE - 1, a.Sk - 1) / cp.shard_rows;
+          for (int q = lo; q <= hi && ok; q++) {
+            if (q == cp.rank || (ready >> q & 1u)) continue;
+            ok = cp_wait_done(cp.done + q, npieces);
+            ready |= 1u << q;
+          }
+          if (!ok) break;
+        }
         if (!mbar_wait(&sm.k_empty[s], ph ^ 1)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&sm.k_full[s], 2 * CHUNK);
         for (int c = 0; c < 2; c++)
-          tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, j * TILE, b);
+          tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, kb * TILE, b);
         kpend |= 1u << s;
         kph = (kph & ~(1u << s)) | (ph << s);
         if (!mbar_wait(&sm.v_empty[s], ph ^ 1)) {
@@ -215,7 +372,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         mbar_arrive_expect_tx(&sm.v_full[s], 2 * CHUNK);
         for (int c = 0; c < 2; c++)
-          tma_load_3d(sm.v[s] + c * CHUNK, &tmV, &sm.v_full[s], hk * HD + c * 64, j * TILE, b);
+          tma_load_3d(sm.v[s] + c * CHUNK, &tmV, &sm.v_full[s], hk * HD + c * 64, kb * TILE, b);
         vpend |= 1u << s;
         vph = (vph & ~(1u << s)) | (ph << s);
       }
@@ -337,7 +494,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(&sm.p_full[t]);
         continue;
       }
-      const int kbase = j * TILE;
+      int kbase = j * TILE;
+      if constexpr (CP) kbase = sm.order[j] * TILE;
       const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0 + t * TILE);
       // Single pass over the S row: all 128 columns in flight in one TMEM round trip,
       // 8-way tree max, exp2 in registers, P packed in place (pair i of chunk c -> word i),
@@ -517,16 +675,84 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
   a.n_qblocks = (p.Sq + 2 * TILE - 1) / (2 * TILE);
   a.diag = p.diag_mode;
   a.trace = reinterpret_cast<unsigned long long*>(p.trace);
-  const int smem = (int)sizeof(Smem) + 1024;
+  const int smem = (int)sizeof(SmemBase) + 1024;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   const long long grid = (long long)a.n_qblocks * p.Hq * p.B;
   if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-  attn_fwd_kernel<<<(int)grid, NTHREADS, smem, stream>>>(tq, tk, tv, a);
+  CpArgs none{};
+  attn_fwd_kernel<false><<<(int)grid, NTHREADS, smem, stream>>>(tq, tk, tv, a, none);
+  return cudaGetLastError();
+}
+
+cudaError_t attention_cp_fwd(const AttnProblem& p, const AttnCpProblem& c, cudaStream_t stream) {
+  if (p.B == 0 || p.Sq == 0) return cudaSuccess;
+  if (p.Hq % p.Hk || p.causal) return cudaErrorInvalidValue;
+  if (c.world < 1 || c.world > kCpMaxRanks || c.rank < 0 || c.rank >= c.world || c.shard_rows <= 0 ||
+      (long long)c.world * c.shard_rows != p.Sk || (p.Sk + TILE - 1) / TILE > CP_MAX_KV_BLOCKS ||
+      c.flags == nullptr || c.counters == nullptr)
+    return cudaErrorInvalidValue;
+  for (int r = 0; r < c.world; r++)
+    if (c.peer_kv[r] == nullptr || (r != c.rank && c.peer_acks[r] == nullptr)) return cudaErrorInvalidValue;
+  // K|V interleaved per token: row = [K (Hk*128) | V (Hk*128)] bf16, rows contiguous, batches contiguous
+  const long long row_el = 2LL * p.Hk * HD;
+  const uint8_t* base = static_cast<const uint8_t*>(c.peer_kv[c.rank]);
+  if (reinterpret_cast<uintptr_t>(base) & 255) return cudaErrorMisalignedAddress;
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap_3d(&tq, p.q, p.Hq, p.Sq, p.B, p.q_row, p.q_batch)) return cudaErrorInvalidValue;
+  if (!make_tmap_3d(&tk, base, p.Hk, p.Sk, p.B, row_el, row_el * p.Sk)) return cudaErrorInvalidValue;
+  if (!make_tmap_3d(&tv, base + p.Hk * HD * 2, p.Hk, p.Sk, p.B, row_el, row_el * p.Sk))
+    return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(p.o) & 15 || p.o_row % 8 || p.o_batch % 8) return cudaErrorMisalignedAddress;
+  AttnArgs a;
+  a.B = p.B;
+  a.Sq = p.Sq;
+  a.Sk = p.Sk;
+  a.Hq = p.Hq;
+  a.Hk = p.Hk;
+  a.o = p.o;
+  a.o_row = p.o_row;
+  a.o_batch = p.o_batch;
+  a.scale_log2 = p.scale * 1.4426950408889634f;
+  a.causal = 0;
+  a.n_qblocks = (p.Sq + 2 * TILE - 1) / (2 * TILE);
+  a.diag = p.diag_mode;
+  a.trace = reinterpret_cast<unsigned long long*>(p.trace);
+  CpArgs k{};
+  k.rank = c.rank;
+  k.world = c.world;
+  k.shard_rows = c.shard_rows;
+  k.row_bytes = row_el * 2;
+  k.batch_bytes = k.row_bytes * p.Sk;
+  k.shard_bytes = k.row_bytes * c.shard_rows;
+  for (int r = 0; r < c.world; r++) {
+    k.peer_kv[r] = static_cast<const uint8_t*>(c.peer_kv[r]);
+    k.peer_acks[r] = c.peer_acks[r];
+  }
+  k.local_kv = static_cast<uint8_t*>(c.peer_kv[c.rank]);
+  k.flags = c.flags;
+  k.flag_stride = c.flag_stride;
+  k.epoch = c.epoch;
+  k.claim = c.counters;
+  k.done = c.counters + c.world;
+  k.pieces_per_batch = (int)((k.shard_bytes + CP_PIECE - 1) / CP_PIECE);
+  k.batches = p.B;
+  cudaError_t e = cudaMemsetAsync(c.counters, 0, 2 * sizeof(unsigned int) * c.world, stream);
+  if (e != cudaSuccess) return e;
+  const int smem = (int)sizeof(SmemCP) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    e = cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const long long grid = (long long)a.n_qblocks * p.Hq * p.B;
+  if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+  attn_fwd_kernel<true><<<(int)grid, NTHREADS_CP, smem, stream>>>(tq, tk, tv, a, k);
   return cudaGetLastError();
 }
 

@@ -207,6 +207,51 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
   check_ok(ft::attention_fwd(p, at::cuda::getCurrentCUDAStream()), "attention_fwd");
 }
 
+// Context-parallel attention: q [B, Sq, Hq, 128] local queries, o like q; kv_local is this
+// rank's [B, Sk, 2, Hk, 128] K|V buffer (own rows written and published before the call).
+void attention_cp(const Tensor& q, const Tensor& kv_local, Tensor& o, double scale, std::vector<uint64_t> peer_kv,
+                  uint64_t flags, int64_t flag_stride, std::vector<uint64_t> peer_acks, int64_t rank,
+                  int64_t shard_rows, uint64_t epoch, Tensor& counters) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 4 && q.size(3) == 128 &&
+                  q.stride(3) == 1 && q.stride(2) == 128, "q: [B, S, H, 128] bf16 CUDA, heads packed");
+  TORCH_CHECK(o.sizes() == q.sizes() && o.stride(2) == 128 && o.stride(3) == 1, "o must match q");
+  TORCH_CHECK(kv_local.is_cuda() && kv_local.scalar_type() == at::kBFloat16 && kv_local.dim() == 5 &&
+                  kv_local.size(2) == 2 && kv_local.size(4) == 128 && kv_local.is_contiguous(),
+              "kv_local: contiguous [B, Sk, 2, Hk, 128] bf16");
+  const int world = (int)peer_kv.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kCpMaxRanks && (int)peer_acks.size() == world, "one kv/ack pointer per rank");
+  TORCH_CHECK(peer_kv[rank] == reinterpret_cast<uint64_t>(kv_local.data_ptr()), "peer_kv[rank] must be kv_local");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 2 * world,
+              "counters: int32 CUDA tensor with 2*world entries");
+  c10::cuda::CUDAGuard g(q.device());
+  ft::AttnProblem p;
+  p.B = q.size(0);
+  p.Sq = q.size(1);
+  p.Sk = kv_local.size(1);
+  p.Hq = q.size(2);
+  p.Hk = kv_local.size(3);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.q_row = q.stride(1);
+  p.o_row = o.stride(1);
+  p.q_batch = q.stride(0);
+  p.o_batch = o.stride(0);
+  p.scale = (float)scale;
+  ft::AttnCpProblem c;
+  c.rank = (int)rank;
+  c.world = world;
+  c.shard_rows = (int)shard_rows;
+  for (int r = 0; r < world; r++) {
+    c.peer_kv[r] = reinterpret_cast<void*>(peer_kv[r]);
+    c.peer_acks[r] = reinterpret_cast<uint64_t*>(peer_acks[r]);
+  }
+  c.flags = reinterpret_cast<const uint64_t*>(flags);
+  c.flag_stride = (int)flag_stride;
+  c.epoch = epoch;
+  c.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  check_ok(ft::attention_cp_fwd(p, c, at::cuda::getCurrentCUDAStream()), "attention_cp_fwd");
+}
+
 // Direct call of the striped gather with a caller-owned counter buffer (tests and tools).
 void p2p_gather_raw(std::vector<uint64_t> heaps, std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank,
                     int n_slots, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
@@ -318,6 +363,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("causal") = false, py::arg("diag_mode") = 0, py::arg("trace") = py::none());
   m.def("device_error", &device_error, py::arg("reset") = false);
   m.def("p2p_gather_raw", &p2p_gather_raw);
+  m.def("attention_cp", &attention_cp);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
   m.def("device_malloc", [](size_t n) { return reinterpret_cast<uintptr_t>(ft::device_malloc(n)); });

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <stdint.h>
 
 namespace ft {
 
@@ -21,5 +22,18 @@ struct AttnProblem {
 };
 
 cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream);
+
+// Context-parallel attention with the K/V all-gather fused in (see attention_sm100.cu).
+constexpr int kCpMaxRanks = 8;
+struct AttnCpProblem {
+  int rank = 0, world = 1, shard_rows = 0;   // Sk == world * shard_rows
+  void* peer_kv[kCpMaxRanks] = {};           // each rank's [B, Sk, 2, Hk*128] bf16 buffer (K|V per token)
+  const uint64_t* flags = nullptr;           // local: flags[q * flag_stride] = epoch rank q published
+  int flag_stride = 1;
+  uint64_t* peer_acks[kCpMaxRanks] = {};     // per peer p: the word that tells p we finished reading it
+  uint64_t epoch = 0;
+  unsigned int* counters = nullptr;          // 2 * world uint32 scratch, zeroed by the launcher
+};
+cudaError_t attention_cp_fwd(const AttnProblem& p, const AttnCpProblem& cp, cudaStream_t stream);
 
 }  // namespace ft
