@@ -132,7 +132,7 @@ class WanBlock(nn.Module):
         self.ffn_out = nn.Linear(cfg.ffn_dim, d)
 
     # ------------------------------------------------------------------ fused B200 path
-    def _forward_fused(self, x, ctx, e, rope, seq_len):
+    def _forward_fused(self, x, ctx, e, rope, seq_len, cp=None):
         from flextensor_b200 import ops
 
         cfg = self.cfg
@@ -146,11 +146,21 @@ class WanBlock(nn.Module):
         a1 = self.attn1
         h = ops.layernorm_modulate(x2, scale1, shift1, mod_rows=seq_len, eps=cfg.eps)
         q = ops.linear(h, a1.to_q.weight, a1.to_q.bias)
-        k = ops.linear(h, a1.to_k.weight, a1.to_k.bias)
-        v = ops.linear(h, a1.to_v.weight, a1.to_v.bias)
         ops.qk_rmsnorm_rope(q, a1.norm_q.weight, cos, sin, Dh, seq_len, eps=cfg.eps, out=q)
-        ops.qk_rmsnorm_rope(k, a1.norm_k.weight, cos, sin, Dh, seq_len, eps=cfg.eps, out=k)
-        o = ops.attention(q.view(B, seq_len, H, Dh), k.view(B, seq_len, H, Dh), v.view(B, seq_len, H, Dh))
+        if cp is not None:
+            # context parallel: K/V rows go straight into this rank's rows of the shared
+            # full-sequence buffer; the attention kernel gathers the other ranks' rows itself
+            k, v = cp.begin()
+            ops.linear(h, a1.to_k.weight, a1.to_k.bias, out=k)
+            ops.linear(h, a1.to_v.weight, a1.to_v.bias, out=v)
+            ops.qk_rmsnorm_rope(k, a1.norm_k.weight, cos, sin, Dh, seq_len, eps=cfg.eps, out=k)
+            cp.publish()
+            o = cp.attention(q.view(B, seq_len, H, Dh))
+        else:
+            k = ops.linear(h, a1.to_k.weight, a1.to_k.bias)
+            v = ops.linear(h, a1.to_v.weight, a1.to_v.bias)
+            ops.qk_rmsnorm_rope(k, a1.norm_k.weight, cos, sin, Dh, seq_len, eps=cfg.eps, out=k)
+            o = ops.attention(q.view(B, seq_len, H, Dh), k.view(B, seq_len, H, Dh), v.view(B, seq_len, H, Dh))
         ops.linear(o.view(-1, cfg.dim), a1.to_out.weight, a1.to_out.bias, epi="gate_res", residual=x2,
                    gate=gate1, gate_rows=seq_len, out=x2)
         # cross attention (LayerNorm with affine, no modulation)
@@ -173,7 +183,7 @@ class WanBlock(nn.Module):
         return x
 
     # ------------------------------------------------------------------ plain torch path
-    def _forward_torch(self, x, ctx, e, rope, seq_len):
+    def _forward_torch(self, x, ctx, e, rope, seq_len, cp=None):
         cfg = self.cfg
         B = x.shape[0]
         H, Dh = cfg.num_heads, cfg.head_dim
@@ -187,8 +197,12 @@ class WanBlock(nn.Module):
         v = F.linear(h, a1.to_v.weight, a1.to_v.bias)
         q = apply_rope_torch(q.view(B, seq_len, H, Dh).float(), cos, sin).to(x.dtype)
         k = apply_rope_torch(k.view(B, seq_len, H, Dh).float(), cos, sin).to(x.dtype)
-        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
-                                           v.view(B, seq_len, H, Dh).transpose(1, 2)).transpose(1, 2)
+        sdpa = lambda qq, kk, vv: F.scaled_dot_product_attention(  # noqa: E731
+            qq.transpose(1, 2), kk.transpose(1, 2), vv.transpose(1, 2)).transpose(1, 2)
+        if cp is not None:  # Ulysses all-to-all (NCCL baseline)
+            o = cp(q, k, v.view(B, seq_len, H, Dh), sdpa)
+        else:
+            o = sdpa(q, k, v.view(B, seq_len, H, Dh))
         y = F.linear(o.reshape(B, seq_len, cfg.dim), a1.to_out.weight, a1.to_out.bias)
         x = (x.float() + y.float() * gate1).to(x.dtype)
         a2 = self.attn2
@@ -205,11 +219,11 @@ class WanBlock(nn.Module):
         y = F.linear(f, self.ffn_out.weight, self.ffn_out.bias)
         return (x.float() + y.float() * gate3).to(x.dtype)
 
-    def forward(self, x, ctx, e, rope_cos, rope_sin):
+    def forward(self, x, ctx, e, rope_cos, rope_sin, cp=None):
         seq_len = x.shape[1]
         if self.impl == "fused":
-            return self._forward_fused(x, ctx, e, (rope_cos, rope_sin), seq_len)
-        return self._forward_torch(x, ctx, e, (rope_cos, rope_sin), seq_len)
+            return self._forward_fused(x, ctx, e, (rope_cos, rope_sin), seq_len, cp)
+        return self._forward_torch(x, ctx, e, (rope_cos, rope_sin), seq_len, cp)
 
 
 class WanDiT(nn.Module):
@@ -266,10 +280,23 @@ class WanDiT(nn.Module):
             self._rope_cache[key] = t
         return t
 
-    def forward(self, latent: torch.Tensor, timestep: torch.Tensor, context: torch.Tensor) -> torch.Tensor:
+    def forward(self, latent: torch.Tensor, timestep: torch.Tensor, context: torch.Tensor, cp=None) -> torch.Tensor:
+        """``cp``: a :class:`~flextensor_b200.parallel.cp.ContextParallel` (fused path) or
+        :class:`~flextensor_b200.parallel.cp.UlyssesAttention` (torch path); each rank then runs
+        the blocks on its 1/N of the tokens and the output is gathered after the head."""
         cfg = self.cfg
         dt = self.patch_embedding.weight.dtype
         x, grid = self.patchify(latent.to(dt))
+        rank_rows = None
+        if cp is not None:
+            import torch.distributed as dist
+
+            world = dist.get_world_size(cp.group)
+            shard = x.shape[1] // world
+            if shard * world != x.shape[1]:
+                raise ValueError(f"{x.shape[1]} tokens do not split evenly over {world} ranks")
+            rank_rows = slice(dist.get_rank(cp.group) * shard, (dist.get_rank(cp.group) + 1) * shard)
+            x = x[:, rank_rows].contiguous()
         x = self._lin(x, self.patch_embedding, "bias").contiguous()
         t = sinusoidal(timestep, cfg.freq_dim).to(dt)
         temb = self._lin(F.silu(self._lin(t, self.time_embedding_1).float()).to(dt), self.time_embedding_2)
@@ -277,13 +304,25 @@ class WanDiT(nn.Module):
         ctx = self._lin(context.to(dt), self.text_embedding_1, "gelu")
         ctx = self._lin(ctx, self.text_embedding_2).contiguous()
         cos, sin = self.rope(grid, x.device)
+        if rank_rows is not None:
+            cos, sin = cos[rank_rows].contiguous(), sin[rank_rows].contiguous()
         for blk in self.blocks:
-            x = blk(x, ctx, e, cos, sin)
+            x = blk(x, ctx, e, cos, sin, cp=cp) if cp is not None else blk(x, ctx, e, cos, sin)
         mod = self.head_scale_shift.float() + temb.float()[:, None]
         shift, scale = mod[:, 0:1], mod[:, 1:2]
         h = (F.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps) * (1 + scale) + shift).to(dt)
         y = self._lin(h, self.proj_out)
+        if cp is not None:
+            y = _gather_seq(y, cp.group)
         return self.unpatchify(y, grid)
+
+
+def _gather_seq(y: torch.Tensor, group) -> torch.Tensor:
+    import torch.distributed as dist
+
+    parts = [torch.empty_like(y) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, y.contiguous(), group=group)
+    return torch.cat(parts, dim=1)
 
 
 def init_wan_params_(model: nn.Module, seed: int = 0, std: float = 0.02) -> None:

@@ -102,3 +102,22 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float
     native.lib().attention(q, k, v, out, float(scale), bool(causal), int(_diag_mode), _trace)
     _count()
     return out
+
+
+def attention_cp(q: torch.Tensor, kv_local: torch.Tensor, *, peer_kv: list[int], flags_ptr: int, flag_stride: int,
+                 peer_acks: list[int], rank: int, shard_rows: int, epoch: int, counters: torch.Tensor,
+                 scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Context-parallel attention: local queries ``q [B, Sq, Hq, 128]`` over the keys of every
+    rank. ``kv_local [B, Sk, 2, Hk, 128]`` is this rank's full-sequence K|V buffer with its own
+    rows ``[rank*shard_rows, (rank+1)*shard_rows)`` written and published (epoch flag) before
+    the call; the kernel pulls the other ranks' rows from ``peer_kv`` over NVLink while it
+    computes (see ``attention_sm100.cu``)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    native.lib().attention_cp(q, kv_local, out, float(scale), [int(p) for p in peer_kv], int(flags_ptr),
+                              int(flag_stride), [int(p) for p in peer_acks], int(rank), int(shard_rows), int(epoch),
+                              counters)
+    _count()
+    return out

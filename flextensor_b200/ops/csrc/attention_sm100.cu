@@ -258,6 +258,7 @@ __device__ void cp_gather(SmemCP& sm, const CpArgs& c) {
       mbar_arrive_expect_tx(&sm.stage_full[st], n);
       bulk_load_g2s(sm.stage[st], c.peer_kv[p] + at, n, &sm.stage_full[st]);
       if (!mbar_wait(&sm.stage_full[st], ph[st])) {
+        spin_drain(&sm.stage_full[st], ph[st]);  // never leave the CTA with a load in flight
         ok = false;
         break;
       }

@@ -252,6 +252,37 @@ void attention_cp(const Tensor& q, const Tensor& kv_local, Tensor& o, double sca
   check_ok(ft::attention_cp_fwd(p, c, at::cuda::getCurrentCUDAStream()), "attention_cp_fwd");
 }
 
+// Epoch flags over peer memory (the CP and TP layers' signalling): publish stores `epoch` into
+// flags[p][rank*n_slots + slot] of every rank p; wait_acks waits (bounded, on the device) until
+// every peer's acks[rank][p*n_slots + slot] of this rank reached `epoch`.
+static ft::PeerTable flag_table(const std::vector<uint64_t>& flags, const std::vector<uint64_t>& acks, int rank,
+                                int n_slots) {
+  const int world = (int)flags.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kMaxRanks && acks.size() == flags.size(), "one flag/ack array per rank");
+  ft::PeerTable t;
+  for (int p = 0; p < world; p++) {
+    t.heap[p] = nullptr;
+    t.flags[p] = reinterpret_cast<uint64_t*>(flags[p]);
+    t.acks[p] = reinterpret_cast<uint64_t*>(acks[p]);
+  }
+  t.rank = rank;
+  t.world = world;
+  t.n_slots = n_slots;
+  return t;
+}
+
+void p2p_publish_raw(std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank, int n_slots, int slot,
+                     uint64_t epoch) {
+  auto t = flag_table(flags, acks, rank, n_slots);
+  check_ok(ft::p2p_publish(t, slot, epoch, at::cuda::getCurrentCUDAStream()), "p2p_publish");
+}
+
+void p2p_wait_acks_raw(std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank, int n_slots, int slot,
+                       uint64_t epoch) {
+  auto t = flag_table(flags, acks, rank, n_slots);
+  check_ok(ft::p2p_wait_acks(t, slot, epoch, at::cuda::getCurrentCUDAStream()), "p2p_wait_acks");
+}
+
 // Direct call of the striped gather with a caller-owned counter buffer (tests and tools).
 void p2p_gather_raw(std::vector<uint64_t> heaps, std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank,
                     int n_slots, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
@@ -364,6 +395,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("device_error", &device_error, py::arg("reset") = false);
   m.def("p2p_gather_raw", &p2p_gather_raw);
   m.def("attention_cp", &attention_cp);
+  m.def("p2p_publish_raw", &p2p_publish_raw);
+  m.def("p2p_wait_acks_raw", &p2p_wait_acks_raw);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
   m.def("device_malloc", [](size_t n) { return reinterpret_cast<uintptr_t>(ft::device_malloc(n)); });
