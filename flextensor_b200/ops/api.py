@@ -23,9 +23,9 @@ def launch_count() -> int:
     return _launches
 
 
-def _count() -> None:
+def _count(n: int = 1) -> None:
     global _launches
-    _launches += 1
+    _launches += n
 
 
 def _2d(t: torch.Tensor) -> torch.Tensor:
@@ -120,4 +120,40 @@ def attention_cp(q: torch.Tensor, kv_local: torch.Tensor, *, peer_kv: list[int],
                               int(flag_stride), [int(p) for p in peer_acks], int(rank), int(shard_rows), int(epoch),
                               counters)
     _count()
+    return out
+
+
+TP_EPI = {"none": 0, "bias": 1, "swiglu": 2}
+
+
+def tp_allgather_gemm(a_full: torch.Tensor, weight: torch.Tensor, *, peer_a: list[int], flags_ptr: int,
+                      flag_stride: int, peer_acks: list[int], rank: int, epoch: int, counters: torch.Tensor,
+                      bias: torch.Tensor | None = None, epi: str = "none", out: torch.Tensor | None = None):
+    """All-gather -> GEMM: ``a_full [M, K]`` is this rank's full-row buffer with its own rows
+    written and published; the kernel pulls peers' rows over NVLink while multiplying.
+    ``epi="swiglu"``: weight rows interleaved (gate, up) -> ``[M, N/2]``."""
+    n_out = weight.shape[0] // 2 if epi == "swiglu" else weight.shape[0]
+    if out is None:
+        out = torch.empty(a_full.shape[0], n_out, dtype=torch.bfloat16, device=a_full.device)
+    native.lib().tp_ag_gemm(a_full, weight, out, bias, TP_EPI[epi], [int(p) for p in peer_a], int(flags_ptr),
+                            int(flag_stride), [int(p) for p in peer_acks], int(rank), int(epoch), counters)
+    _count()
+    return out
+
+
+def tp_gemm_reducescatter(a: torch.Tensor, weight: torch.Tensor, *, stage: list[int], peer_flags: list[int],
+                          rank: int, epoch: int, counters: torch.Tensor) -> None:
+    """GEMM -> reduce-scatter, sender side: partial ``a @ weight.T`` rows go straight into the
+    owning rank's staging slot ``[world, M/world, N]`` (``stage[p]``); then flags."""
+    native.lib().tp_gemm_rs(a, weight, [int(p) for p in stage], [int(p) for p in peer_flags], int(rank), int(epoch),
+                            counters)
+    _count()
+
+
+def tp_reduce(stage: torch.Tensor, world: int, rows: int, out: torch.Tensor, *, flags_ptr: int, flag_stride: int,
+              epoch: int, peer_acks: list[int], rank: int, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Owner side: ``out = residual + sum of the world partial rows`` once every sender flagged."""
+    native.lib().tp_reduce(stage, int(world), int(rows), out, residual, int(flags_ptr), int(flag_stride), int(epoch),
+                           [int(p) for p in peer_acks], int(rank))
+    _count(2)
     return out

@@ -23,6 +23,7 @@ SOURCES = [
     "norm.cu",
     "attention_sm100.cu",
     "p2p.cu",
+    "tp_sm100.cu",
 ]
 
 CUDA_FLAGS = [

@@ -12,6 +12,7 @@
 #include "ft_ops.h"
 #include "ft_ops_norm.h"
 #include "ft_runtime.h"
+#include "ft_tp.h"
 
 namespace {
 
@@ -283,6 +284,98 @@ void p2p_wait_acks_raw(std::vector<uint64_t> flags, std::vector<uint64_t> acks, 
   check_ok(ft::p2p_wait_acks(t, slot, epoch, at::cuda::getCurrentCUDAStream()), "p2p_wait_acks");
 }
 
+// Tensor-parallel fused GEMMs. a_full: this rank's [M, K] buffer (own rows written + published);
+// w: [N, K] shard; out: [M, N] (or [M, N/2] with SwiGLU). Pointers of peers come as integers.
+void tp_ag_gemm(const Tensor& a_full, const Tensor& w, Tensor& out, const c10::optional<Tensor>& bias, int64_t epi,
+                std::vector<uint64_t> peer_a, uint64_t flags, int64_t flag_stride, std::vector<uint64_t> peer_acks,
+                int64_t rank, uint64_t epoch, Tensor& counters) {
+  TORCH_CHECK(a_full.is_cuda() && a_full.scalar_type() == at::kBFloat16 && a_full.dim() == 2 && a_full.is_contiguous(),
+              "a_full: contiguous [M, K] bf16");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.stride(1) == 1, "w: [N, K] bf16");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "out: 2-D bf16");
+  const int world = (int)peer_a.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kTpMaxRanks && (int)peer_acks.size() == world, "one pointer per rank");
+  TORCH_CHECK(peer_a[rank] == reinterpret_cast<uint64_t>(a_full.data_ptr()), "peer_a[rank] must be a_full");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 2 * world, "counters");
+  c10::cuda::CUDAGuard g(a_full.device());
+  ft::TpGemmProblem p;
+  p.M = a_full.size(0);
+  p.K = a_full.size(1);
+  p.N = w.size(0);
+  p.rank = (int)rank;
+  p.world = world;
+  p.W = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.ldw = w.stride(0);
+  if (bias && bias->defined()) p.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  p.epi = (int)epi;
+  TORCH_CHECK(out.size(0) == p.M && out.size(1) == (p.epi == ft::TP_EPI_SWIGLU ? p.N / 2 : p.N), "out shape");
+  for (int r = 0; r < world; r++) {
+    p.peer_a[r] = reinterpret_cast<const void*>(peer_a[r]);
+    p.peer_acks[r] = reinterpret_cast<uint64_t*>(peer_acks[r]);
+  }
+  p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldc = out.stride(0);
+  p.flags = reinterpret_cast<const uint64_t*>(flags);
+  p.flag_stride = (int)flag_stride;
+  p.epoch = epoch;
+  p.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  p.num_sms = num_sms_for(a_full.get_device());
+  check_ok(ft::tp_allgather_gemm(p, at::cuda::getCurrentCUDAStream()), "tp_allgather_gemm");
+}
+
+void tp_gemm_rs(const Tensor& a, const Tensor& w, std::vector<uint64_t> stage, std::vector<uint64_t> peer_flags,
+                int64_t rank, uint64_t epoch, Tensor& counters) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.dim() == 2 && a.stride(1) == 1, "a: [M, K] bf16");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.stride(1) == 1, "w: [N, K] bf16");
+  const int world = (int)stage.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kTpMaxRanks && (int)peer_flags.size() == world, "one pointer per rank");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 1, "counters");
+  c10::cuda::CUDAGuard g(a.device());
+  ft::TpGemmProblem p;
+  p.M = a.size(0);
+  p.K = a.size(1);
+  p.N = w.size(0);
+  p.rank = (int)rank;
+  p.world = world;
+  p.A = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+  p.lda = a.stride(0);
+  p.W = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.ldw = w.stride(0);
+  for (int r = 0; r < world; r++) {
+    p.stage[r] = reinterpret_cast<void*>(stage[r]);
+    p.peer_flags[r] = reinterpret_cast<uint64_t*>(peer_flags[r]);
+  }
+  p.epoch = epoch;
+  p.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  p.num_sms = num_sms_for(a.get_device());
+  check_ok(ft::tp_gemm_reducescatter(p, at::cuda::getCurrentCUDAStream()), "tp_gemm_reducescatter");
+}
+
+void tp_reduce(const Tensor& stage, int64_t world, int64_t rows, Tensor& out, const c10::optional<Tensor>& residual,
+               uint64_t flags, int64_t flag_stride, uint64_t epoch, std::vector<uint64_t> peer_acks, int64_t rank) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "out");
+  c10::cuda::CUDAGuard g(out.device());
+  ft::TpReduceProblem r;
+  r.rank = (int)rank;
+  r.world = (int)world;
+  r.rows = (int)rows;
+  r.N = out.size(1);
+  r.stage = stage.data_ptr();
+  if (residual && residual->defined()) {
+    TORCH_CHECK(residual->stride(1) == 1 && residual->sizes() == out.sizes(), "residual like out");
+    r.residual = residual->data_ptr();
+    r.ldr = residual->stride(0);
+  }
+  r.out = out.data_ptr();
+  r.ldo = out.stride(0);
+  r.flags = reinterpret_cast<const uint64_t*>(flags);
+  r.flag_stride = (int)flag_stride;
+  r.epoch = epoch;
+  TORCH_CHECK((int)peer_acks.size() == r.world, "one ack pointer per rank");
+  for (int q = 0; q < r.world; q++) r.peer_acks[q] = reinterpret_cast<uint64_t*>(peer_acks[q]);
+  check_ok(ft::tp_reduce(r, at::cuda::getCurrentCUDAStream()), "tp_reduce");
+}
+
 // Direct call of the striped gather with a caller-owned counter buffer (tests and tools).
 void p2p_gather_raw(std::vector<uint64_t> heaps, std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank,
                     int n_slots, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
@@ -313,7 +406,8 @@ int device_error(bool reset) {
   int n = ft::norm_device_error(reset);
   int a = ft::attn_device_error(reset);
   int p = ft::p2p_device_error(reset);
-  return e ? e : (n ? n : (a ? a : p));
+  int t = ft::tp_device_error(reset);
+  return e ? e : (n ? n : (a ? a : (p ? p : t)));
 }
 
 struct PyEngine {
@@ -396,6 +490,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_gather_raw", &p2p_gather_raw);
   m.def("attention_cp", &attention_cp);
   m.def("p2p_publish_raw", &p2p_publish_raw);
+  m.def("tp_ag_gemm", &tp_ag_gemm);
+  m.def("tp_gemm_rs", &tp_gemm_rs);
+  m.def("tp_reduce", &tp_reduce);
   m.def("p2p_wait_acks_raw", &p2p_wait_acks_raw);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });

@@ -1,0 +1,59 @@
+// Tensor-parallel fused collective GEMMs (tp_sm100.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ft {
+
+constexpr int kTpMaxRanks = 8;
+
+enum TpEpilogue : int {
+  TP_EPI_NONE = 0,
+  TP_EPI_BIAS = 1,
+  TP_EPI_SWIGLU = 2,  // weight rows interleaved (gate_j, up_j): C[:, j] = silu(g_j) * u_j, N/2 outputs
+};
+
+struct TpGemmProblem {
+  int M = 0, N = 0, K = 0;     // M = all rows (world * rows per rank)
+  int rank = 0, world = 1;
+  const __nv_bfloat16* A = nullptr;  // reduce-scatter: local [M, K] input (lda)
+  int lda = 0;
+  const __nv_bfloat16* W = nullptr;  // [N, K] weight shard (ldw)
+  int ldw = 0;
+  const __nv_bfloat16* bias = nullptr;
+  int epi = TP_EPI_NONE;
+  // all-gather -> GEMM
+  const void* peer_a[kTpMaxRanks] = {};  // each rank's full [M, K] A buffer (own rows written + published)
+  __nv_bfloat16* C = nullptr;            // local output [M, N or N/2] (ldc)
+  int ldc = 0;
+  const uint64_t* flags = nullptr;       // local flags[q * flag_stride] = epoch rank q published
+  int flag_stride = 1;
+  uint64_t* peer_acks[kTpMaxRanks] = {}; // word telling rank p we finished reading its rows
+  // GEMM -> reduce-scatter
+  void* stage[kTpMaxRanks] = {};         // rank p's staging [world][M/world][N] for this slot
+  uint64_t* peer_flags[kTpMaxRanks] = {};// word telling rank p our partial rows are complete
+  uint64_t epoch = 0;
+  unsigned int* counters = nullptr;      // scratch: 2*world (all-gather) / 1 (reduce-scatter), zeroed here
+  int num_sms = 0;
+};
+
+struct TpReduceProblem {
+  int rank = 0, world = 1, rows = 0, N = 0;
+  const void* stage = nullptr;           // local [world][rows][N]
+  const void* residual = nullptr;        // optional [rows, N] (ldr)
+  int ldr = 0;
+  void* out = nullptr;                   // [rows, N] (ldo); may alias residual
+  int ldo = 0;
+  const uint64_t* flags = nullptr;       // local flags[q * flag_stride]
+  int flag_stride = 1;
+  uint64_t epoch = 0;
+  uint64_t* peer_acks[kTpMaxRanks] = {}; // word telling rank q its slot in our staging is free
+};
+
+cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream);
+cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream);
+cudaError_t tp_reduce(const TpReduceProblem& r, cudaStream_t stream);
+int tp_device_error(bool reset);
+
+}  // namespace ft

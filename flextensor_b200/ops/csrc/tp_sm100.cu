@@ -1,0 +1,591 @@
+// Tensor-parallel GEMMs with the collective fused in (sm_100a, NVLink peer memory).
+//
+// Both kernels are the persistent warp-specialised tcgen05 GEMM of gemm_sm100.cu (TMA ring of
+// A 128x64 and W BNx64 tiles, one elected MMA thread, double-buffered TMEM accumulator, four
+// epilogue warps reading TMEM), with the collective built into the data path:
+//
+// all-gather -> GEMM (column-parallel layer, sequence-parallel input):
+//   A is the full [M, K] activation; each rank owns rows [rank*R, (rank+1)*R) of it (R = M /
+//   world) in its own copy of the buffer (symmetric heap) and has published an epoch flag.
+//   Warp 6 of every CTA pulls peers' rows into the local copy (12 KB bulk copies peer -> smem
+//   -> HBM, pieces claimed from a per-peer ticket counter, so any running CTA can finish a
+//   peer's rows and nothing waits on a CTA that is not resident) and acknowledges each peer
+//   when its rows are local. M tiles are walked starting at this rank's own rows; before the
+//   first load of an A tile the producer waits until every rank owning rows of the tile is
+//   complete locally. Epilogue: bias, or SwiGLU over interleaved (gate, up) weight rows.
+//
+// GEMM -> reduce-scatter (row-parallel layer): every rank computes its partial product of all
+//   M rows; the epilogue stores each output row straight into the staging buffer of the rank
+//   that owns the row (slot [source rank] of that rank's [world, R, N] staging area, plain
+//   16-byte stores over NVLink). M tiles start with the next rank's rows so remote traffic
+//   begins early and the own rows come last. After its last tile each CTA fences; the last
+//   CTA stores the epoch into every owner's flag. The owner's reduce kernel (tp_reduce) waits
+//   for all flags, sums the world partials (+ residual) in fp32 and acknowledges the senders.
+//
+// Every wait is bounded (device error word on timeout); no TMA multicast anywhere.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "ft_ops.h"
+#include "ft_tp.h"
+#include "sm100_common.cuh"
+
+namespace ft {
+
+FT_DEFINE_ERROR_READER(tp_device_error)
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int GROUP_M = 8;
+constexpr int TP_PIECE = 12288;
+constexpr int NTHREADS = 224;  // warp 0 TMA, 1 MMA, 2-5 epilogue, 6 gather (AG) / idle (RS)
+
+struct TpArgs {
+  int M, N, K;
+  int num_m_tiles, num_n_tiles, num_tiles, m_rot;
+  int epi;  // TP_EPI_NONE / TP_EPI_BIAS / TP_EPI_SWIGLU
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* C;
+  int ldc;
+  int rank, world, rows;
+  // all-gather side
+  const uint8_t* peer_a[kTpMaxRanks];
+  uint8_t* local_a;
+  long long row_bytes;
+  const uint64_t* flags;
+  int flag_stride;
+  uint64_t* peer_acks[kTpMaxRanks];
+  uint64_t epoch;
+  unsigned int* claim;
+  unsigned int* done;
+  int pieces;  // per rank
+  // reduce-scatter side
+  __nv_bfloat16* stage[kTpMaxRanks];  // rank p's staging base for this slot: [world][rows][N]
+  uint64_t* peer_flags[kTpMaxRanks];  // where rank p learns our partial rows are complete
+  unsigned int* cta_done;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int RING = STAGES * (A_BYTES + B_BYTES);
+  static constexpr int SMEM = 1024 + RING + 2 * TP_PIECE + 512;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const TpArgs& p, int& mt, int& nt) {
+  const int per_group = GROUP_M * p.num_n_tiles;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int first = g * GROUP_M;
+  const int gsz = min(GROUP_M, p.num_m_tiles - first);
+  mt = (first + r % gsz + p.m_rot) % p.num_m_tiles;
+  nt = r / gsz;
+}
+
+__device__ bool wait_u64(const uint64_t* f, uint64_t target) {
+  const long long t0 = clock64();
+  while (ld_acquire_sys_u64(f) < target) {
+    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
+      record_error(kErrPeerTimeout);
+      return false;
+    }
+    if (error_raised()) return false;
+    __nanosleep(128);
+  }
+  return true;
+}
+
+__device__ bool wait_done(const unsigned int* d, unsigned int target) {
+  const long long t0 = clock64();
+  while (ld_acquire_gpu_u32(d) < target) {
+    if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
+      record_error(kErrWaitTimeout);
+      return false;
+    }
+    if (error_raised()) return false;
+    __nanosleep(64);
+  }
+  fence_proxy_async_global();
+  return true;
+}
+
+// One lane of warp 6: pull peers' A rows into the local copy (see the file comment).
+__device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_full) {
+  const unsigned int npieces = (unsigned int)c.pieces;
+  const long long rank_bytes = c.row_bytes * c.rows;
+  uint32_t ph[2] = {0, 0};
+  int issued = 0, pend_p = -1;
+  bool ok = true;
+  auto finish = [&](int p) {
+    fence_proxy_async_global();
+    const unsigned int old = atom_add_release_gpu_u32(c.done + p, 1u);
+    if (old + 1 == npieces) {
+      __threadfence_system();
+      st_release_sys_u64(c.peer_acks[p], c.epoch);
+    }
+  };
+  for (int d = 1; d < c.world && ok; d++) {
+    const int p = (c.rank + d) % c.world;
+    bool flagged = false;
+    for (;;) {
+      const unsigned int idx = atomicAdd(c.claim + p, 1u);
+      if (idx >= npieces) break;
+      if (!flagged) {
+        if (!wait_u64(c.flags + (size_t)p * c.flag_stride, c.epoch)) {
+          ok = false;
+          break;
+        }
+        flagged = true;
+      }
+      const long long off = (long long)idx * TP_PIECE;
+      const uint32_t n = (uint32_t)min((long long)TP_PIECE, rank_bytes - off);
+      const long long at = (long long)p * rank_bytes + off;
+      const int st = issued & 1;
+      uint8_t* buf = stage + st * TP_PIECE;
+      mbar_arrive_expect_tx(&stage_full[st], n);
+      bulk_load_g2s(buf, c.peer_a[p] + at, n, &stage_full[st]);
+      if (!mbar_wait(&stage_full[st], ph[st])) {
+        const long long t0 = clock64();  // never leave with a load in flight
+        while (!mbar_try_wait(smem_u32(&stage_full[st]), ph[st]) &&
+               (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+        }
+        ok = false;
+        break;
+      }
+      ph[st] ^= 1;
+      bulk_store_s2g(c.local_a + at, buf, n);
+      bulk_commit();
+      issued++;
+      if (pend_p >= 0) {
+        bulk_wait<1>();
+        finish(pend_p);
+      }
+      pend_p = p;
+    }
+  }
+  bulk_wait<0>();
+  if (ok && pend_p >= 0) finish(pend_p);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+// 32 accumulator columns of one row -> bias / SwiGLU -> bf16 store to dst (a row pointer
+// already offset to the tile's first output column).
+__device__ __forceinline__ void epi_row32(const TpArgs& p, float (&v)[32], int col0, __nv_bfloat16* dst,
+                                          int n_out) {
+  if (p.epi == TP_EPI_BIAS && p.bias != nullptr) {
+#pragma unroll
+    for (int e = 0; e < 32; e++) v[e] += (col0 + e < p.N) ? __bfloat162float(p.bias[col0 + e]) : 0.f;
+  }
+  if (p.epi == TP_EPI_SWIGLU) {  // columns (2j, 2j+1) = (gate_j, up_j) -> 16 outputs
+    const int o0 = col0 / 2;
+    if (o0 + 16 <= n_out) {
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        uint4 u;
+        u.x = pack_bf16x2(silu(v[j * 16 + 0]) * v[j * 16 + 1], silu(v[j * 16 + 2]) * v[j * 16 + 3]);
+        u.y = pack_bf16x2(silu(v[j * 16 + 4]) * v[j * 16 + 5], silu(v[j * 16 + 6]) * v[j * 16 + 7]);
+        u.z = pack_bf16x2(silu(v[j * 16 + 8]) * v[j * 16 + 9], silu(v[j * 16 + 10]) * v[j * 16 + 11]);
+        u.w = pack_bf16x2(silu(v[j * 16 + 12]) * v[j * 16 + 13], silu(v[j * 16 + 14]) * v[j * 16 + 15]);
+        *reinterpret_cast<uint4*>(dst + j * 8) = u;
+      }
+    } else {
+      for (int j = 0; j < 16; j++)
+        if (o0 + j < n_out) dst[j] = __float2bfloat16(silu(v[2 * j]) * v[2 * j + 1]);
+    }
+    return;
+  }
+  if (col0 + 32 <= n_out) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint4 u;
+      u.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
+      u.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
+      u.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
+      u.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
+      *reinterpret_cast<uint4*>(dst + j * 8) = u;
+    }
+  } else {
+    for (int e = 0; e < 32; e++)
+      if (col0 + e < n_out) dst[e] = __float2bfloat16(v[e]);
+  }
+}
+
+template <int BN, bool AG>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tp_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ TpArgs p) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint8_t* stage = smem + C::RING;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage + 2 * TP_PIECE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* stage_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stage_full + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+      mbar_init(&stage_full[b], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 6) {
+    if constexpr (AG) {
+      if (lane == 0) gather_rows(p, stage, stage_full);
+    }
+  } else if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      uint32_t pend = 0, pend_ph = 0;
+      uint32_t ready = 0;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        int mt, nt;
+        tile_coords(tile, p, mt, nt);
+        if constexpr (AG) {
+          const int lo = mt * BM / p.rows, hi = min(mt * BM + BM - 1, p.M - 1) / p.rows;
+          for (int q = lo; q <= hi && ok; q++) {
+            if (q == p.rank || (ready >> q & 1u)) continue;
+            ok = wait_done(p.done + q, (unsigned int)p.pieces);
+            ready |= 1u << q;
+          }
+          if (!ok) break;
+        }
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&empty[s], ph ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+          tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, mt * BM);
+          tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, nt * BN);
+          pend |= 1u << s;
+          pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        for (int st = 0; st < STAGES; st++) {
+          if (!(pend >> st & 1)) continue;
+          const long long t0 = clock64();
+          while (!mbar_try_wait(smem_u32(&full[st]), (pend_ph >> st) & 1) &&
+                 (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * C::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            umma_bf16_ss(d, umma_desc_kmajor_sw128(a0 + k * 32), umma_desc_kmajor_sw128(b0 + k * 32), idesc,
+                         (kb | k) != 0);
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+      if (!ok) {
+        umma_commit(drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(smem_u32(drain), 0) &&
+               (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    const int n_out = p.epi == TP_EPI_SWIGLU ? p.N / 2 : p.N;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      int mt, nt;
+      tile_coords(tile, p, mt, nt);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph))) break;
+      tc_fence_after();
+      const int row = mt * BM + q * 32 + lane;
+      __nv_bfloat16* rowp = nullptr;
+      if (row < p.M) {
+        if constexpr (AG) {
+          rowp = p.C + (size_t)row * p.ldc;
+        } else {
+          const int owner = row / p.rows;
+          rowp = p.stage[owner] + ((size_t)p.rank * p.rows + (row - owner * p.rows)) * p.N;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nt * BN + c * 32;
+        if (rowp != nullptr && col0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; e++) v[e] = __uint_as_float(r[e]);
+          epi_row32(p, v, col0, rowp + (p.epi == TP_EPI_SWIGLU ? col0 / 2 : col0), n_out);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+    }
+    if constexpr (!AG) __threadfence_system();  // this thread's peer stores before the completion flag
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (!AG) {
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const unsigned int old = atomicAdd(p.cta_done, 1u);
+      if (old == gridDim.x - 1) {  // last CTA: every partial row of every CTA is stored
+        __threadfence_system();
+        for (int r = 0; r < p.world; r++) st_release_sys_u64(p.peer_flags[r], p.epoch);
+      }
+    }
+  }
+}
+
+// Owner side of the reduce-scatter: out[r] = (residual[r] +) sum_src stage[src][r], fp32 sum.
+__global__ void __launch_bounds__(256)
+    tp_reduce_kernel(const __nv_bfloat16* stage, int world, int rows, int N, const __nv_bfloat16* residual,
+                     int ldr, __nv_bfloat16* out, int ldo, const uint64_t* flags, int flag_stride, uint64_t epoch) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int q = 0; q < world && ok; q++)
+      if (!wait_u64(flags + (size_t)q * flag_stride, epoch)) ok = 0;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int vec = N / 8;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)rows * vec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / vec), c = (int)(i % vec) * 8;
+    float acc[8];
+    if (residual != nullptr) {
+      const uint4 u = *reinterpret_cast<const uint4*>(residual + (size_t)r * ldr + c);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = __bfloat162float(b[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = 0.f;
+    }
+    for (int s = 0; s < world; s++) {
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(stage + ((size_t)s * rows + r) * N + c));
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] += __bfloat162float(b[e]);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + (size_t)r * ldo + c) = o;
+  }
+}
+
+struct AckList {
+  uint64_t* ptr[kTpMaxRanks];
+  int n;
+  uint64_t epoch;
+};
+
+// Runs after tp_reduce_kernel in stream order: every staged row has been read, so each sender
+// may reuse its slot in this rank's staging area.
+__global__ void tp_ack_kernel(AckList a) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int i = 0; i < a.n; i++)
+      if (a.ptr[i] != nullptr) st_release_sys_u64(a.ptr[i], a.epoch);
+  }
+}
+
+template <int BN, bool AG>
+cudaError_t launch(const TpArgs& a, const CUtensorMap& tA, const CUtensorMap& tB, int num_sms, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(tp_gemm_kernel<BN, AG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<BN>::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
+  tp_gemm_kernel<BN, AG><<<grid, NTHREADS, Cfg<BN>::SMEM, s>>>(tA, tB, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+static cudaError_t fill_common(const TpGemmProblem& g, TpArgs& a, int bn) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaErrorInvalidValue;
+  if (g.K % 8 || g.N % 32 || g.world < 1 || g.world > kTpMaxRanks || g.rank < 0 || g.rank >= g.world)
+    return cudaErrorInvalidValue;
+  if (g.M % g.world) return cudaErrorInvalidValue;
+  a.M = g.M;
+  a.N = g.N;
+  a.K = g.K;
+  a.num_m_tiles = (g.M + BM - 1) / BM;
+  a.num_n_tiles = (g.N + bn - 1) / bn;
+  a.num_tiles = a.num_m_tiles * a.num_n_tiles;
+  a.epi = g.epi;
+  a.bias = g.bias;
+  a.rank = g.rank;
+  a.world = g.world;
+  a.rows = g.M / g.world;
+  a.epoch = g.epoch;
+  a.flags = g.flags;
+  a.flag_stride = g.flag_stride;
+  for (int r = 0; r < g.world; r++) a.peer_acks[r] = g.peer_acks[r];
+  return cudaSuccess;
+}
+
+cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream) {
+  TpArgs a{};
+  const int bn = g.N >= 256 ? 256 : 128;
+  cudaError_t e = fill_common(g, a, bn);
+  if (e != cudaSuccess) return e;
+  if (g.counters == nullptr || g.C == nullptr || g.flags == nullptr) return cudaErrorInvalidValue;
+  if (g.epi == TP_EPI_SWIGLU && g.N % 64) return cudaErrorInvalidValue;
+  const uint8_t* local = static_cast<const uint8_t*>(g.peer_a[g.rank]);
+  a.row_bytes = (long long)g.K * 2;
+  for (int r = 0; r < g.world; r++) {
+    if (g.peer_a[r] == nullptr || (r != g.rank && g.peer_acks[r] == nullptr)) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(g.peer_a[r]) & 15) return cudaErrorMisalignedAddress;
+    a.peer_a[r] = static_cast<const uint8_t*>(g.peer_a[r]);
+  }
+  if ((a.row_bytes * a.rows) % 16) return cudaErrorInvalidValue;
+  a.local_a = const_cast<uint8_t*>(local);
+  a.C = g.C;
+  a.ldc = g.ldc;
+  a.claim = g.counters;
+  a.done = g.counters + g.world;
+  a.pieces = (int)((a.row_bytes * a.rows + TP_PIECE - 1) / TP_PIECE);
+  a.m_rot = (g.rank * a.rows) / BM;
+  e = cudaMemsetAsync(g.counters, 0, 2 * sizeof(unsigned int) * g.world, stream);
+  if (e != cudaSuccess) return e;
+  CUtensorMap tA, tB;
+  if (!make_tmap_2d_bf16(&tA, local, g.K, g.M, g.K, BK, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tB, g.W, g.K, g.N, g.ldw, BK, bn)) return cudaErrorInvalidValue;
+  const int sms = g.num_sms > 0 ? g.num_sms : 148;
+  return bn == 256 ? launch<256, true>(a, tA, tB, sms, stream) : launch<128, true>(a, tA, tB, sms, stream);
+}
+
+cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream) {
+  TpArgs a{};
+  const int bn = g.N >= 256 ? 256 : 128;
+  cudaError_t e = fill_common(g, a, bn);
+  if (e != cudaSuccess) return e;
+  if (g.counters == nullptr || g.epi == TP_EPI_SWIGLU) return cudaErrorInvalidValue;
+  for (int r = 0; r < g.world; r++) {
+    if (g.stage[r] == nullptr || g.peer_flags[r] == nullptr) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(g.stage[r]) & 15) return cudaErrorMisalignedAddress;
+    a.stage[r] = static_cast<__nv_bfloat16*>(g.stage[r]);
+    a.peer_flags[r] = g.peer_flags[r];
+  }
+  a.cta_done = g.counters;
+  a.m_rot = (((g.rank + 1) % g.world) * a.rows) / BM;
+  e = cudaMemsetAsync(g.counters, 0, sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return e;
+  CUtensorMap tA, tB;
+  if (!make_tmap_2d_bf16(&tA, g.A, g.K, g.M, g.lda, BK, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tB, g.W, g.K, g.N, g.ldw, BK, bn)) return cudaErrorInvalidValue;
+  const int sms = g.num_sms > 0 ? g.num_sms : 148;
+  return bn == 256 ? launch<256, false>(a, tA, tB, sms, stream) : launch<128, false>(a, tA, tB, sms, stream);
+}
+
+cudaError_t tp_reduce(const TpReduceProblem& r, cudaStream_t stream) {
+  if (r.world < 1 || r.world > kTpMaxRanks || r.N % 8 || r.rows <= 0 || r.stage == nullptr || r.out == nullptr ||
+      r.flags == nullptr)
+    return cudaErrorInvalidValue;
+  const long long work = (long long)r.rows * (r.N / 8);
+  int grid = (int)((work + 255) / 256);
+  if (grid > 4 * 148) grid = 4 * 148;
+  if (grid < 1) grid = 1;
+  tp_reduce_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(r.stage), r.world, r.rows, r.N,
+                                             static_cast<const __nv_bfloat16*>(r.residual), r.ldr,
+                                             static_cast<__nv_bfloat16*>(r.out), r.ldo, r.flags, r.flag_stride,
+                                             r.epoch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  AckList a{};
+  a.n = r.world;
+  a.epoch = r.epoch;
+  for (int q = 0; q < r.world; q++) a.ptr[q] = q == r.rank ? nullptr : r.peer_acks[q];
+  tp_ack_kernel<<<1, 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace ft

@@ -1,0 +1,92 @@
+"""Tensor-parallel fused GEMMs, ranks emulated on one GPU (every rank's buffers are separate
+allocations; flags are set before the launches that read them, so no kernel waits on another
+launch): all-gather -> GEMM (bias / SwiGLU) and GEMM -> reduce-scatter -> reduce, against fp32
+references."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from flextensor_b200.ops import api as ops  # noqa: E402
+from flextensor_b200.ops import native  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6))
+
+
+@pytest.mark.parametrize("W,R,K,N,epi,rank", [(4, 200, 256, 384, "bias", 1), (2, 256, 512, 1024, "swiglu", 0),
+                                              (8, 96, 128, 256, "none", 7), (3, 333, 192, 512, "swiglu", 2)])
+def test_allgather_gemm(W, R, K, N, epi, rank):
+    M = W * R
+    g = torch.Generator(device=DEV).manual_seed(W * 10 + rank)
+    a = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    bias = torch.randn(N, device=DEV, generator=g).bfloat16() if epi == "bias" else None
+    bufs = []
+    for p in range(W):
+        b = torch.zeros(M, K, device=DEV, dtype=torch.bfloat16)
+        b[p * R:(p + 1) * R] = a[p * R:(p + 1) * R]
+        bufs.append(b)
+    flags = torch.zeros(W, dtype=torch.int64, device=DEV)
+    acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    counters = torch.zeros(2 * W, dtype=torch.int32, device=DEV)
+    for epoch in (1, 2):
+        flags.fill_(epoch)
+        out = ops.tp_allgather_gemm(bufs[rank], w, peer_a=[b.data_ptr() for b in bufs], flags_ptr=flags.data_ptr(),
+                                    flag_stride=1, peer_acks=[x.data_ptr() + 8 * rank for x in acks], rank=rank,
+                                    epoch=epoch, counters=counters, bias=bias, epi=epi)
+        torch.cuda.synchronize()
+        assert native.device_error(reset=True) == 0
+        ref = a.float() @ w.float().t()
+        if bias is not None:
+            ref = ref + bias.float()
+        if epi == "swiglu":
+            ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+        assert _rel(out, ref) < 2e-2
+        assert torch.equal(bufs[rank], a), "rows not gathered"
+        for p in range(W):
+            if p != rank:
+                assert int(acks[p][rank]) == epoch
+        for p in range(W):  # next epoch: clear the gathered rows again
+            if p != rank:
+                bufs[rank][p * R:(p + 1) * R].zero_()
+
+
+@pytest.mark.parametrize("W,R,K,N", [(4, 200, 256, 384), (2, 256, 512, 512), (8, 64, 128, 256)])
+def test_gemm_reducescatter(W, R, K, N):
+    M = W * R
+    g = torch.Generator(device=DEV).manual_seed(W + N)
+    a = [torch.randn(M, K, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    w = [(torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16() for _ in range(W)]
+    res = [torch.randn(R, N, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    stage = [torch.zeros(W, R, N, device=DEV, dtype=torch.bfloat16) for _ in range(W)]
+    flags = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]   # flags[owner][src]
+    acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]    # acks[src][owner]
+    counters = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for epoch in (1, 2):
+        for r in range(W):
+            ops.tp_gemm_reducescatter(a[r], w[r], stage=[s.data_ptr() for s in stage],
+                                      peer_flags=[f.data_ptr() + 8 * r for f in flags], rank=r, epoch=epoch,
+                                      counters=counters)
+        outs = []
+        for p in range(W):
+            o = torch.empty(R, N, device=DEV, dtype=torch.bfloat16)
+            ops.tp_reduce(stage[p], W, R, o, flags_ptr=flags[p].data_ptr(), flag_stride=1, epoch=epoch,
+                          peer_acks=[x.data_ptr() + 8 * p for x in acks], rank=p, residual=res[p])
+            outs.append(o)
+        torch.cuda.synchronize()
+        assert native.device_error(reset=True) == 0
+        full = sum(a[r].float() @ w[r].float().t() for r in range(W))
+        for p in range(W):
+            ref = full[p * R:(p + 1) * R] + res[p].float()
+            assert _rel(outs[p], ref) < 2e-2, f"owner {p}"
+            for q in range(W):
+                if q != p:
+                    assert int(acks[q][p]) == epoch
