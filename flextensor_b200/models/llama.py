@@ -1,0 +1,253 @@
+"""Llama-3-shape decoder (GQA, RoPE, SwiGLU), random-init, with single-GPU and tensor-parallel
+paths built on the native kernels.
+
+Weight layout is chosen for the kernels (``state_dict`` differs from HF checkpoints, which are
+not used here): ``wqkv`` stacks q, k, v rows; ``w_gate_up`` interleaves gate and up rows
+(row 2j = gate_j, row 2j+1 = up_j) so one GEMM with the SwiGLU epilogue produces
+``silu(gate) * up``; RoPE rotates interleaved pairs.
+
+Tensor parallelism (``LlamaTP``): heads, FFN columns and their weight rows/columns are split
+over the ranks, and the residual stream is sequence-parallel (each rank holds 1/N of the token
+rows between layers). Per layer: RMSNorm of the own rows straight into the all-gather buffer ->
+all-gather+QKV GEMM -> RoPE -> causal GQA attention on the local heads -> o_proj
+GEMM+reduce-scatter -> owner reduce with the residual -> RMSNorm -> all-gather+gate/up GEMM
+(SwiGLU) -> down GEMM+reduce-scatter -> reduce. ``collective="nccl"`` runs the same GEMMs around
+NCCL all-gather / reduce-scatter (the baseline).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+
+@dataclass
+class LlamaConfig:
+    dim: int = 8192
+    n_layers: int = 80
+    n_heads: int = 64
+    n_kv_heads: int = 8
+    ffn_dim: int = 28672
+    vocab: int = 128256
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+
+LLAMA3_70B = LlamaConfig()
+
+
+def tiny_llama(**kw) -> LlamaConfig:
+    base = dict(dim=512, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab=1024)
+    base.update(kw)
+    return LlamaConfig(**base)
+
+
+def rope_tables_1d(seq_len: int, head_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64, device=device) / head_dim))
+    ang = torch.outer(torch.arange(seq_len, dtype=torch.float64, device=device), inv)
+    return torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous()
+
+
+def _rope_torch(x, cos, sin):  # x [B, S, H, D] fp32, interleaved pairs
+    b, s, h, d = x.shape
+    xr = x.view(b, s, h, d // 2, 2)
+    re, im = xr[..., 0], xr[..., 1]
+    c, sn = cos[None, :s, None, :], sin[None, :s, None, :]
+    return torch.stack([re * c - im * sn, re * sn + im * c], dim=-1).view(b, s, h, d)
+
+
+def _rms_torch(x, w, eps):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+class LlamaLayer(nn.Module):
+    def __init__(self, cfg: LlamaConfig, n_heads: int | None = None, n_kv: int | None = None,
+                 ffn: int | None = None):
+        super().__init__()
+        self.cfg = cfg
+        hq, hk, f = n_heads or cfg.n_heads, n_kv or cfg.n_kv_heads, ffn or cfg.ffn_dim
+        self.hq, self.hk, self.f = hq, hk, f
+        D = cfg.head_dim
+        self.attn_norm = nn.Parameter(torch.ones(cfg.dim))
+        self.wqkv = nn.Parameter(torch.empty((hq + 2 * hk) * D, cfg.dim))
+        self.wo = nn.Parameter(torch.empty(cfg.dim, hq * D))
+        self.ffn_norm = nn.Parameter(torch.ones(cfg.dim))
+        self.w_gate_up = nn.Parameter(torch.empty(2 * f, cfg.dim))
+        self.w_down = nn.Parameter(torch.empty(cfg.dim, f))
+
+    # ---------------------------------------------------------------- single GPU
+    def forward_torch(self, x, B, S, rope):
+        cfg, D = self.cfg, self.cfg.head_dim
+        h = _rms_torch(x, self.attn_norm, cfg.eps)
+        qkv = F.linear(h, self.wqkv)
+        q, k, v = qkv.split([self.hq * D, self.hk * D, self.hk * D], dim=-1)
+        q = _rope_torch(q.reshape(B, S, self.hq, D).float(), *rope).to(x.dtype)
+        k = _rope_torch(k.reshape(B, S, self.hk, D).float(), *rope).to(x.dtype)
+        v = v.reshape(B, S, self.hk, D)
+        rep = self.hq // self.hk
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.repeat_interleave(rep, 2).transpose(1, 2),
+                                           v.repeat_interleave(rep, 2).transpose(1, 2), is_causal=True)
+        x = x + F.linear(o.transpose(1, 2).reshape(B * S, -1), self.wo)
+        h = _rms_torch(x, self.ffn_norm, cfg.eps)
+        gu = F.linear(h, self.w_gate_up)
+        return x + F.linear(F.silu(gu[:, 0::2]) * gu[:, 1::2], self.w_down)
+
+    def forward_fused(self, x, B, S, rope):
+        from flextensor_b200 import ops
+
+        cfg, D = self.cfg, self.cfg.head_dim
+        h = ops.rmsnorm(x, self.attn_norm, eps=cfg.eps)
+        qkv = ops.linear(h, self.wqkv, None, epi="none")
+        qn, kn = self.hq * D, self.hk * D
+        q, k, v = qkv[:, :qn], qkv[:, qn:qn + kn], qkv[:, qn + kn:]
+        ops.rope(q, *rope, D, S, out=q)
+        ops.rope(k, *rope, D, S, out=k)
+        o = ops.attention(q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D), causal=True)
+        ops.linear(o.view(B * S, -1), self.wo, None, epi="res", residual=x, out=x)
+        h = ops.rmsnorm(x, self.ffn_norm, eps=cfg.eps, out=h)
+        f = ops.linear_swiglu(h, self.w_gate_up)
+        ops.linear(f, self.w_down, None, epi="res", residual=x, out=x)
+        return x
+
+    # ---------------------------------------------------------------- tensor parallel (one rank's shard)
+    def forward_tp(self, x_local, B, S, rope, tp):
+        from flextensor_b200 import ops
+
+        cfg, D = self.cfg, self.cfg.head_dim
+        qn, kn = self.hq * D, self.hk * D
+        fused = tp.collective == "fused"
+        if fused:  # RMSNorm of the own rows straight into the all-gather buffer
+            ops.rmsnorm(x_local, self.attn_norm, eps=cfg.eps, out=tp._ag.begin())
+            tp._ag.publish()
+            qkv = tp._ag.gemm(self.wqkv)
+        else:
+            h = ops.rmsnorm(x_local, self.attn_norm, eps=cfg.eps)
+            qkv = ops.linear(tp._nccl.all_gather(h), self.wqkv, None, epi="none")
+        q, k, v = qkv[:, :qn], qkv[:, qn:qn + kn], qkv[:, qn + kn:]
+        ops.rope(q, *rope, D, S, out=q)
+        ops.rope(k, *rope, D, S, out=k)
+        o = ops.attention(q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D), causal=True)
+        o2 = o.view(B * S, -1)
+        if fused:
+            tp._rs.gemm(o2, self.wo)
+            tp._rs.reduce(x_local, residual=x_local)
+            ops.rmsnorm(x_local, self.ffn_norm, eps=cfg.eps, out=tp._ag.begin())
+            tp._ag.publish()
+            f = tp._ag.gemm(self.w_gate_up, epi="swiglu")
+            tp._rs.gemm(f, self.w_down)
+            tp._rs.reduce(x_local, residual=x_local)
+        else:
+            x_local += tp._nccl.reduce_scatter(ops.linear(o2, self.wo, None, epi="none"))
+            h = ops.rmsnorm(x_local, self.ffn_norm, eps=cfg.eps)
+            f = ops.linear_swiglu(tp._nccl.all_gather(h), self.w_gate_up)
+            x_local += tp._nccl.reduce_scatter(ops.linear(f, self.w_down, None, epi="none"))
+        return x_local
+
+    def forward(self, x, B, S, rope, impl="fused", tp=None):
+        if tp is not None:
+            return self.forward_tp(x, B, S, rope, tp)
+        return self.forward_fused(x, B, S, rope) if impl == "fused" else self.forward_torch(x, B, S, rope)
+
+
+class LlamaModel(nn.Module):
+    def __init__(self, cfg: LlamaConfig = LLAMA3_70B, impl: str = "fused"):
+        super().__init__()
+        self.cfg = cfg
+        self.impl = impl
+        self.embed = nn.Embedding(cfg.vocab, cfg.dim)
+        self.layers = nn.ModuleList([LlamaLayer(cfg) for _ in range(cfg.n_layers)])
+        self.norm = nn.Parameter(torch.ones(cfg.dim))
+        self.lm_head = nn.Parameter(torch.empty(cfg.vocab, cfg.dim))
+        self._rope = {}
+
+    def rope(self, S, device):
+        key = (S, str(device))
+        if key not in self._rope:
+            self._rope[key] = rope_tables_1d(S, self.cfg.head_dim, self.cfg.rope_theta, device)
+        return self._rope[key]
+
+    def forward(self, tokens: torch.Tensor, last_only: bool = True) -> torch.Tensor:
+        """tokens ``[B, S]`` (equal-length prompts) -> logits ``[B, vocab]`` of the last position
+        (or ``[B, S, vocab]``)."""
+        B, S = tokens.shape
+        x = self.embed(tokens).reshape(B * S, -1).contiguous()
+        rope = self.rope(S, x.device)
+        for layer in self.layers:
+            x = layer(x, B, S, rope, self.impl)
+        h = x.view(B, S, -1)[:, -1] if last_only else x.view(B, S, -1)
+        h = _rms_torch(h, self.norm, self.cfg.eps)
+        return F.linear(h, self.lm_head)
+
+
+def init_llama_params_(model: nn.Module, seed: int = 0, std: float = 0.02) -> None:
+    g = torch.Generator(device=next(model.parameters()).device)
+    g.manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("norm") or name == "norm":
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, std, generator=g)
+
+
+# ----------------------------------------------------------------------------- tensor parallel
+class LlamaTP(nn.Module):
+    """One rank's shard of the decoder layers (heads / FFN split over ``world`` ranks)."""
+
+    def __init__(self, cfg: LlamaConfig, rank: int, world: int, layers: int | None = None):
+        super().__init__()
+        if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.ffn_dim % world:
+            raise ValueError("heads, kv heads and FFN width must split evenly over the ranks")
+        self.cfg, self.rank, self.world = cfg, rank, world
+        n = layers if layers is not None else cfg.n_layers
+        self.layers = nn.ModuleList([LlamaLayer(cfg, cfg.n_heads // world, cfg.n_kv_heads // world,
+                                                cfg.ffn_dim // world) for _ in range(n)])
+        self._ag = self._rs = self._nccl = None
+
+    @torch.no_grad()
+    def load_from_full(self, full: LlamaModel) -> "LlamaTP":
+        cfg, r, W, D = self.cfg, self.rank, self.world, self.cfg.head_dim
+        hq, hk, f = cfg.n_heads // W, cfg.n_kv_heads // W, cfg.ffn_dim // W
+        for mine, src in zip(self.layers, full.layers):
+            qn, kn = cfg.n_heads * D, cfg.n_kv_heads * D
+            q = src.wqkv[:qn].view(cfg.n_heads, D, -1)[r * hq:(r + 1) * hq].reshape(hq * D, -1)
+            k = src.wqkv[qn:qn + kn].view(cfg.n_kv_heads, D, -1)[r * hk:(r + 1) * hk].reshape(hk * D, -1)
+            v = src.wqkv[qn + kn:].view(cfg.n_kv_heads, D, -1)[r * hk:(r + 1) * hk].reshape(hk * D, -1)
+            mine.wqkv.copy_(torch.cat([q, k, v]))
+            mine.wo.copy_(src.wo.view(cfg.dim, cfg.n_heads, D)[:, r * hq:(r + 1) * hq].reshape(cfg.dim, -1))
+            mine.w_gate_up.copy_(src.w_gate_up.view(cfg.ffn_dim, 2, -1)[r * f:(r + 1) * f].reshape(2 * f, -1))
+            mine.w_down.copy_(src.w_down[:, r * f:(r + 1) * f])
+            mine.attn_norm.copy_(src.attn_norm)
+            mine.ffn_norm.copy_(src.ffn_norm)
+        return self
+
+    def setup(self, tokens_total: int, group=None, collective: str = "fused") -> None:
+        from flextensor_b200.parallel.tp import NcclTP, TPAllGather, TPReduceScatter
+
+        self.collective = collective
+        if collective == "fused":
+            self._ag = TPAllGather(tokens_total, self.cfg.dim, group)
+            self._rs = TPReduceScatter(tokens_total, self.cfg.dim, group)
+        else:
+            self._nccl = NcclTP(group)
+
+    def close(self) -> None:
+        for o in (self._ag, self._rs):
+            if o is not None:
+                o.close()
+        self._ag = self._rs = None
+
+    def forward(self, x_local: torch.Tensor, B: int, S: int, rope) -> torch.Tensor:
+        """x_local ``[B*S/world, dim]`` (this rank's token rows) -> same rows after all layers.
+        Each layer is called as a module (``layers.*`` are offload units)."""
+        for L in self.layers:
+            x_local = L(x_local, B, S, rope, tp=self)
+        return x_local

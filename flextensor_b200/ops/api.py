@@ -80,6 +80,17 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None = None, *, eps: float =
     return out
 
 
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, head_dim: int, seq_len: int, *,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """Interleaved-pair rotary embedding per head (row position = row index mod ``seq_len``)."""
+    x2 = _2d(x)
+    if out is None:
+        out = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    native.lib().rmsnorm(x2, _2d(out), None, cos, sin, int(head_dim), int(seq_len), -1.0)
+    _count()
+    return out
+
+
 def qk_rmsnorm_rope(x: torch.Tensor, weight: torch.Tensor | None, cos: torch.Tensor, sin: torch.Tensor,
                     head_dim: int, seq_len: int, *, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
     """RMSNorm over the full row, then interleaved-pair RoPE per head (tables ``[seq_len, head_dim/2]``)."""
@@ -157,3 +168,21 @@ def tp_reduce(stage: torch.Tensor, world: int, rows: int, out: torch.Tensor, *, 
                            [int(p) for p in peer_acks], int(rank))
     _count(2)
     return out
+
+
+_swiglu_dummies: dict = {}
+
+
+def linear_swiglu(x: torch.Tensor, weight_gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(x @ Wg.T) * (x @ Wu.T)`` with gate/up rows interleaved in ``weight_gate_up`` ``[2F, K]``
+    (one tcgen05 GEMM, SwiGLU in the epilogue; the all-gather GEMM kernel with one rank)."""
+    a = x if x.is_contiguous() else x.contiguous()
+    key = a.device
+    d = _swiglu_dummies.get(key)
+    if d is None:
+        d = (torch.zeros(2, dtype=torch.int64, device=a.device), torch.zeros(2, dtype=torch.int32, device=a.device))
+        _swiglu_dummies[key] = d
+    flags, counters = d
+    return tp_allgather_gemm(a, weight_gate_up, peer_a=[a.data_ptr()], flags_ptr=flags.data_ptr(), flag_stride=1,
+                             peer_acks=[flags.data_ptr() + 8], rank=0, epoch=0, counters=counters, epi="swiglu",
+                             out=out)

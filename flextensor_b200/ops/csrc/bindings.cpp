@@ -145,6 +145,7 @@ void rmsnorm(const Tensor& x, Tensor& y, const c10::optional<Tensor>& weight, co
   a.ldy = y.stride(0);
   a.D = x.size(1);
   a.eps = (float)eps;
+  a.no_norm = eps < 0;  // rope only
   if (weight && weight->defined()) {
     TORCH_CHECK(weight->numel() == a.D && weight->is_contiguous(), "weight must be [D]");
     a.weight = weight->data_ptr();

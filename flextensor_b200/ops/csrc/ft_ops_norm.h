@@ -34,6 +34,7 @@ struct RmsArgs {
   const float* sin = nullptr;
   int head_dim = 0;
   int seq_len = 0;
+  bool no_norm = false;  // rotary embedding only (no RMS scaling, no weight)
 };
 
 cudaError_t ln_modulate(const LnArgs& a, int rows, cudaStream_t st);

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(RmsArgs a) {
       for (int e = 0; e < 8; e++) ss += v[i][e] * v[i][e];
     }
   }
-  const float r = rsqrtf(block_sum<NT>(ss, red) / a.D + a.eps);
+  const float r = a.no_norm ? 1.f : rsqrtf(block_sum<NT>(ss, red) / a.D + a.eps);
   // optional rotary embedding on interleaved pairs, per head of size a.head_dim
   const int pos = a.seq_len > 0 ? row % a.seq_len : 0;
 #pragma unroll

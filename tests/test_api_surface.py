@@ -1,0 +1,28 @@
+"""Every public kernel entry point of ``ops.api`` is re-exported by ``flextensor_b200.ops``, and
+the model modules only call names that exist there (catches a missing export on CPU)."""
+
+import ast
+import inspect
+import pathlib
+
+import flextensor_b200.ops as ops
+from flextensor_b200.ops import api
+
+ROOT = pathlib.Path(__file__).resolve().parents[1] / "flextensor_b200"
+
+
+def test_ops_reexports_api():
+    public = {n for n, f in vars(api).items() if inspect.isfunction(f) and not n.startswith("_")
+              and f.__module__ == api.__name__}
+    missing = sorted(public - set(ops.__all__))
+    assert not missing, f"not exported from flextensor_b200.ops: {missing}"
+
+
+def test_models_use_existing_ops():
+    used = set()
+    for path in list((ROOT / "models").glob("*.py")) + list((ROOT / "parallel").glob("*.py")):
+        for node in ast.walk(ast.parse(path.read_text())):
+            if isinstance(node, ast.Attribute) and isinstance(node.value, ast.Name) and node.value.id == "ops":
+                used.add((path.name, node.attr))
+    bad = [(f, a) for f, a in used if not hasattr(ops, a)]
+    assert not bad, f"calls to missing ops: {bad}"

@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker_body(rank, world, port, q):
     import datetime
 
     import torch.distributed as dist
@@ -62,6 +62,16 @@ def _worker(rank, world, port, q):
     q.put((rank, max(errs), err_u, err_word, float(want.abs().max())))
 
 
+def _worker(rank, world, port, q):
+    try:
+        _worker_body(rank, world, port, q)
+    except BaseException:  # report instead of leaving the parent waiting on the queue
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+        raise
+
+
 def test_cp_dit_two_ranks():
     import torch.multiprocessing as mp
 
@@ -71,7 +81,9 @@ def test_cp_dit_two_ranks():
     ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in ps:
         p.start()
-    res = sorted(q.get(timeout=300) for _ in ps)
+    res = sorted((q.get(timeout=300) for _ in ps), key=lambda t: t[0])
+    for r in res:
+        assert r[1] != "error", f"rank {r[0]} failed:\n{r[2]}"
     for p in ps:
         p.join(60)
     for rank, err, err_u, word, scale in res:
