@@ -119,7 +119,7 @@ def attention_cp(q: torch.Tensor, kv_local: torch.Tensor, *, peer_kv: list[int],
                  peer_acks: list[int], rank: int, shard_rows: int, epoch: int, counters: torch.Tensor,
                  scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """Context-parallel attention: local queries ``q [B, Sq, Hq, 128]`` over the keys of every
-    rank. ``kv_local [B, Sk, 2, Hk, 128]`` is this rank's full-sequence K|V buffer with its own
+    rank. ``kv_local [B, 2, Sk, Hk, 128]`` is this rank's full-sequence K/V buffer with its own
     rows ``[rank*shard_rows, (rank+1)*shard_rows)`` written and published (epoch flag) before
     the call; the kernel pulls the other ranks' rows from ``peer_kv`` over NVLink while it
     computes (see ``attention_sm100.cu``)."""

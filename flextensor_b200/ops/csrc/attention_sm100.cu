@@ -43,7 +43,6 @@ constexpr float RESCALE_THRESHOLD = 8.0f;
 constexpr int NTHREADS = 320;            // plain attention: 10 warps
 constexpr int NTHREADS_CP = 352;         // context-parallel: + warp 10, the K/V gather warp
 constexpr int CP_PIECE = 12288;          // bytes per gather step (peer -> smem -> local HBM)
-constexpr int CP_MAX_KV_BLOCKS = 1024;   // 128-key blocks (131072 keys)
 
 struct AttnArgs {
   int B, Sq, Sk, Hq, Hk;
@@ -69,22 +68,21 @@ struct SmemBase {
 struct SmemCP : SmemBase {
   alignas(128) uint8_t stage[2][CP_PIECE];  // gather staging (peer -> here -> local HBM)
   uint64_t stage_full[2];
-  int n_order;
-  uint16_t order[CP_MAX_KV_BLOCKS];         // KV block processing order (own shard first)
+  int run_a[kCpMaxRanks], run_len[kCpMaxRanks];  // KV block order: runs [a, a+len) for distance 0..W-1
 };
 template <bool CP>
 using SmemT = typename std::conditional<CP, SmemCP, SmemBase>::type;
 
 // Context-parallel extension: this rank's queries attend over the K/V of all ranks. Each rank
-// writes its K/V rows (K|V interleaved per token) into its own copy of the full-sequence
-// buffer and publishes an epoch flag; inside this kernel, warp 10 of every CTA pulls peers'
+// writes its K/V rows into its own copy of the full-sequence buffer [B, 2, S, Hk, 128] (K block,
+// then V block) and publishes an epoch flag; inside this kernel, warp 10 of every CTA pulls peers'
 // rows into the local buffer (claiming 12 KB pieces from a per-peer ticket counter, so any
 // resident CTA can finish a chunk and no CTA waits on a CTA that is not running), and the TMA
 // producer waits for a peer's chunk to be complete before loading its keys. KV blocks are
 // processed own-shard first, then peers in the order they are gathered.
 struct CpArgs {
   int rank, world, shard_rows;
-  long long row_bytes, batch_bytes, shard_bytes;  // per token row / batch / one rank's rows of a batch
+  long long row_bytes, part_bytes, batch_bytes, shard_bytes;  // token row / K or V part / batch / one rank's rows
   const uint8_t* peer_kv[kCpMaxRanks];             // each rank's full-sequence K|V buffer (own at [rank])
   uint8_t* local_kv;
   const uint64_t* flags;                           // flags[q * flag_stride]: epoch rank q published
@@ -93,7 +91,7 @@ struct CpArgs {
   uint64_t epoch;
   unsigned int* claim;                             // [world], zero at launch
   unsigned int* done;                              // [world], zero at launch
-  int pieces_per_batch, batches;
+  int pieces_per_part, pieces_per_batch, batches;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -205,21 +203,45 @@ __device__ bool cp_wait_done(const unsigned int* d, unsigned int target) {
 }
 
 // KV blocks in gather order: a block is processed once every rank whose rows it holds is
-// local; blocks needing only this rank's rows come first.
-__device__ void cp_build_order(SmemCP& sm, const CpArgs& c, int Sk) {
-  int n = 0;
-  for (int d = 0; d < c.world; d++) {
-    const int p = (c.rank + d) % c.world;
-    const int first = p * c.shard_rows / TILE, last = ((p + 1) * c.shard_rows - 1) / TILE;
-    for (int kb = first; kb <= last; kb++) {
-      const int lo = kb * TILE / c.shard_rows, hi = min(kb * TILE + TILE - 1, Sk - 1) / c.shard_rows;
-      int md = 0;
-      for (int q = lo; q <= hi; q++) md = max(md, (q - c.rank + c.world) % c.world);
-      if (md == d && n < CP_MAX_KV_BLOCKS) sm.order[n++] = (uint16_t)kb;
+// local; blocks needing only this rank's rows come first. A block belongs to the run of the
+// rank (among those whose rows it holds) that is gathered last, so run d is rank
+// (rank + d)'s block range, trimmed by its first / last block when that block also holds rows
+// of a rank gathered later. O(world) work, done by one thread at CTA start.
+__device__ int cp_block_owner(const CpArgs& c, int kb, int Sk) {
+  const int lo = kb * TILE / c.shard_rows, hi = min(kb * TILE + TILE - 1, Sk - 1) / c.shard_rows;
+  int best = lo, bd = -1;
+  for (int q = lo; q <= hi; q++) {
+    const int d = (q - c.rank + c.world) % c.world;
+    if (d > bd) {
+      bd = d;
+      best = q;
     }
   }
-  sm.n_order = n;
+  return best;
 }
+
+__device__ void cp_build_runs(SmemCP& sm, const CpArgs& c, int Sk) {
+  for (int d = 0; d < c.world; d++) {
+    const int p = (c.rank + d) % c.world;
+    int a = p * c.shard_rows / TILE, b = ((p + 1) * c.shard_rows - 1) / TILE;
+    if (a <= b && cp_block_owner(c, a, Sk) != p) a++;
+    if (a <= b && cp_block_owner(c, b, Sk) != p) b--;
+    sm.run_a[d] = a;
+    sm.run_len[d] = b >= a ? b - a + 1 : 0;
+  }
+}
+
+// Next KV block in run order (call once per block, in order).
+struct KvCursor {
+  int d = 0, i = 0;
+  __device__ __forceinline__ int next(const SmemCP& sm) {
+    while (i >= sm.run_len[d]) {
+      d++;
+      i = 0;
+    }
+    return sm.run_a[d] + i++;
+  }
+};
 
 // Warp 10 (one lane): claim 12 KB pieces of peers' rows and move them peer -> smem -> local
 // HBM with bulk copies, two pieces in flight; the CTA that completes a peer's chunk tells the
@@ -251,9 +273,12 @@ __device__ void cp_gather(SmemCP& sm, const CpArgs& c) {
         flagged = true;
       }
       const int b = idx / c.pieces_per_batch;
-      const long long off = (long long)(idx % c.pieces_per_batch) * CP_PIECE;
+      const int rem = idx % c.pieces_per_batch;
+      const int part = rem / c.pieces_per_part;  // 0: K rows, 1: V rows
+      const long long off = (long long)(rem % c.pieces_per_part) * CP_PIECE;
       const uint32_t n = (uint32_t)min((long long)CP_PIECE, c.shard_bytes - off);
-      const long long at = (long long)b * c.batch_bytes + (long long)p * c.shard_bytes + off;
+      const long long at =
+          (long long)b * c.batch_bytes + (long long)part * c.part_bytes + (long long)p * c.shard_bytes + off;
       const int st = issued & 1;
       mbar_arrive_expect_tx(&sm.stage_full[st], n);
       bulk_load_g2s(sm.stage[st], c.peer_kv[p] + at, n, &sm.stage_full[st]);
@@ -312,7 +337,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
     if constexpr (CP) {
       mbar_init(&sm.stage_full[0], 1);
       mbar_init(&sm.stage_full[1], 1);
-      cp_build_order(sm, cp, a.Sk);
+      cp_build_runs(sm, cp, a.Sk);
     }
     fence_barrier_init();
   }
@@ -343,12 +368,13 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
       bool ok = true;
       uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
       uint32_t ready = 0;  // CP: peers whose rows are complete in the local buffer
+      [[maybe_unused]] KvCursor cur;
       for (int j = 0; j < n_kv && ok; j++) {
         const int s = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
         int kb = j;
         if constexpr (CP) {
-          kb = sm.order[j];
+          kb = cur.next(sm);
           const unsigned int npieces = (unsigned int)(cp.pieces_per_batch * cp.batches);
           const int lo = kb * TILE / cp.shard_rows, hi = min(kb * TILE + TILE - 1, a.Sk - 1) / cp.shard_rows;
           for (int q = lo; q <= hi && ok; q++) {
@@ -482,7 +508,10 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
     const bool active = (t == 0) || has_b;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    [[maybe_unused]] KvCursor cur;
     for (int j = 0; active && j < n_kv; j++) {
+      int kbase = j * TILE;
+      if constexpr (CP) kbase = cur.next(sm) * TILE;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1))) {
         ok = false;
         break;
@@ -495,8 +524,6 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
         if (lane == 0) mbar_arrive(&sm.p_full[t]);
         continue;
       }
-      int kbase = j * TILE;
-      if constexpr (CP) kbase = sm.order[j] * TILE;
       const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0 + t * TILE);
       // Single pass over the S row: all 128 columns in flight in one TMEM round trip,
       // 8-way tree max, exp2 in registers, P packed in place (pair i of chunk c -> word i),
@@ -694,19 +721,19 @@ cudaError_t attention_cp_fwd(const AttnProblem& p, const AttnCpProblem& c, cudaS
   if (p.B == 0 || p.Sq == 0) return cudaSuccess;
   if (p.Hq % p.Hk || p.causal) return cudaErrorInvalidValue;
   if (c.world < 1 || c.world > kCpMaxRanks || c.rank < 0 || c.rank >= c.world || c.shard_rows <= 0 ||
-      (long long)c.world * c.shard_rows != p.Sk || (p.Sk + TILE - 1) / TILE > CP_MAX_KV_BLOCKS ||
+      (long long)c.world * c.shard_rows != p.Sk ||
       c.flags == nullptr || c.counters == nullptr)
     return cudaErrorInvalidValue;
   for (int r = 0; r < c.world; r++)
     if (c.peer_kv[r] == nullptr || (r != c.rank && c.peer_acks[r] == nullptr)) return cudaErrorInvalidValue;
   // K|V interleaved per token: row = [K (Hk*128) | V (Hk*128)] bf16, rows contiguous, batches contiguous
-  const long long row_el = 2LL * p.Hk * HD;
+  const long long row_el = (long long)p.Hk * HD;  // [B, 2, Sk, Hk, 128]: K block, then V block
   const uint8_t* base = static_cast<const uint8_t*>(c.peer_kv[c.rank]);
   if (reinterpret_cast<uintptr_t>(base) & 255) return cudaErrorMisalignedAddress;
   CUtensorMap tq, tk, tv;
   if (!make_tmap_3d(&tq, p.q, p.Hq, p.Sq, p.B, p.q_row, p.q_batch)) return cudaErrorInvalidValue;
-  if (!make_tmap_3d(&tk, base, p.Hk, p.Sk, p.B, row_el, row_el * p.Sk)) return cudaErrorInvalidValue;
-  if (!make_tmap_3d(&tv, base + p.Hk * HD * 2, p.Hk, p.Sk, p.B, row_el, row_el * p.Sk))
+  if (!make_tmap_3d(&tk, base, p.Hk, p.Sk, p.B, row_el, 2 * row_el * p.Sk)) return cudaErrorInvalidValue;
+  if (!make_tmap_3d(&tv, base + row_el * p.Sk * 2, p.Hk, p.Sk, p.B, row_el, 2 * row_el * p.Sk))
     return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(p.o) & 15 || p.o_row % 8 || p.o_batch % 8) return cudaErrorMisalignedAddress;
   AttnArgs a;
@@ -728,7 +755,8 @@ cudaError_t attention_cp_fwd(const AttnProblem& p, const AttnCpProblem& c, cudaS
   k.world = c.world;
   k.shard_rows = c.shard_rows;
   k.row_bytes = row_el * 2;
-  k.batch_bytes = k.row_bytes * p.Sk;
+  k.part_bytes = k.row_bytes * p.Sk;
+  k.batch_bytes = 2 * k.part_bytes;
   k.shard_bytes = k.row_bytes * c.shard_rows;
   for (int r = 0; r < c.world; r++) {
     k.peer_kv[r] = static_cast<const uint8_t*>(c.peer_kv[r]);
@@ -740,7 +768,8 @@ cudaError_t attention_cp_fwd(const AttnProblem& p, const AttnCpProblem& c, cudaS
   k.epoch = c.epoch;
   k.claim = c.counters;
   k.done = c.counters + c.world;
-  k.pieces_per_batch = (int)((k.shard_bytes + CP_PIECE - 1) / CP_PIECE);
+  k.pieces_per_part = (int)((k.shard_bytes + CP_PIECE - 1) / CP_PIECE);
+  k.pieces_per_batch = 2 * k.pieces_per_part;
   k.batches = p.B;
   cudaError_t e = cudaMemsetAsync(c.counters, 0, 2 * sizeof(unsigned int) * c.world, stream);
   if (e != cudaSuccess) return e;

@@ -210,7 +210,7 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
 }
 
 // Context-parallel attention: q [B, Sq, Hq, 128] local queries, o like q; kv_local is this
-// rank's [B, Sk, 2, Hk, 128] K|V buffer (own rows written and published before the call).
+// rank's [B, 2, Sk, Hk, 128] K/V buffer (own rows written and published before the call).
 void attention_cp(const Tensor& q, const Tensor& kv_local, Tensor& o, double scale, std::vector<uint64_t> peer_kv,
                   uint64_t flags, int64_t flag_stride, std::vector<uint64_t> peer_acks, int64_t rank,
                   int64_t shard_rows, uint64_t epoch, Tensor& counters) {
@@ -218,8 +218,8 @@ void attention_cp(const Tensor& q, const Tensor& kv_local, Tensor& o, double sca
                   q.stride(3) == 1 && q.stride(2) == 128, "q: [B, S, H, 128] bf16 CUDA, heads packed");
   TORCH_CHECK(o.sizes() == q.sizes() && o.stride(2) == 128 && o.stride(3) == 1, "o must match q");
   TORCH_CHECK(kv_local.is_cuda() && kv_local.scalar_type() == at::kBFloat16 && kv_local.dim() == 5 &&
-                  kv_local.size(2) == 2 && kv_local.size(4) == 128 && kv_local.is_contiguous(),
-              "kv_local: contiguous [B, Sk, 2, Hk, 128] bf16");
+                  kv_local.size(1) == 2 && kv_local.size(4) == 128 && kv_local.is_contiguous(),
+              "kv_local: contiguous [B, 2, Sk, Hk, 128] bf16");
   const int world = (int)peer_kv.size();
   TORCH_CHECK(world >= 1 && world <= ft::kCpMaxRanks && (int)peer_acks.size() == world, "one kv/ack pointer per rank");
   TORCH_CHECK(peer_kv[rank] == reinterpret_cast<uint64_t>(kv_local.data_ptr()), "peer_kv[rank] must be kv_local");
@@ -229,7 +229,7 @@ void attention_cp(const Tensor& q, const Tensor& kv_local, Tensor& o, double sca
   ft::AttnProblem p;
   p.B = q.size(0);
   p.Sq = q.size(1);
-  p.Sk = kv_local.size(1);
+  p.Sk = kv_local.size(2);
   p.Hq = q.size(2);
   p.Hk = kv_local.size(3);
   p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());

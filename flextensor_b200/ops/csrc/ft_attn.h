@@ -27,7 +27,7 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream);
 constexpr int kCpMaxRanks = 8;
 struct AttnCpProblem {
   int rank = 0, world = 1, shard_rows = 0;   // Sk == world * shard_rows
-  void* peer_kv[kCpMaxRanks] = {};           // each rank's [B, Sk, 2, Hk*128] bf16 buffer (K|V per token)
+  void* peer_kv[kCpMaxRanks] = {};           // each rank's [B, 2, Sk, Hk, 128] bf16 buffer (K block, V block)
   const uint64_t* flags = nullptr;           // local: flags[q * flag_stride] = epoch rank q published
   int flag_stride = 1;
   uint64_t* peer_acks[kCpMaxRanks] = {};     // per peer p: the word that tells p we finished reading it

@@ -2,7 +2,7 @@
 self-attention runs on the local queries over the keys of every rank.
 
 Data plane (no NCCL in the attention path): every rank holds, in a symmetric heap, two
-full-sequence K|V buffers ``[B, S, 2, H*128]`` (one per parity of the attention call, so a
+full-sequence K/V buffers ``[2, S, H*128]`` (a K block, then a V block) (one per parity of the attention call, so a
 call's rows stay readable while the next call is being projected). For each attention call:
 
 1. ``begin()`` -- before the projections overwrite this rank's rows of the slot, wait (on the
@@ -60,9 +60,9 @@ class ContextParallel:
 
     # ------------------------------------------------------------------ buffers
     def slot_kv(self, slot: int) -> torch.Tensor:
-        """The local full-sequence K|V buffer of ``slot`` as ``[S, 2*kv_dim]`` bf16."""
+        """The local full-sequence K/V buffer of ``slot`` as ``[2, S, kv_dim]`` bf16."""
         n = self.seq_len * 2 * self.kv_dim
-        return self.heap.view(self.slot_off[slot], n * 2).view(torch.bfloat16).view(self.seq_len, 2 * self.kv_dim)
+        return self.heap.view(self.slot_off[slot], n * 2).view(torch.bfloat16).view(2, self.seq_len, self.kv_dim)
 
     def shard_rows(self, t: torch.Tensor, dim: int = 1) -> torch.Tensor:
         return t.narrow(dim, self.rank * self.shard, self.shard)
@@ -77,8 +77,9 @@ class ContextParallel:
         if epoch > 1:
             native.lib().p2p_wait_acks_raw(self.flags, self.acks, self.rank, N_SLOTS, slot, epoch - 1)
         self._cur = (slot, epoch)
-        rows = self.slot_kv(slot)[self.rank * self.shard:(self.rank + 1) * self.shard]
-        return rows[:, :self.kv_dim], rows[:, self.kv_dim:]
+        kv = self.slot_kv(slot)
+        rows = slice(self.rank * self.shard, (self.rank + 1) * self.shard)
+        return kv[0, rows], kv[1, rows]
 
     def publish(self) -> None:
         slot, epoch = self._cur
@@ -89,7 +90,7 @@ class ContextParallel:
         from flextensor_b200.ops.api import attention_cp
 
         slot, epoch = self._cur
-        kv = self.slot_kv(slot).view(1, self.seq_len, 2, self.kv_heads, 128)
+        kv = self.slot_kv(slot).view(1, 2, self.seq_len, self.kv_heads, 128)
         flags_local = self.flags[self.rank] + slot * 8           # entry of rank q at [q * N_SLOTS + slot]
         acks = [self.acks[p] + (self.rank * N_SLOTS + slot) * 8 for p in range(self.world)]
         return attention_cp(q, kv, peer_kv=[p + self.slot_off[slot] for p in self.heap.ptrs], flags_ptr=flags_local,

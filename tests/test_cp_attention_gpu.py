@@ -35,10 +35,10 @@ def _setup(B, W, S_loc, Hq, Hk, seed):
     q = torch.randn(B, S_loc, Hq, 128, device=DEV, generator=g).bfloat16()
     bufs = []
     for p in range(W):
-        kv = torch.zeros(B, Sk, 2, Hk, 128, device=DEV, dtype=torch.bfloat16)
+        kv = torch.zeros(B, 2, Sk, Hk, 128, device=DEV, dtype=torch.bfloat16)
         rows = slice(p * S_loc, (p + 1) * S_loc)
-        kv[:, rows, 0] = k[:, rows]
-        kv[:, rows, 1] = v[:, rows]
+        kv[:, 0, rows] = k[:, rows]
+        kv[:, 1, rows] = v[:, rows]
         bufs.append(kv)
     return q, k, v, bufs
 
@@ -63,7 +63,7 @@ def test_cp_attention_matches_full_attention(B, W, S_loc, Hq, Hk, rank):
         assert native.device_error(reset=True) == 0
         err = (out.float() - _ref(q, k, v)).abs().max().item()
         assert err < 2e-2, f"max abs err {err}"
-        assert torch.equal(bufs[rank][:, :, 0], k) and torch.equal(bufs[rank][:, :, 1], v), "K/V not gathered"
+        assert torch.equal(bufs[rank][:, 0], k) and torch.equal(bufs[rank][:, 1], v), "K/V not gathered"
         for p in range(W):
             if p != rank:
                 assert int(acks[p][rank]) == epoch, f"peer {p} not acked"
