@@ -24,6 +24,7 @@ SOURCES = [
     "attention_sm100.cu",
     "p2p.cu",
     "tp_sm100.cu",
+    "moe_sm100.cu",
 ]
 
 CUDA_FLAGS = [

@@ -13,6 +13,7 @@
 #include "ft_ops_norm.h"
 #include "ft_runtime.h"
 #include "ft_tp.h"
+#include "ft_moe.h"
 
 namespace {
 
@@ -377,6 +378,83 @@ void tp_reduce(const Tensor& stage, int64_t world, int64_t rows, Tensor& out, co
   check_ok(ft::tp_reduce(r, at::cuda::getCurrentCUDAStream()), "tp_reduce");
 }
 
+// Expert-parallel MoE expert GEMMs (dispatch = gate/up with the row pull, else down with the
+// combine stores). Peer addresses arrive as integers; weights as one tensor per local expert.
+void moe_gemm(bool dispatch, int64_t rank, int64_t local_experts, int64_t d, int64_t f, int64_t max_rows,
+              std::vector<uint64_t> peer_send, std::vector<uint64_t> peer_table, uint64_t flags, int64_t flag_stride,
+              std::vector<uint64_t> send_acks, Tensor& a_local, Tensor& h_local, std::vector<Tensor> weights,
+              std::vector<uint64_t> peer_comb, std::vector<uint64_t> comb_flags, uint64_t epoch, Tensor& counters) {
+  const int world = (int)peer_table.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kMoeMaxRanks, "1..8 ranks");
+  TORCH_CHECK((int)weights.size() == local_experts, "one weight per local expert");
+  TORCH_CHECK(a_local.is_cuda() && a_local.is_contiguous() && h_local.is_cuda() && h_local.is_contiguous(), "buffers");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 2 * world + 1, "counters");
+  c10::cuda::CUDAGuard g(a_local.device());
+  ft::MoeProblem p;
+  p.rank = (int)rank;
+  p.world = world;
+  p.local_experts = (int)local_experts;
+  p.d = (int)d;
+  p.f = (int)f;
+  p.max_rows = (int)max_rows;
+  for (int r = 0; r < world; r++) {
+    p.peer_table[r] = reinterpret_cast<const int*>(peer_table[r]);
+    if (dispatch) {
+      p.peer_send[r] = reinterpret_cast<const void*>(peer_send.at(r));
+      p.send_acks[r] = reinterpret_cast<uint64_t*>(send_acks.at(r));
+    } else {
+      p.peer_comb[r] = reinterpret_cast<void*>(peer_comb.at(r));
+      p.comb_flags[r] = reinterpret_cast<uint64_t*>(comb_flags.at(r));
+    }
+  }
+  for (int j = 0; j < (int)local_experts; j++) {
+    const Tensor& w = weights[j];
+    TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.is_contiguous(), "expert weights: contiguous bf16");
+    if (dispatch) {
+      TORCH_CHECK(w.size(0) == 2 * f && w.size(1) == d, "gate/up weight must be [2f, d]");
+      p.w_gate_up[j] = w.data_ptr();
+    } else {
+      TORCH_CHECK(w.size(0) == d && w.size(1) == f, "down weight must be [d, f]");
+      p.w_down[j] = w.data_ptr();
+    }
+  }
+  p.flags = reinterpret_cast<const uint64_t*>(flags);
+  p.flag_stride = (int)flag_stride;
+  p.a_local = a_local.data_ptr();
+  p.h_local = h_local.data_ptr();
+  p.epoch = epoch;
+  p.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  p.num_sms = num_sms_for(a_local.get_device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  check_ok(dispatch ? ft::moe_dispatch_gemm(p, st) : ft::moe_combine_gemm(p, st), "moe_gemm");
+}
+
+void moe_reduce(const Tensor& comb, const Tensor& pos, const Tensor& weight, const c10::optional<Tensor>& residual,
+                Tensor& out, uint64_t flags, int64_t flag_stride, int64_t world, int64_t rank, uint64_t epoch) {
+  TORCH_CHECK(pos.scalar_type() == at::kInt && weight.scalar_type() == at::kFloat && pos.is_contiguous() &&
+                  weight.is_contiguous() && pos.sizes() == weight.sizes(), "pos int32 / weight fp32 [tokens, topk]");
+  TORCH_CHECK(out.is_contiguous() && comb.is_contiguous(), "contiguous comb/out");
+  c10::cuda::CUDAGuard g(out.device());
+  ft::MoeCombineProblem p;
+  p.tokens = pos.size(0);
+  p.topk = pos.size(1);
+  p.d = out.size(1);
+  p.world = (int)world;
+  p.rank = (int)rank;
+  p.comb = comb.data_ptr();
+  p.pos = pos.data_ptr<int>();
+  p.weight = weight.data_ptr<float>();
+  if (residual && residual->defined()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == out.sizes(), "residual like out");
+    p.residual = residual->data_ptr();
+  }
+  p.out = out.data_ptr();
+  p.flags = reinterpret_cast<const uint64_t*>(flags);
+  p.flag_stride = (int)flag_stride;
+  p.epoch = epoch;
+  check_ok(ft::moe_combine_reduce(p, at::cuda::getCurrentCUDAStream()), "moe_combine_reduce");
+}
+
 // Direct call of the striped gather with a caller-owned counter buffer (tests and tools).
 void p2p_gather_raw(std::vector<uint64_t> heaps, std::vector<uint64_t> flags, std::vector<uint64_t> acks, int rank,
                     int n_slots, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
@@ -408,7 +486,8 @@ int device_error(bool reset) {
   int a = ft::attn_device_error(reset);
   int p = ft::p2p_device_error(reset);
   int t = ft::tp_device_error(reset);
-  return e ? e : (n ? n : (a ? a : (p ? p : t)));
+  int m = ft::moe_device_error(reset);
+  return e ? e : (n ? n : (a ? a : (p ? p : (t ? t : m))));
 }
 
 struct PyEngine {
@@ -494,6 +573,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_ag_gemm", &tp_ag_gemm);
   m.def("tp_gemm_rs", &tp_gemm_rs);
   m.def("tp_reduce", &tp_reduce);
+  m.def("moe_gemm", &moe_gemm);
+  m.def("moe_reduce", &moe_reduce);
   m.def("p2p_wait_acks_raw", &p2p_wait_acks_raw);
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
