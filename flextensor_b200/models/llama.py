@@ -85,22 +85,14 @@ class LlamaLayer(nn.Module):
 
     # ---------------------------------------------------------------- single GPU
     def forward_torch(self, x, B, S, rope):
-        cfg, D = self.cfg, self.cfg.head_dim
-        h = _rms_torch(x, self.attn_norm, cfg.eps)
-        qkv = F.linear(h, self.wqkv)
-        q, k, v = qkv.split([self.hq * D, self.hk * D, self.hk * D], dim=-1)
-        q = _rope_torch(q.reshape(B, S, self.hq, D).float(), *rope).to(x.dtype)
-        k = _rope_torch(k.reshape(B, S, self.hk, D).float(), *rope).to(x.dtype)
-        v = v.reshape(B, S, self.hk, D)
-        rep = self.hq // self.hk
-        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.repeat_interleave(rep, 2).transpose(1, 2),
-                                           v.repeat_interleave(rep, 2).transpose(1, 2), is_causal=True)
-        x = x + F.linear(o.transpose(1, 2).reshape(B * S, -1), self.wo)
+        cfg = self.cfg
+        x = self.attention_torch(x, B, S, rope)
         h = _rms_torch(x, self.ffn_norm, cfg.eps)
         gu = F.linear(h, self.w_gate_up)
         return x + F.linear(F.silu(gu[:, 0::2]) * gu[:, 1::2], self.w_down)
 
-    def forward_fused(self, x, B, S, rope):
+    def attention_fused(self, x, B, S, rope):
+        """x += o_proj(causal GQA attention(RMSNorm(x))), native kernels, in place."""
         from flextensor_b200 import ops
 
         cfg, D = self.cfg, self.cfg.head_dim
@@ -112,7 +104,27 @@ class LlamaLayer(nn.Module):
         ops.rope(k, *rope, D, S, out=k)
         o = ops.attention(q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D), causal=True)
         ops.linear(o.view(B * S, -1), self.wo, None, epi="res", residual=x, out=x)
-        h = ops.rmsnorm(x, self.ffn_norm, eps=cfg.eps, out=h)
+        return x
+
+    def attention_torch(self, x, B, S, rope):
+        cfg, D = self.cfg, self.cfg.head_dim
+        h = _rms_torch(x, self.attn_norm, cfg.eps)
+        qkv = F.linear(h, self.wqkv)
+        q, k, v = qkv.split([self.hq * D, self.hk * D, self.hk * D], dim=-1)
+        q = _rope_torch(q.reshape(B, S, self.hq, D).float(), *rope).to(x.dtype)
+        k = _rope_torch(k.reshape(B, S, self.hk, D).float(), *rope).to(x.dtype)
+        v = v.reshape(B, S, self.hk, D)
+        rep = self.hq // self.hk
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.repeat_interleave(rep, 2).transpose(1, 2),
+                                           v.repeat_interleave(rep, 2).transpose(1, 2), is_causal=True)
+        return x + F.linear(o.transpose(1, 2).reshape(B * S, -1), self.wo)
+
+    def forward_fused(self, x, B, S, rope):
+        from flextensor_b200 import ops
+
+        cfg = self.cfg
+        x = self.attention_fused(x, B, S, rope)
+        h = ops.rmsnorm(x, self.ffn_norm, eps=cfg.eps)
         f = ops.linear_swiglu(h, self.w_gate_up)
         ops.linear(f, self.w_down, None, epi="res", residual=x, out=x)
         return x
