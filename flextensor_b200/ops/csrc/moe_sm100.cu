@@ -146,11 +146,28 @@ __device__ void build_layout(Layout& L, const MoeArgs& a) {
   L.m_tiles = L.ok ? row / BM : 0;
 }
 
-__device__ __forceinline__ int tile_group(const Layout& L, int el, int mt) {
-  const int r0 = mt * BM;
-  for (int j = el - 1; j >= 0; j--)
-    if (r0 >= L.group_start[j]) return j;
-  return 0;
+// Linear tile index -> (expert group j, M tile, N tile). Tiles go expert group by expert group;
+// inside a group, GROUP_M M tiles share each N tile before moving on, so an expert's weight
+// tile is read from HBM once per GROUP_M M tiles instead of once per M tile (an expert's
+// gate/up weight is 400 MB at the Mixtral shape, far larger than L2).
+constexpr int GROUP_M = 16;
+
+__device__ __forceinline__ void tile_coords(const Layout& L, int el, int n_tiles, int tile, int& j, int& mt,
+                                            int& nt) {
+  j = 0;
+  for (; j < el; j++) {
+    const int mtj = (L.group_rows[j] + BM - 1) / BM;
+    if (tile < mtj * n_tiles) break;
+    tile -= mtj * n_tiles;
+  }
+  const int mtj = (L.group_rows[j] + BM - 1) / BM;
+  const int per_group = GROUP_M * n_tiles;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int first = g * GROUP_M;
+  const int gsz = min(GROUP_M, mtj - first);
+  mt = L.group_start[j] / BM + first + r % gsz;
+  nt = r / gsz;
 }
 
 // Gather lane: claim pieces source by source (own rows first) and move them into a_local.
@@ -270,8 +287,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       uint32_t pend = 0, pend_ph = 0, ready = 0;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int mt = tile / a.num_n_tiles, nt = tile % a.num_n_tiles;
-        const int j = tile_group(L, a.el, mt);
+        int j, mt, nt;
+        tile_coords(L, a.el, a.num_n_tiles, tile, j, mt, nt);
         if constexpr (DISPATCH) {
           const int r0 = mt * BM, r1 = r0 + BM;
           for (int dd = 0; dd < a.world && ok; dd++) {
@@ -355,8 +372,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int tile = blockIdx.x; L.ok && tile < num_tiles; tile += gridDim.x) {
-      const int mt = tile / a.num_n_tiles, nt = tile % a.num_n_tiles;
-      const int j = tile_group(L, a.el, mt);
+      int j, mt, nt;
+      tile_coords(L, a.el, a.num_n_tiles, tile, j, mt, nt);
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.tfull[acc], acc_ph))) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
