@@ -21,6 +21,7 @@ from __future__ import annotations
 import contextlib
 import functools
 import logging
+from dataclasses import dataclass
 import os
 import threading
 from collections.abc import Callable
@@ -48,11 +49,20 @@ class OffloadPhase(Enum):
     INFERENCE = "inference"
 
 
-class StrategyReplanStatus(Enum):
-    IDLE = "idle"
-    PENDING = "pending"
-    DONE = "done"
-    FAILED = "failed"
+@dataclass(frozen=True)
+class StrategyReplanStatus:
+    """Snapshot of the strategy-replan lifecycle (reading it changes nothing).
+
+    ``state``: ``"idle"`` before any request, ``"in_progress"`` while the warm / measure tail
+    rides the caller's forwards, ``"done"`` once it finished (rebuilt or refused),
+    ``"failed"`` if the rebuild raised (inference is unsafe afterwards). ``can_request``:
+    whether ``request_strategy_replan()`` may be called now. ``applied``: ``None`` before and
+    during a request, ``True`` after a rebuild, ``False`` after a refusal or failure.
+    Mirrors ``src/flextensor/compile/replan_status.py:15``."""
+
+    state: str = "idle"
+    can_request: bool = True
+    applied: bool | None = None
 
 
 _ONE_SHOT = ("skip_discovery", "offload_timing", "piecewise_prefetch", "profile_mode", "transfer_mode")
@@ -131,7 +141,8 @@ class OffloadManager:
         self._compiled: dict[str, Callable] = {}
         self._skip_discovery_honored: bool | None = None
         self._manual_blocks = False
-        self._replan_status = StrategyReplanStatus.IDLE
+        self._replan_status = StrategyReplanStatus()
+        self._tail: dict | None = None  # armed replan tail: {"warm": n, "measure": n, "seen": k}
         self._manual_update_state = False
         self._owner_thread = threading.get_ident()
         self._carrier = None
@@ -252,7 +263,38 @@ class OffloadManager:
             self._tm.join_after_forward()
         if not self._manual_update_state:
             self.update_state()
+        if self._tail is not None and self.phase == OffloadPhase.INFERENCE:
+            self._advance_tail()
         return None
+
+    # ------------------------------------------------------------------ replan tail
+    def _advance_tail(self) -> None:
+        """Warm -> measure -> rebuild, one step per completed forward (see request_strategy_replan)."""
+        t = self._tail
+        t["seen"] += 1
+        tm = self._tm
+        if t["seen"] == t["warm"]:  # warm-up done: measure from a clean slate
+            if tm.timing is None:
+                from flextensor_b200.runtime.timing import OffloadTimingCollector
+
+                tm.timing = OffloadTimingCollector(tm.device, "eager")
+                t["temporary_timing"] = True
+            tm.loader.timing = tm.timing
+            tm.reset_offload_timing()
+        if t["seen"] < t["warm"] + t["measure"]:
+            return
+        self._tail = None
+        try:
+            applied = self._replan_from_timing()
+            self._replan_status = StrategyReplanStatus("done", True, applied)
+        except Exception:
+            self._replan_status = StrategyReplanStatus("failed", False, False)
+            raise
+        finally:
+            if t.get("temporary_timing"):
+                tm.timing = None
+                if tm.loader is not None:
+                    tm.loader.timing = None
 
     # ------------------------------------------------------------------ offload
     @_error_boundary
@@ -480,14 +522,32 @@ class OffloadManager:
         return self._replan_status
 
     @_error_boundary
-    def request_strategy_replan(self, *, manual_update_state: bool = False) -> int:
-        """Re-plan from inference timings (compute budgets per trap) and rebuild the loader."""
+    def request_strategy_replan(self, *, manual_update_state: bool = False, warmup_forwards: int = 1,
+                                measure_forwards: int = 3) -> int:
+        """Re-plan from measured inference compute times.
+
+        Arms a tail that rides the caller's next forwards: ``warmup_forwards`` forwards are
+        discarded, the next ``measure_forwards`` are timed per trap (offload timing is enabled
+        for them if it is off), and after the last one the strategy is recomputed from those
+        compute budgets and the loader rebuilt. Returns the number of forwards until the
+        rebuild (``StrategyReplanStatus`` tracks progress)."""
+        if self.phase != OffloadPhase.INFERENCE or self._tm is None or self._tm.loader is None:
+            raise RuntimeError("request_strategy_replan() needs a manager in the INFERENCE phase")
+        if not self._replan_status.can_request:
+            raise RuntimeError(f"a replan cannot be requested now (state={self._replan_status.state!r})")
+        if warmup_forwards < 1 or measure_forwards < 1:
+            raise ValueError("warmup_forwards and measure_forwards must be >= 1")
         self._manual_update_state = manual_update_state
+        self._tail = {"warm": warmup_forwards, "measure": measure_forwards, "seen": 0}
+        self._replan_status = StrategyReplanStatus("in_progress", False, None)
+        return warmup_forwards + measure_forwards
+
+    def _replan_from_timing(self) -> bool:
         tm = self._tm
-        rep = tm.collect_offload_timing() if tm is not None else None
-        if tm is None or rep is None or not rep.per_trap:
-            self._replan_status = StrategyReplanStatus.FAILED
-            return 0
+        rep = tm.collect_offload_timing()
+        if rep is None or not rep.per_trap:
+            LOGGER.warning("strategy replan refused: no per-trap timing was collected")
+            return False
         budgets = rep.compute_budgets_by_profile_label()
         from flextensor_b200.core.stats import LayerStatistics
 
@@ -502,8 +562,7 @@ class OffloadManager:
         result = tm.strategy.compute(tm.layer_stats, tm.memory_stats, tm._gpu_budget())
         tm.strategy_result = result
         tm._build_from_result(result)
-        self._replan_status = StrategyReplanStatus.DONE
-        return len(result.strategy_map)
+        return True
 
     def clear_profiling_durations(self) -> None:
         if self._tm is not None:

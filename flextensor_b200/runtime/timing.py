@@ -160,18 +160,42 @@ def format_offload_timing_table(report: OffloadTimingReport | None) -> str:
     return "\n".join(rows)
 
 
+class _HostStamp:
+    """CPU-device stand-in for a CUDA event (copies there are synchronous)."""
+
+    def __init__(self):
+        self.t = None
+
+    def record(self, *_):
+        import time
+
+        self.t = time.perf_counter()
+
+    def elapsed_time(self, other: "_HostStamp") -> float:
+        return (other.t - self.t) * 1e3
+
+
 class OffloadTimingCollector:
     def __init__(self, device: torch.device, mode: str = "eager"):
         self.device = torch.device(device)
         self.external = mode == "cuda_graph"
-        self.enabled = self.device.type == "cuda" and mode != "off"
+        self.enabled = mode != "off"
+        self.host_clock = self.device.type != "cuda"  # CPU device: wall-clock stamps
         self._pending: list[tuple[dict, list]] = []
         self._done: deque[OffloadTimingSnapshot] = deque(maxlen=MAX_PASSES)
         self._cur: dict | None = None
 
     def _ev(self):
+        if self.host_clock:
+            return _HostStamp()
         return torch.cuda.Event(enable_timing=True, external=self.external) if self.external else \
             torch.cuda.Event(enable_timing=True)
+
+    def _record(self, e) -> None:
+        if self.host_clock:
+            e.record()
+        else:
+            e.record(torch.cuda.current_stream(self.device))
 
     def on_pass_start(self) -> None:
         if self.enabled:
@@ -180,13 +204,13 @@ class OffloadTimingCollector:
     def on_enter(self, label: str) -> None:
         if self.enabled and self._cur is not None:
             e = self._ev()
-            e.record(torch.cuda.current_stream(self.device))
+            self._record(e)
             self._cur[label] = [e, None]
 
     def on_exit(self, label: str) -> None:
         if self.enabled and self._cur is not None and label in self._cur:
             e = self._ev()
-            e.record(torch.cuda.current_stream(self.device))
+            self._record(e)
             self._cur[label][1] = e
 
     def on_pass_end(self, engine) -> None:
@@ -198,7 +222,8 @@ class OffloadTimingCollector:
     def _resolve(self) -> None:
         if not self._pending:
             return
-        torch.cuda.synchronize(self.device)
+        if not self.host_clock:
+            torch.cuda.synchronize(self.device)
         for comp, recs in self._pending:
             vals: dict[str, dict] = {}
             for label, (a, b) in comp.items():

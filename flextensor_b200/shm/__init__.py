@@ -20,11 +20,12 @@ from flextensor_b200.shm.namespace import (
 )
 from flextensor_b200.shm.segment import ProcessFileLock, ShmSegment
 from flextensor_b200.shm.store import ShmWeightStore
+from flextensor_b200.shm.sync import MultiprocessCondition, SemaphoreLock, SharedMultiString
 from flextensor_b200.shm.tensor_store import SharedTensorStore
 
 __all__ = [
     "CoordBlockHeader", "CoordinatorState", "ProcessFileLock", "SHM_PROTOCOL_VERSION", "SharedTensorStore",
     "ShmCoordinator", "ShmCoordinatorError", "ShmCreatorDiedError", "ShmCreatorFailedError", "ShmSegment",
-    "ShmWeightStore", "apply_rank_suffix", "cleanup_namespace", "compute_shm_namespace", "coord_block_name",
+    "ShmWeightStore", "MultiprocessCondition", "SemaphoreLock", "SharedMultiString", "apply_rank_suffix", "cleanup_namespace", "compute_shm_namespace", "coord_block_name",
     "profile_block_name", "retire_abandoned", "weight_block_name",
 ]

@@ -193,3 +193,28 @@ def test_custom_ops_external_compile_path():
     t = torch.zeros(1)
     torch.library.opcheck(torch.ops.flextensor_b200.pre_compute.default, (t, "nope", 0),
                           test_utils=("test_schema", "test_faketensor"))
+
+
+def test_strategy_replan_tail():
+    from flextensor_b200.runtime.manager import StrategyReplanStatus
+
+    m, x = make()
+    ref = m(x).detach().clone()
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg())
+    with torch.no_grad():
+        for _ in range(om.iters_before_inference):
+            mm(x)
+    assert om.strategy_replan_status == StrategyReplanStatus("idle", True, None)
+    n = om.request_strategy_replan(warmup_forwards=1, measure_forwards=2)
+    assert n == 3 and om.strategy_replan_status.state == "in_progress"
+    with pytest.raises(RuntimeError):
+        om.request_strategy_replan()
+    with torch.no_grad():
+        for i in range(n):
+            y = mm(x)
+            assert torch.equal(y, ref)
+    st = om.strategy_replan_status
+    assert st.state == "done" and st.can_request and st.applied is True
+    with torch.no_grad():
+        assert torch.equal(mm(x), ref)  # rebuilt loader still streams correctly
