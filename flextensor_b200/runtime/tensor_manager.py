@@ -226,6 +226,33 @@ class TensorManager:
         for _, b in self.model.named_buffers():
             if b.device != self.device:
                 b.data = b.data.to(self.device)
+        if self.move_top_level_buffers_to_gpu:
+            self._move_attribute_tensors()
+
+    def _move_attribute_tensors(self) -> None:
+        """Plain tensor attributes of modules (not registered as parameter or buffer, e.g. a
+        cached frequency table) follow the model to the device, as the reference's unmapped-
+        tensor processor does (``tensor_processors.py:686``); lists/tuples/dicts of tensors
+        held as attributes are handled one level deep."""
+        moved: dict[int, torch.Tensor] = {}
+
+        def to_dev(t: torch.Tensor) -> torch.Tensor:
+            if t.device == self.device or t.is_meta:
+                return t
+            if id(t) not in moved:
+                moved[id(t)] = t.to(self.device)
+            return moved[id(t)]
+
+        for m in self.model.modules():
+            for k, v in list(vars(m).items()):
+                if k.startswith("_") or isinstance(v, nn.Parameter):
+                    continue
+                if isinstance(v, torch.Tensor):
+                    setattr(m, k, to_dev(v))
+                elif isinstance(v, (list, tuple)) and v and all(isinstance(x, torch.Tensor) for x in v):
+                    setattr(m, k, type(v)(to_dev(x) for x in v))
+                elif isinstance(v, dict) and v and all(isinstance(x, torch.Tensor) for x in v.values()):
+                    setattr(m, k, {kk: to_dev(x) for kk, x in v.items()})
 
     # ================================================================== phases
     def _striping(self):

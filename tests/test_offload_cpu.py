@@ -218,3 +218,26 @@ def test_strategy_replan_tail():
     assert st.state == "done" and st.can_request and st.applied is True
     with torch.no_grad():
         assert torch.equal(mm(x), ref)  # rebuilt loader still streams correctly
+
+
+def test_plain_tensor_attributes_follow_the_model():
+    class WithTable(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc = nn.Linear(8, 8)
+            self.table = torch.arange(8.0)          # plain attribute, not a buffer
+            self.pair = (torch.ones(8), torch.zeros(8))
+
+        def forward(self, x):
+            return self.fc(x) + self.table + self.pair[0]
+
+    torch.manual_seed(0)
+    m = WithTable()
+    x = torch.randn(2, 8)
+    ref = m(x).detach()
+    mm = ft.offload(m, ft.OffloadConfig(pinned_memory=False, include_patterns=["fc"], profiling_iters=1,
+                                        num_blocks=2, min_blocks=2,
+                                        load_strategy=NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2, cyclic=True)))
+    with torch.no_grad():
+        for _ in range(4):
+            assert torch.allclose(mm(x), ref)
