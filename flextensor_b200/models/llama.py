@@ -91,8 +91,12 @@ class LlamaLayer(nn.Module):
         gu = F.linear(h, self.w_gate_up)
         return x + F.linear(F.silu(gu[:, 0::2]) * gu[:, 1::2], self.w_down)
 
-    def attention_fused(self, x, B, S, rope):
-        """x += o_proj(causal GQA attention(RMSNorm(x))), native kernels, in place."""
+    def attention_fused(self, x, B, S, rope, cache=None, pos: int = 0):
+        """x += o_proj(causal GQA attention(RMSNorm(x))), native kernels, in place.
+
+        ``cache`` = (k_cache, v_cache) ``[B, L_max, Hk, 128]``: prefill (``pos == 0``, S tokens)
+        stores the rotated keys and the values of positions [0, S); a decode step (S == 1,
+        ``rope`` holding position ``pos``) appends position ``pos`` and attends over [0, pos]."""
         from flextensor_b200 import ops
 
         cfg, D = self.cfg, self.cfg.head_dim
@@ -102,8 +106,18 @@ class LlamaLayer(nn.Module):
         q, k, v = qkv[:, :qn], qkv[:, qn:qn + kn], qkv[:, qn + kn:]
         ops.rope(q, *rope, D, S, out=q)
         ops.rope(k, *rope, D, S, out=k)
-        o = ops.attention(q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D), causal=True)
-        ops.linear(o.view(B * S, -1), self.wo, None, epi="res", residual=x, out=x)
+        qv, kv_, vv = q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D)
+        if cache is None:
+            o = ops.attention(qv, kv_, vv, causal=True)
+        else:
+            kc, vc = cache
+            kc[:, pos:pos + S].copy_(kv_)
+            vc[:, pos:pos + S].copy_(vv)
+            if S == 1:  # decode: one query per sequence over every cached key
+                o = ops.attention(qv, kc[:, :pos + 1], vc[:, :pos + 1], causal=False)
+            else:
+                o = ops.attention(qv, kv_, vv, causal=True)
+        ops.linear(o.reshape(B * S, -1), self.wo, None, epi="res", residual=x, out=x)
         return x
 
     def attention_torch(self, x, B, S, rope):
@@ -119,11 +133,11 @@ class LlamaLayer(nn.Module):
                                            v.repeat_interleave(rep, 2).transpose(1, 2), is_causal=True)
         return x + F.linear(o.transpose(1, 2).reshape(B * S, -1), self.wo)
 
-    def forward_fused(self, x, B, S, rope):
+    def forward_fused(self, x, B, S, rope, cache=None, pos: int = 0):
         from flextensor_b200 import ops
 
         cfg = self.cfg
-        x = self.attention_fused(x, B, S, rope)
+        x = self.attention_fused(x, B, S, rope, cache, pos)
         h = ops.rmsnorm(x, self.ffn_norm, eps=cfg.eps)
         f = ops.linear_swiglu(h, self.w_gate_up)
         ops.linear(f, self.w_down, None, epi="res", residual=x, out=x)
@@ -163,9 +177,11 @@ class LlamaLayer(nn.Module):
             x_local += tp._nccl.reduce_scatter(ops.linear(f, self.w_down, None, epi="none"))
         return x_local
 
-    def forward(self, x, B, S, rope, impl="fused", tp=None):
+    def forward(self, x, B, S, rope, impl="fused", tp=None, cache=None, pos: int = 0):
         if tp is not None:
             return self.forward_tp(x, B, S, rope, tp)
+        if cache is not None:
+            return self.forward_fused(x, B, S, rope, cache, pos)
         return self.forward_fused(x, B, S, rope) if impl == "fused" else self.forward_torch(x, B, S, rope)
 
 
@@ -197,6 +213,54 @@ class LlamaModel(nn.Module):
         h = x.view(B, S, -1)[:, -1] if last_only else x.view(B, S, -1)
         h = _rms_torch(h, self.norm, self.cfg.eps)
         return F.linear(h, self.lm_head)
+
+
+    # ---------------------------------------------------------------- KV-cache generation
+    def new_cache(self, batch: int, max_len: int, device=None, dtype=torch.bfloat16):
+        cfg = self.cfg
+        dev = device or self.lm_head.device
+        return [(torch.empty(batch, max_len, cfg.n_kv_heads, cfg.head_dim, device=dev, dtype=dtype),
+                 torch.empty(batch, max_len, cfg.n_kv_heads, cfg.head_dim, device=dev, dtype=dtype))
+                for _ in self.layers]
+
+    def _logits(self, h_last):
+        return F.linear(_rms_torch(h_last, self.norm, self.cfg.eps), self.lm_head)
+
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor, cache) -> torch.Tensor:
+        """Native path: run the prompts, fill the cache, return last-position logits."""
+        B, S = tokens.shape
+        x = self.embed(tokens).reshape(B * S, -1).contiguous()
+        rope = self.rope(cache[0][0].shape[1], x.device)
+        rope_s = (rope[0][:S], rope[1][:S])
+        for layer, c in zip(self.layers, cache):
+            x = layer(x, B, S, rope_s, self.impl, cache=c, pos=0)
+        return self._logits(x.view(B, S, -1)[:, -1])
+
+    @torch.no_grad()
+    def decode_step(self, token: torch.Tensor, cache, pos: int) -> torch.Tensor:
+        """One new token per sequence at position ``pos``; returns its logits ``[B, vocab]``."""
+        B = token.shape[0]
+        x = self.embed(token.view(B)).contiguous()
+        cos, sin = self.rope(cache[0][0].shape[1], x.device)
+        rope_p = (cos[pos:pos + 1].contiguous(), sin[pos:pos + 1].contiguous())
+        for layer, c in zip(self.layers, cache):
+            x = layer(x, B, 1, rope_p, self.impl, cache=c, pos=pos)
+        return self._logits(x)
+
+    @torch.no_grad()
+    def generate(self, tokens: torch.Tensor, max_new: int) -> torch.Tensor:
+        """Greedy continuation ``[B, max_new]`` with a KV cache."""
+        B, S = tokens.shape
+        cache = self.new_cache(B, S + max_new, tokens.device)
+        logits = self.prefill(tokens, cache)
+        out = []
+        for i in range(max_new):
+            nxt = logits.argmax(-1)
+            out.append(nxt)
+            if i + 1 < max_new:
+                logits = self.decode_step(nxt, cache, S + i)
+        return torch.stack(out, dim=1)
 
 
 def init_llama_params_(model: nn.Module, seed: int = 0, std: float = 0.02) -> None:

@@ -50,3 +50,25 @@ def test_llama_fused_matches_torch():
         b = m(tokens).float()
     assert native.device_error(reset=True) == 0
     assert float((a - b).abs().max() / b.abs().max()) < 5e-2
+
+
+def test_kv_cache_decode_matches_recompute():
+    cfg = tiny_llama(n_layers=2)
+    m = LlamaModel(cfg, impl="fused").to(DEV)
+    init_llama_params_(m, seed=1)
+    m = m.to(torch.bfloat16)
+    B, S, new = 3, 100, 5
+    tokens = torch.randint(0, cfg.vocab, (B, S), device=DEV, generator=torch.Generator(device=DEV).manual_seed(4))
+    with torch.no_grad():
+        cache = m.new_cache(B, S + new)
+        logits = m.prefill(tokens, cache)
+        seq = tokens
+        for i in range(new):
+            ref = m(seq).float()  # recompute over the whole sequence
+            assert float((logits.float() - ref).abs().max() / ref.abs().max()) < 3e-2, f"step {i}"
+            nxt = logits.argmax(-1)
+            seq = torch.cat([seq, nxt[:, None]], dim=1)
+            logits = m.decode_step(nxt, cache, S + i)
+    assert native.device_error(reset=True) == 0
+    out = m.generate(tokens, 4)
+    assert out.shape == (B, 4)
