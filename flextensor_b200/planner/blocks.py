@@ -28,22 +28,33 @@ from typing import Protocol
 class MemoryBlockPlanner:
     """Path-graph colouring of labels (execution order) onto slots."""
 
-    def __init__(self, layer_sizes: "OrderedDict[str, int] | dict[str, int]"):
+    def __init__(self, layer_sizes: "OrderedDict[str, int] | dict[str, int]", cyclic: bool = False):
+        """``cyclic``: the schedule wraps across forwards (the last transfer label feeds the first
+        compute label of the next forward), so the first and last labels are adjacent too; an
+        odd number of labels then needs three slots."""
         self.layer_sizes = OrderedDict(layer_sizes)
         self.layers = list(self.layer_sizes)
+        self.cyclic = cyclic and len(self.layers) > 2
 
     def _neighbours(self, idx: int) -> set[str]:
         out = set()
+        n = len(self.layers)
         if idx > 0:
             out.add(self.layers[idx - 1])
-        if idx + 1 < len(self.layers):
+        elif self.cyclic:
+            out.add(self.layers[-1])
+        if idx + 1 < n:
             out.add(self.layers[idx + 1])
+        elif self.cyclic:
+            out.add(self.layers[0])
         return out
 
     def find_minimum_blocks_sequential(self) -> int:
         if not self.layers:
             return 0
-        return 1 if len(self.layers) == 1 else 2
+        if len(self.layers) == 1:
+            return 1
+        return 3 if self.cyclic and len(self.layers) % 2 else 2
 
     def optimize_block_distribution(self, num_blocks: int) -> dict[int, list[str]]:
         """Balanced colouring with ``num_blocks`` slots (fewest-labels slot first)."""

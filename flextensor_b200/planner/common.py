@@ -111,8 +111,12 @@ def build_block_data(
     if not sizes:
         return BlockStrategyData({}, {}, {}, {}, {})
     order = list(sizes)
+    t2c = calculate_transfer_to_compute_map(layer_stats, strategy_map)
+    pos = {l.label: i for i, l in enumerate(layer_stats)}
+    cyclic = any(pos[t2c[t]] <= pos[t] for t in order if t in t2c and t2c[t] in pos)  # schedule wraps
     if assignment is None:
-        alloc = MemoryBlockPlanner(sizes).optimize_block_distribution(max(2, n_blocks))
+        planner = MemoryBlockPlanner(sizes, cyclic=cyclic)
+        alloc = planner.optimize_block_distribution(max(planner.find_minimum_blocks_sequential(), n_blocks))
         where = {l: b for b, ls in alloc.items() for l in ls}
     elif isinstance(assignment, StrictRoundRobinAssignment):
         where = assignment.assign(sizes, n_blocks)
@@ -120,7 +124,6 @@ def build_block_data(
         where = assignment.assign(sizes, n_blocks)
     alloc = allocation_from_assignment(order, where)
     block_sizes = {b: max(sizes[l] for l in ls) for b, ls in alloc.items()}
-    t2c = calculate_transfer_to_compute_map(layer_stats, strategy_map)
     return BlockStrategyData(
         label_to_size_map=dict(sizes),
         allocation_ordered=alloc,
