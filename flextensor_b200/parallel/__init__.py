@@ -1,5 +1,10 @@
-"""Multi-GPU data plane: symmetric peer heaps, striped host streaming, NCCL helpers."""
+"""Multi-GPU data plane on one node: symmetric peer heaps, striped host streaming, context /
+tensor / expert parallelism with the collectives fused into the kernels, NCCL baselines, and a
+bounded CPU control plane."""
 
+from flextensor_b200.parallel.control import ControlPlane, ReplicaFatalError
+from flextensor_b200.parallel.cp import ContextParallel, UlyssesAttention
+from flextensor_b200.parallel.ep import ExpertParallel, NcclExpertParallel, route_topk
 from flextensor_b200.parallel.striped import (
     StripedTransferEngine,
     disable_striped_streaming,
@@ -7,6 +12,8 @@ from flextensor_b200.parallel.striped import (
     striping_group,
 )
 from flextensor_b200.parallel.symm import SymmetricHeap
+from flextensor_b200.parallel.tp import NcclTP, TPAllGather, TPReduceScatter
 
-__all__ = ["StripedTransferEngine", "SymmetricHeap", "disable_striped_streaming", "enable_striped_streaming",
-           "striping_group"]
+__all__ = ["ContextParallel", "ControlPlane", "ExpertParallel", "NcclExpertParallel", "NcclTP", "ReplicaFatalError",
+           "StripedTransferEngine", "SymmetricHeap", "TPAllGather", "TPReduceScatter", "UlyssesAttention",
+           "disable_striped_streaming", "enable_striped_streaming", "route_topk", "striping_group"]
