@@ -33,6 +33,7 @@ from flextensor_b200.contrib.vllm.patterns import resolve_vllm_patterns
 LOGGER = logging.getLogger("vllm.flextensor_b200.worker")
 MANAGER_NAME = "vllm"
 _register_env_var("FT_VLLM_USE_V2_WORKER")
+_register_env_var("FT_VLLM_REPLAN_AFTER")
 
 from vllm.v1.worker.gpu_worker import Worker  # noqa: E402
 
@@ -53,6 +54,40 @@ def _validate(vllm_config, cfg) -> None:
 
 
 class FlexTensorOffloadWorker(Worker):
+    """Production profile refresh: the first plan comes from estimated layer times (or a saved
+    profile); after ``FT_VLLM_REPLAN_AFTER`` model steps (default 64, 0 = never) the worker asks
+    the manager for a strategy replan, whose warm / measure tail times the next real batches
+    per trap and rebuilds the plan from those compute times; the refreshed plan is saved to
+    ``profile_storage_dir`` when one is configured and writable."""
+
+    _ft_steps = 0
+    _ft_replan_after = None
+
+    def execute_model(self, scheduler_output):
+        out = super().execute_model(scheduler_output)
+        om = getattr(self, "_ft_manager", None)
+        if om is None:
+            return out
+        if self._ft_replan_after is None:
+            self._ft_replan_after = int(os.environ.get("FT_VLLM_REPLAN_AFTER", "64"))
+        self._ft_steps += 1
+        st = om.strategy_replan_status
+        if self._ft_replan_after and self._ft_steps == self._ft_replan_after and st.can_request:
+            try:
+                om.request_strategy_replan()
+                LOGGER.info("FlexTensor: profile refresh armed after %d steps", self._ft_steps)
+            except Exception:  # noqa: BLE001 - a refresh is an optimisation, never fatal
+                LOGGER.warning("FlexTensor: profile refresh could not start", exc_info=True)
+        elif st.state == "done" and st.applied and not getattr(self, "_ft_saved", False):
+            self._ft_saved = True
+            cfg = om.config
+            if cfg.profile_storage_dir and not cfg.profile_read_only:
+                try:
+                    om.save_profile(cfg.profile_storage_dir)
+                except Exception:  # noqa: BLE001
+                    LOGGER.warning("FlexTensor: saving the refreshed profile failed", exc_info=True)
+        return out
+
     def load_model(self, *args, **kwargs) -> None:
         if self.device.index is None:
             raise FlexTensorWorkerError(f"worker device needs an explicit index, got {self.device}")
@@ -97,6 +132,7 @@ class FlexTensorOffloadWorker(Worker):
             else:
                 om.offload_static(raw, cfg)
             boot.manager = om
+            self._ft_manager = om
             self.model_runner.model_memory_usage += torch.cuda.memory_allocated(self.device) - before
             LOGGER.info("FlexTensor took over %s: %.2f GB staged on host, ring slots %.2f GB",
                         type(raw).__name__, boot.staged_bytes / 1e9,
