@@ -97,6 +97,18 @@ class ContextParallel:
                             flag_stride=N_SLOTS, peer_acks=acks, rank=self.rank, shard_rows=self.shard,
                             epoch=epoch, counters=self.counters, scale=scale, out=out)
 
+    def gather_kv_attention(self, q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
+                            scale: float | None = None) -> torch.Tensor:
+        """Cross-attention of any queries ``q [1, Sq, Hq, 128]`` (e.g. replicated audio tokens)
+        over keys/values that are sharded by sequence across the ranks (e.g. the video tokens):
+        each rank contributes ``k_local / v_local [shard, kv_dim]`` and the fused kernel gathers
+        the rest (the reference's gather-KV cross-attention, without an NCCL all-gather)."""
+        kr, vr = self.begin()
+        kr.copy_(k_local.reshape(self.shard, self.kv_dim))
+        vr.copy_(v_local.reshape(self.shard, self.kv_dim))
+        self.publish()
+        return self.attention(q, scale=scale)
+
     def gather_sequence(self, x_local: torch.Tensor) -> torch.Tensor:
         """All-gather ``[B, shard, C]`` -> ``[B, S, C]`` (small tensors after the output head)."""
         import torch.distributed as dist
