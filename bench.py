@@ -252,6 +252,8 @@ def import_arm(impl: str):
         os.environ.setdefault("DISABLE_BEARTYPE", "1")
         import flextensor as ft  # noqa: PLC0415
 
+        if os.path.abspath(ref) not in os.path.abspath(ft.__file__):  # never our compatibility facade
+            return None, f"'import flextensor' resolved to {ft.__file__}, not baseline/_ref"
         return ft, None
     sys.path.insert(0, ROOT)
     import flextensor_b200 as ft  # noqa: PLC0415

@@ -26,3 +26,14 @@ def test_models_use_existing_ops():
                 used.add((path.name, node.attr))
     bad = [(f, a) for f, a in used if not hasattr(ops, a)]
     assert not bad, f"calls to missing ops: {bad}"
+
+
+def test_flextensor_facade():
+    import flextensor
+    import flextensor_b200
+
+    assert set(flextensor.__all__) == set(flextensor_b200.__all__)
+    assert flextensor.offload is flextensor_b200.offload
+    from flextensor.config import OffloadConfig
+
+    assert OffloadConfig is flextensor_b200.OffloadConfig
