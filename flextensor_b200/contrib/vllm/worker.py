@@ -37,6 +37,13 @@ _register_env_var("FT_VLLM_REPLAN_AFTER")
 
 from vllm.v1.worker.gpu_worker import Worker  # noqa: E402
 
+_selector = os.environ.get("FT_VLLM_USE_V2_WORKER", "1")
+if _selector not in ("0", "1"):
+    raise ValueError(f"FT_VLLM_USE_V2_WORKER must be '0' (legacy) or '1' (v2), got {_selector!r}")
+if _selector == "0":
+    LOGGER.warning("FT_VLLM_USE_V2_WORKER=0: there is no separate legacy worker in flextensor_b200; the "
+                   "state-takeover worker serves both settings")
+
 
 class FlexTensorWorkerError(RuntimeError):
     pass
