@@ -302,7 +302,17 @@ __device__ void cp_gather(SmemCP& sm, const CpArgs& c) {
   if (ok && pend_p >= 0) finish(pend_p);
 }
 
-template <bool CP>
+// EMU: how many of every 8 exp2 pairs run on the FMA pipe (exp2_fma) instead of MUFU.
+template <int EMU>
+__device__ __forceinline__ bool emu_pair(int i) {
+  const int k = i & 7;
+  if constexpr (EMU == 2) return k == 2 || k == 6;
+  if constexpr (EMU == 4) return (k & 1) == 1;
+  if constexpr (EMU == 1) return k == 5;
+  return k == 2 || k == 5 || k == 7;  // 3 pairs in 8
+}
+
+template <bool CP, int EMU = 3>
 __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnArgs a, const __grid_constant__ CpArgs cp) {
@@ -581,7 +591,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
           float x0, x1;
           f2unpack(x2, x0, x1);
           float p0, p1;
-          if ((i & 7) == 2 || (i & 7) == 5 || (i & 7) == 7) {  // 3 pairs in 8 on the FMA pipe
+          if (emu_pair<EMU>(i)) {  // EMU pairs in 8 on the FMA pipe
             p0 = exp2_fma(x0);
             p1 = exp2_fma(x1);
           } else {
@@ -704,17 +714,36 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
   a.diag = p.diag_mode;
   a.trace = reinterpret_cast<unsigned long long*>(p.trace);
   const int smem = (int)sizeof(SmemBase) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
   const long long grid = (long long)a.n_qblocks * p.Hq * p.B;
   if (grid > 0x7fffffff) return cudaErrorInvalidValue;
   CpArgs none{};
-  attn_fwd_kernel<false><<<(int)grid, NTHREADS, smem, stream>>>(tq, tk, tv, a, none);
-  return cudaGetLastError();
+  // diag_mode 101..104 (timing experiments only): run with that many exp2 pairs in 8 on the FMA pipe
+  const int emu = (p.diag_mode >= 101 && p.diag_mode <= 104) ? p.diag_mode - 100 : 3;
+  if (emu != 3) a.diag = 0;
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<(int)grid, NTHREADS, smem, stream>>>(tq, tk, tv, a, none);
+    return cudaGetLastError();
+  };
+  switch (emu) {
+    case 1:
+      return go(attn_fwd_kernel<false, 1>);
+    case 2:
+      return go(attn_fwd_kernel<false, 2>);
+    case 4:
+      return go(attn_fwd_kernel<false, 4>);
+    default: {
+      static bool attr = false;
+      if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+      }
+      attn_fwd_kernel<false, 3><<<(int)grid, NTHREADS, smem, stream>>>(tq, tk, tv, a, none);
+      return cudaGetLastError();
+    }
+  }
 }
 
 cudaError_t attention_cp_fwd(const AttnProblem& p, const AttnCpProblem& c, cudaStream_t stream) {
