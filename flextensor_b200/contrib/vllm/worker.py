@@ -34,6 +34,7 @@ LOGGER = logging.getLogger("vllm.flextensor_b200.worker")
 MANAGER_NAME = "vllm"
 _register_env_var("FT_VLLM_USE_V2_WORKER")
 _register_env_var("FT_VLLM_REPLAN_AFTER")
+_register_env_var("FT_VLLM_FUSED_TP")
 
 from vllm.v1.worker.gpu_worker import Worker  # noqa: E402
 
@@ -95,12 +96,33 @@ class FlexTensorOffloadWorker(Worker):
                     LOGGER.warning("FlexTensor: saving the refreshed profile failed", exc_info=True)
         return out
 
+    def _maybe_fuse_tp(self) -> None:
+        """``FT_VLLM_FUSED_TP=1``: fused GEMM + all-reduce for the row-parallel layers (eager mode)."""
+        if os.environ.get("FT_VLLM_FUSED_TP", "0") != "1":
+            return
+        par = self.vllm_config.parallel_config
+        if par.tensor_parallel_size <= 1:
+            return
+        from vllm.config import CUDAGraphMode
+
+        comp = self.vllm_config.compilation_config
+        if comp.cudagraph_mode is not None and comp.cudagraph_mode != CUDAGraphMode.NONE:
+            LOGGER.warning("FT_VLLM_FUSED_TP needs eager execution (enforce_eager); keeping vLLM's all-reduce")
+            return
+        from vllm.distributed.parallel_state import get_tp_group
+
+        from flextensor_b200.contrib.vllm.tp_patch import patch_row_parallel
+
+        max_rows = self.vllm_config.scheduler_config.max_num_batched_tokens
+        patch_row_parallel(self.model_runner.get_model(), max_rows, get_tp_group().cpu_group)
+
     def load_model(self, *args, **kwargs) -> None:
         if self.device.index is None:
             raise FlexTensorWorkerError(f"worker device needs an explicit index, got {self.device}")
         cfg = load_config(gpu_device=self.device.index)
         if not cfg.enabled:
             super().load_model(*args, **kwargs)
+            self._maybe_fuse_tp()
             return
         if kwargs.get("load_dummy_weights"):
             raise FlexTensorWorkerError("load_dummy_weights=True is not supported")
@@ -141,6 +163,7 @@ class FlexTensorOffloadWorker(Worker):
             boot.manager = om
             self._ft_manager = om
             self.model_runner.model_memory_usage += torch.cuda.memory_allocated(self.device) - before
+            self._maybe_fuse_tp()
             LOGGER.info("FlexTensor took over %s: %.2f GB staged on host, ring slots %.2f GB",
                         type(raw).__name__, boot.staged_bytes / 1e9,
                         om.get_gpu_memory_usage().blocks_bytes / 1e9)

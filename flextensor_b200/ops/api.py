@@ -162,10 +162,14 @@ def tp_gemm_reducescatter(a: torch.Tensor, weight: torch.Tensor, *, stage: list[
 
 
 def tp_reduce(stage: torch.Tensor, world: int, rows: int, out: torch.Tensor, *, flags_ptr: int, flag_stride: int,
-              epoch: int, peer_acks: list[int], rank: int, residual: torch.Tensor | None = None) -> torch.Tensor:
-    """Owner side: ``out = residual + sum of the world partial rows`` once every sender flagged."""
+              epoch: int, peer_acks: list[int], rank: int, residual: torch.Tensor | None = None,
+              out_peers: list[int] | None = None, row_base: int = 0, stage_rows: int = 0) -> torch.Tensor:
+    """Owner side: ``out = residual + sum of the world partial rows`` once every sender flagged.
+    ``out_peers`` (all-reduce): write the reduced rows at ``row_base`` of every rank's output
+    instead; the acknowledgements that follow also certify that the rows arrived."""
     native.lib().tp_reduce(stage, int(world), int(rows), out, residual, int(flags_ptr), int(flag_stride), int(epoch),
-                           [int(p) for p in peer_acks], int(rank))
+                           [int(p) for p in peer_acks], int(rank), [int(p) for p in (out_peers or [])],
+                           int(row_base), int(stage_rows))
     _count(2)
     return out
 

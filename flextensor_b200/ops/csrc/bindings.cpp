@@ -354,7 +354,8 @@ void tp_gemm_rs(const Tensor& a, const Tensor& w, std::vector<uint64_t> stage, s
 }
 
 void tp_reduce(const Tensor& stage, int64_t world, int64_t rows, Tensor& out, const c10::optional<Tensor>& residual,
-               uint64_t flags, int64_t flag_stride, uint64_t epoch, std::vector<uint64_t> peer_acks, int64_t rank) {
+               uint64_t flags, int64_t flag_stride, uint64_t epoch, std::vector<uint64_t> peer_acks, int64_t rank,
+               std::vector<uint64_t> out_peers, int64_t row_base, int64_t stage_rows) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "out");
   c10::cuda::CUDAGuard g(out.device());
   ft::TpReduceProblem r;
@@ -375,6 +376,13 @@ void tp_reduce(const Tensor& stage, int64_t world, int64_t rows, Tensor& out, co
   r.epoch = epoch;
   TORCH_CHECK((int)peer_acks.size() == r.world, "one ack pointer per rank");
   for (int q = 0; q < r.world; q++) r.peer_acks[q] = reinterpret_cast<uint64_t*>(peer_acks[q]);
+  r.stage_rows = (int)stage_rows;
+  if (!out_peers.empty()) {
+    TORCH_CHECK((int)out_peers.size() == r.world, "one output pointer per rank");
+    for (int q = 0; q < r.world; q++) r.out_peers[q] = reinterpret_cast<void*>(out_peers[q]);
+    r.out_peers_n = r.world;
+    r.row_base = row_base;
+  }
   check_ok(ft::tp_reduce(r, at::cuda::getCurrentCUDAStream()), "tp_reduce");
 }
 
@@ -572,7 +580,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_publish_raw", &p2p_publish_raw);
   m.def("tp_ag_gemm", &tp_ag_gemm);
   m.def("tp_gemm_rs", &tp_gemm_rs);
-  m.def("tp_reduce", &tp_reduce);
+  m.def("tp_reduce", &tp_reduce, py::arg("stage"), py::arg("world"), py::arg("rows"), py::arg("out"),
+        py::arg("residual"), py::arg("flags"), py::arg("flag_stride"), py::arg("epoch"), py::arg("peer_acks"),
+        py::arg("rank"), py::arg("out_peers") = std::vector<uint64_t>{}, py::arg("row_base") = 0,
+        py::arg("stage_rows") = 0);
   m.def("moe_gemm", &moe_gemm);
   m.def("moe_reduce", &moe_reduce);
   m.def("p2p_wait_acks_raw", &p2p_wait_acks_raw);

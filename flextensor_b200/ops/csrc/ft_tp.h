@@ -49,6 +49,12 @@ struct TpReduceProblem {
   int flag_stride = 1;
   uint64_t epoch = 0;
   uint64_t* peer_acks[kTpMaxRanks] = {}; // word telling rank q its slot in our staging is free
+  int stage_rows = 0;                    // row stride of the staging slots (0: = rows)
+  // all-reduce: write the reduced rows to every rank's output at row_base (instead of `out`);
+  // the acknowledgements that follow then also mean "my rows are in your output"
+  void* out_peers[kTpMaxRanks] = {};
+  int out_peers_n = 0;
+  long long row_base = 0;
 };
 
 cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream);

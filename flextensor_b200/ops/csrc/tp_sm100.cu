@@ -417,9 +417,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // Owner side of the reduce-scatter: out[r] = (residual[r] +) sum_src stage[src][r], fp32 sum.
+struct OutList {
+  __nv_bfloat16* ptr[kTpMaxRanks];  // every rank's output buffer (all-reduce broadcast), or ptr[0] only
+  int n;
+};
+
 __global__ void __launch_bounds__(256)
-    tp_reduce_kernel(const __nv_bfloat16* stage, int world, int rows, int N, const __nv_bfloat16* residual,
-                     int ldr, __nv_bfloat16* out, int ldo, const uint64_t* flags, int flag_stride, uint64_t epoch) {
+    tp_reduce_kernel(const __nv_bfloat16* stage, int world, int rows, int stage_rows, int N,
+                     const __nv_bfloat16* residual, int ldr, OutList outs, long long row_base, int ldo,
+                     const uint64_t* flags, int flag_stride, uint64_t epoch) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
@@ -443,7 +449,7 @@ __global__ void __launch_bounds__(256)
       for (int e = 0; e < 8; e++) acc[e] = 0.f;
     }
     for (int s = 0; s < world; s++) {
-      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(stage + ((size_t)s * rows + r) * N + c));
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(stage + ((size_t)s * stage_rows + r) * N + c));
       const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
       for (int e = 0; e < 8; e++) acc[e] += __bfloat162float(b[e]);
@@ -453,7 +459,8 @@ __global__ void __launch_bounds__(256)
     o.y = pack_bf16x2(acc[2], acc[3]);
     o.z = pack_bf16x2(acc[4], acc[5]);
     o.w = pack_bf16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(out + (size_t)r * ldo + c) = o;
+    for (int q = 0; q < outs.n; q++)  // local output, or this owner's rows into every rank's output
+      *reinterpret_cast<uint4*>(outs.ptr[q] + (size_t)(row_base + r) * ldo + c) = o;
   }
 }
 
@@ -489,11 +496,13 @@ cudaError_t launch(const TpArgs& a, const CUtensorMap& tA, const CUtensorMap& tB
 
 }  // namespace
 
-static cudaError_t fill_common(const TpGemmProblem& g, TpArgs& a, int bn) {
+static cudaError_t fill_common(const TpGemmProblem& g, TpArgs& a, int bn, bool even_rows) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaErrorInvalidValue;
   if (g.K % 8 || g.N % 32 || g.world < 1 || g.world > kTpMaxRanks || g.rank < 0 || g.rank >= g.world)
     return cudaErrorInvalidValue;
-  if (g.M % g.world) return cudaErrorInvalidValue;
+  // all-gather: every rank owns exactly M / world rows; reduce-scatter: rank p owns rows
+  // [p*R, min((p+1)*R, M)) with R = ceil(M / world) (the last owners may hold fewer)
+  if (even_rows && g.M % g.world) return cudaErrorInvalidValue;
   a.M = g.M;
   a.N = g.N;
   a.K = g.K;
@@ -504,7 +513,7 @@ static cudaError_t fill_common(const TpGemmProblem& g, TpArgs& a, int bn) {
   a.bias = g.bias;
   a.rank = g.rank;
   a.world = g.world;
-  a.rows = g.M / g.world;
+  a.rows = (g.M + g.world - 1) / g.world;
   a.epoch = g.epoch;
   a.flags = g.flags;
   a.flag_stride = g.flag_stride;
@@ -515,7 +524,7 @@ static cudaError_t fill_common(const TpGemmProblem& g, TpArgs& a, int bn) {
 cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream) {
   TpArgs a{};
   const int bn = g.N >= 256 ? 256 : 128;
-  cudaError_t e = fill_common(g, a, bn);
+  cudaError_t e = fill_common(g, a, bn, true);
   if (e != cudaSuccess) return e;
   if (g.counters == nullptr || g.C == nullptr || g.flags == nullptr) return cudaErrorInvalidValue;
   if (g.epi == TP_EPI_SWIGLU && g.N % 64) return cudaErrorInvalidValue;
@@ -546,7 +555,7 @@ cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream) {
 cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream) {
   TpArgs a{};
   const int bn = g.N >= 256 ? 256 : 128;
-  cudaError_t e = fill_common(g, a, bn);
+  cudaError_t e = fill_common(g, a, bn, false);
   if (e != cudaSuccess) return e;
   if (g.counters == nullptr || g.epi == TP_EPI_SWIGLU) return cudaErrorInvalidValue;
   for (int r = 0; r < g.world; r++) {
@@ -567,17 +576,31 @@ cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream) {
 }
 
 cudaError_t tp_reduce(const TpReduceProblem& r, cudaStream_t stream) {
-  if (r.world < 1 || r.world > kTpMaxRanks || r.N % 8 || r.rows <= 0 || r.stage == nullptr || r.out == nullptr ||
-      r.flags == nullptr)
+  if (r.world < 1 || r.world > kTpMaxRanks || r.N % 8 || r.rows < 0 || r.stage == nullptr || r.flags == nullptr)
     return cudaErrorInvalidValue;
+  OutList outs{};
+  long long row_base = 0;
+  if (r.out_peers_n > 0) {  // all-reduce: broadcast this owner's reduced rows to every rank
+    if (r.out_peers_n != r.world) return cudaErrorInvalidValue;
+    outs.n = r.world;
+    for (int q = 0; q < r.world; q++) {
+      if (r.out_peers[q] == nullptr) return cudaErrorInvalidValue;
+      outs.ptr[q] = static_cast<__nv_bfloat16*>(r.out_peers[q]);
+    }
+    row_base = r.row_base;
+  } else {
+    if (r.out == nullptr) return cudaErrorInvalidValue;
+    outs.n = 1;
+    outs.ptr[0] = static_cast<__nv_bfloat16*>(r.out);
+  }
+  const int stage_rows = r.stage_rows > 0 ? r.stage_rows : r.rows;
   const long long work = (long long)r.rows * (r.N / 8);
   int grid = (int)((work + 255) / 256);
   if (grid > 4 * 148) grid = 4 * 148;
   if (grid < 1) grid = 1;
-  tp_reduce_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(r.stage), r.world, r.rows, r.N,
-                                             static_cast<const __nv_bfloat16*>(r.residual), r.ldr,
-                                             static_cast<__nv_bfloat16*>(r.out), r.ldo, r.flags, r.flag_stride,
-                                             r.epoch);
+  tp_reduce_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(r.stage), r.world, r.rows, stage_rows,
+                                             r.N, static_cast<const __nv_bfloat16*>(r.residual), r.ldr, outs,
+                                             row_base, r.ldo, r.flags, r.flag_stride, r.epoch);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   AckList a{};

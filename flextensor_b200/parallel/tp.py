@@ -143,6 +143,66 @@ class TPReduceScatter:
         _close(self)
 
 
+class TPAllReduce:
+    """GEMM + all-reduce for row-parallel layers whose output is replicated (no sequence
+    parallelism, e.g. vLLM's ``RowParallelLinear``): the partial rows go to their owners from the
+    GEMM epilogue (reduce-scatter), each owner sums its rows and writes them into every rank's
+    output buffer, and each rank waits for every owner's acknowledgement. Row counts may vary
+    per call up to ``max_rows``; outputs are views of a double-buffered heap slot that stays
+    valid until two calls later."""
+
+    def __init__(self, max_rows: int, n: int, group=None, device: int | None = None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.max_rows, self.N = max_rows, n
+        self.R_max = (max_rows + self.world - 1) // self.world
+        dev = torch.cuda.current_device() if device is None else device
+        hdr = 4096
+        self.stage_bytes = (self.world * self.R_max * n * 2 + 4095) // 4096 * 4096
+        self.out_bytes = (max_rows * n * 2 + 4095) // 4096 * 4096
+        slot = self.stage_bytes + self.out_bytes
+        self.heap = SymmetricHeap(hdr + N_SLOTS * slot, group, dev)
+        self.f = _Flags(self.heap, self.world)
+        self.stage_off = [hdr + s * slot for s in range(N_SLOTS)]
+        self.out_off = [hdr + s * slot + self.stage_bytes for s in range(N_SLOTS)]
+        self.counters = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+        self.epochs = [0] * N_SLOTS
+        self.calls = 0
+        dist.barrier(group=group)
+
+    def __call__(self, a: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        from flextensor_b200.ops.api import tp_gemm_reducescatter, tp_reduce
+
+        M = a.shape[0]
+        if M > self.max_rows or weight.shape[0] != self.N:
+            raise ValueError(f"TPAllReduce sized for {self.max_rows} x {self.N}, got {M} x {weight.shape[0]}")
+        W, lib = self.world, native.lib()
+        R = (M + W - 1) // W
+        slot = self.calls % N_SLOTS
+        self.calls += 1
+        self.epochs[slot] += 1
+        e = self.epochs[slot]
+        if e > 1:
+            lib.p2p_wait_acks_raw(self.f.flags, self.f.acks, self.rank, N_SLOTS, slot, e - 1)
+        P = self.heap.ptrs
+        tp_gemm_reducescatter(a, weight, stage=[p + self.stage_off[slot] for p in P],
+                              peer_flags=[self.f.flags[p] + (self.rank * N_SLOTS + slot) * 8 for p in range(W)],
+                              rank=self.rank, epoch=e, counters=self.counters)
+        stage = self.heap.view(self.stage_off[slot], W * R * self.N * 2).view(torch.bfloat16).view(W, R, self.N)
+        out = self.heap.view(self.out_off[slot], M * self.N * 2).view(torch.bfloat16).view(M, self.N)
+        rows = max(0, min(R, M - self.rank * R))
+        tp_reduce(stage, W, rows, out, flags_ptr=self.f.flags[self.rank] + slot * 8, flag_stride=N_SLOTS, epoch=e,
+                  peer_acks=[self.f.acks[q] + (self.rank * N_SLOTS + slot) * 8 for q in range(W)], rank=self.rank,
+                  out_peers=[p + self.out_off[slot] for p in P], row_base=self.rank * R, stage_rows=R)
+        lib.p2p_wait_acks_raw(self.f.flags, self.f.acks, self.rank, N_SLOTS, slot, e)  # every owner's rows are in
+        return out
+
+    def close(self) -> None:
+        _close(self)
+
+
 def _close(obj) -> None:
     import torch.distributed as dist
 

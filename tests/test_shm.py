@@ -117,7 +117,7 @@ def test_creator_death_detected():
     t0 = time.monotonic()
     got = _run("hang", follower_timeout=30.0, kill_after=0.5)
     assert got == [("role", False), ("error", "ShmCreatorDiedError")]
-    assert time.monotonic() - t0 < 20
+    assert time.monotonic() - t0 < 28  # below the 30 s follower timeout: death, not timeout (spawn start-up is slow under load)
 
 
 def test_follower_timeout():

@@ -90,3 +90,34 @@ def test_gemm_reducescatter(W, R, K, N):
             for q in range(W):
                 if q != p:
                     assert int(acks[q][p]) == epoch
+
+
+@pytest.mark.parametrize("W,M,K,N", [(2, 37, 256, 256), (4, 300, 128, 512), (8, 5, 128, 256), (3, 3, 64, 256)])
+def test_gemm_allreduce_uneven_rows(W, M, K, N):
+    """GEMM -> reduce-scatter -> owner reduce broadcast into every rank's output (all-reduce),
+    with row counts that do not divide evenly (some owners hold fewer or no rows)."""
+    R = (M + W - 1) // W
+    g = torch.Generator(device=DEV).manual_seed(W * 7 + M)
+    a = [torch.randn(M, K, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    w = [(torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16() for _ in range(W)]
+    stage = [torch.zeros(W, R, N, device=DEV, dtype=torch.bfloat16) for _ in range(W)]
+    outs = [torch.zeros(M, N, device=DEV, dtype=torch.bfloat16) for _ in range(W)]
+    flags = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    counters = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for r in range(W):
+        ops.tp_gemm_reducescatter(a[r], w[r], stage=[s.data_ptr() for s in stage],
+                                  peer_flags=[f.data_ptr() + 8 * r for f in flags], rank=r, epoch=1, counters=counters)
+    for p in range(W):
+        rows = max(0, min(R, M - p * R))
+        ops.tp_reduce(stage[p], W, rows, outs[p], flags_ptr=flags[p].data_ptr(), flag_stride=1, epoch=1,
+                      peer_acks=[x.data_ptr() + 8 * p for x in acks], rank=p, out_peers=[o.data_ptr() for o in outs],
+                      row_base=p * R, stage_rows=R)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    full = sum(a[r].float() @ w[r].float().t() for r in range(W))
+    for q in range(W):
+        assert _rel(outs[q], full) < 2e-2, f"rank {q}'s all-reduced output"
+        for p in range(W):
+            if p != q:
+                assert int(acks[q][p]) == 1
