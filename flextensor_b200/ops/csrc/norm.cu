@@ -56,8 +56,39 @@ __device__ __forceinline__ float ldf(const void* p, int i, bool is_bf16) {
                  : reinterpret_cast<const float*>(p)[i];
 }
 
-// VPT = 8-element vectors per thread held in registers (D <= NT*8*VPT).
-template <int NT, int VPT>
+// Eight consecutive per-column parameters starting at column c (c % 8 == 0). VEC: the pointer is
+// 16-byte aligned, so one 16-byte load (bf16) or two (fp32) through the read-only path; otherwise
+// eight scalar loads.
+template <bool VEC>
+__device__ __forceinline__ void ldp8(const void* p, int c, bool is_bf16, float (&f)[8]) {
+  if constexpr (VEC) {
+    if (is_bf16) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + c));
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; e++) f[e] = __bfloat162float(b[e]);
+    } else {
+      const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + c);
+      const float4 lo = __ldg(q), hi = __ldg(q + 1);
+      f[0] = lo.x, f[1] = lo.y, f[2] = lo.z, f[3] = lo.w, f[4] = hi.x, f[5] = hi.y, f[6] = hi.z, f[7] = hi.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; e++) f[e] = ldf(p, c + e, is_bf16);
+  }
+}
+
+// Four consecutive fp32 values (RoPE cos/sin of four pairs).
+template <bool VEC>
+__device__ __forceinline__ float4 ld4f(const float* p) {
+  if constexpr (VEC) return __ldg(reinterpret_cast<const float4*>(p));
+  return make_float4(p[0], p[1], p[2], p[3]);
+}
+
+// VPT = 8-element vectors per thread held in registers (D <= NT*8*VPT). VEC = every per-column
+// parameter array is 16-byte aligned (vector loads; the parameter traffic is otherwise the
+// limiter of these HBM-bound kernels, not the row itself).
+template <int NT, int VPT, bool VEC>
 __global__ void __launch_bounds__(NT) ln_modulate_kernel(LnArgs a) {
   __shared__ float red[NT / 32];
   const int row = blockIdx.x;
@@ -96,22 +127,36 @@ __global__ void __launch_bounds__(NT) ln_modulate_kernel(LnArgs a) {
   for (int i = 0; i < VPT; i++) {
     const int vi = threadIdx.x + i * NT;
     if (vi < nvec) {
-      float o[8];
+      const int c0 = vi * 8;
+      float o[8], p[8];
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const int c = vi * 8 + e;
-        float t = (v[i][e] - mean) * rstd;
-        if (a.weight) t = t * ldf(a.weight, c, a.affine_bf16) + (a.bias ? ldf(a.bias, c, a.affine_bf16) : 0.f);
-        if (sc) t = t * (1.f + sc[c]);
-        if (sh) t = t + sh[c];
-        o[e] = t;
+      for (int e = 0; e < 8; e++) o[e] = (v[i][e] - mean) * rstd;
+      if (a.weight) {
+        ldp8<VEC>(a.weight, c0, a.affine_bf16, p);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] *= p[e];
       }
-      store8(y + vi * 8, o);
+      if (a.bias) {
+        ldp8<VEC>(a.bias, c0, a.affine_bf16, p);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] += p[e];
+      }
+      if (sc) {
+        ldp8<VEC>(sc, c0, false, p);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] = fmaf(o[e], p[e], o[e]);
+      }
+      if (sh) {
+        ldp8<VEC>(sh, c0, false, p);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] += p[e];
+      }
+      store8(y + c0, o);
     }
   }
 }
 
-template <int NT, int VPT>
+template <int NT, int VPT, bool VEC>
 __global__ void __launch_bounds__(NT) rmsnorm_kernel(RmsArgs a) {
   __shared__ float red[NT / 32];
   const int row = blockIdx.x;
@@ -130,48 +175,72 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(RmsArgs a) {
     }
   }
   const float r = a.no_norm ? 1.f : rsqrtf(block_sum<NT>(ss, red) / a.D + a.eps);
-  // optional rotary embedding on interleaved pairs, per head of size a.head_dim
+  // optional rotary embedding on interleaved pairs, per head of size a.head_dim (a multiple of 8,
+  // so one 8-element vector is four pairs of one head)
   const int pos = a.seq_len > 0 ? row % a.seq_len : 0;
+  const int half = a.head_dim / 2;
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
     const int vi = threadIdx.x + i * NT;
     if (vi < nvec) {
+      const int c0 = vi * 8;
       float o[8];
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const int c = vi * 8 + e;
-        o[e] = v[i][e] * r * (a.weight ? ldf(a.weight, c, a.weight_bf16) : 1.f);
+      for (int e = 0; e < 8; e++) o[e] = v[i][e] * r;
+      if (a.weight) {
+        float w[8];
+        ldp8<VEC>(a.weight, c0, a.weight_bf16, w);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] *= w[e];
       }
       if (a.cos != nullptr) {
+        const size_t t = (size_t)pos * half + (c0 % a.head_dim) / 2;
+        const float4 cs = ld4f<VEC>(a.cos + t), sn = ld4f<VEC>(a.sin + t);
+        const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int c = vi * 8 + e;
-          const int pair = (c % a.head_dim) >> 1;
-          const float cs = a.cos[(size_t)pos * (a.head_dim / 2) + pair];
-          const float sn = a.sin[(size_t)pos * (a.head_dim / 2) + pair];
-          const float re = o[e], im = o[e + 1];
-          o[e] = re * cs - im * sn;
-          o[e + 1] = re * sn + im * cs;
+        for (int q = 0; q < 4; q++) {
+          const float re = o[2 * q], im = o[2 * q + 1];
+          o[2 * q] = re * cv[q] - im * sv[q];
+          o[2 * q + 1] = re * sv[q] + im * cv[q];
         }
       }
-      store8(y + vi * 8, o);
+      store8(y + c0, o);
     }
   }
 }
 
-#define FT_LAUNCH_ROWS(KER, ARGS, ROWS, D, ST)                                           \
+// Launch shape: 128 threads and the fewest vectors per thread that cover the row (no idle lanes
+// at D = 5120: 640 vectors = 128 x 5), wider CTAs past 8192 columns. The scalar-parameter
+// variant keeps three shapes only.
+#define FT_LAUNCH_ROWS(KER, ARGS, ROWS, D, VEC, ST)                                      \
   do {                                                                                   \
     const int nvec = (D) / 8;                                                            \
-    if (nvec <= 128 * 4) KER<128, 4><<<(ROWS), 128, 0, (ST)>>>(ARGS);                    \
-    else if (nvec <= 256 * 4) KER<256, 4><<<(ROWS), 256, 0, (ST)>>>(ARGS);               \
-    else if (nvec <= 512 * 4) KER<512, 4><<<(ROWS), 512, 0, (ST)>>>(ARGS);               \
+    if (VEC && nvec <= 128 * 8) {                                                        \
+      switch ((nvec + 127) / 128) {                                                      \
+        case 1: KER<128, 1, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        case 2: KER<128, 2, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        case 3: KER<128, 3, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        case 4: KER<128, 4, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        case 5: KER<128, 5, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        case 6: KER<128, 6, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        case 7: KER<128, 7, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;                \
+        default: KER<128, 8, true><<<(ROWS), 128, 0, (ST)>>>(ARGS); break;               \
+      }                                                                                  \
+    } else if (VEC && nvec <= 256 * 8) KER<256, 8, true><<<(ROWS), 256, 0, (ST)>>>(ARGS);  \
+    else if (VEC && nvec <= 512 * 8) KER<512, 8, true><<<(ROWS), 512, 0, (ST)>>>(ARGS);    \
+    else if (nvec <= 128 * 4) KER<128, 4, false><<<(ROWS), 128, 0, (ST)>>>(ARGS);        \
+    else if (nvec <= 256 * 4) KER<256, 4, false><<<(ROWS), 256, 0, (ST)>>>(ARGS);        \
+    else if (nvec <= 512 * 8) KER<512, 8, false><<<(ROWS), 512, 0, (ST)>>>(ARGS);        \
     else return cudaErrorInvalidValue;                                                   \
   } while (0)
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 cudaError_t ln_modulate(const LnArgs& a, int rows, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   if (a.D % 8 || a.ldx % 8 || a.ldy % 8) return cudaErrorInvalidValue;
-  FT_LAUNCH_ROWS(ln_modulate_kernel, a, rows, a.D, st);
+  const bool vec = al16(a.weight) && al16(a.bias) && al16(a.scale) && al16(a.shift) && a.mod_stride % 4 == 0;
+  FT_LAUNCH_ROWS(ln_modulate_kernel, a, rows, a.D, vec, st);
   return cudaGetLastError();
 }
 
@@ -179,7 +248,8 @@ cudaError_t rmsnorm(const RmsArgs& a, int rows, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   if (a.D % 8 || a.ldx % 8 || a.ldy % 8) return cudaErrorInvalidValue;
   if (a.cos != nullptr && (a.head_dim % 8 || a.D % a.head_dim || a.seq_len <= 0)) return cudaErrorInvalidValue;
-  FT_LAUNCH_ROWS(rmsnorm_kernel, a, rows, a.D, st);
+  const bool vec = al16(a.weight) && al16(a.cos) && al16(a.sin);
+  FT_LAUNCH_ROWS(rmsnorm_kernel, a, rows, a.D, vec, st);
   return cudaGetLastError();
 }
 

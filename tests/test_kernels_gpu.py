@@ -115,6 +115,42 @@ def test_rmsnorm_and_rope():
     assert rel_err(y, rot) < 1e-2
 
 
+@pytest.mark.parametrize("D", [1000, 4096, 5120, 6144, 8192, 12288])
+def test_norm_vector_shapes_and_scalar_fallback(D):
+    """Every launch shape of the row kernels (1..8 vectors per thread at 128 threads, wider CTAs
+    past 8192 columns) with 16-byte-aligned parameters (vector loads), and the scalar-load
+    variant on parameters that start one element off a 16-byte boundary."""
+    torch.manual_seed(D)
+    M = 300
+    x = (torch.randn(M, D, device=DEV) * 2 + 0.5).bfloat16()
+    buf = torch.randn(4, D + 8, device=DEV) * 0.1
+    for off in (0, 1):
+        sc, sh = buf[0, off:off + D], buf[1, off:off + D]
+        ref = torch.nn.functional.layer_norm(x.float(), (D,), eps=1e-6) * (1 + sc) + sh
+        assert rel_err(ops.layernorm_modulate(x, sc, sh), ref) < 1e-2, off
+        wb = (buf[2] + 1).bfloat16()[off:off + D]
+        bb = buf[3].bfloat16()[off:off + D]
+        ref2 = torch.nn.functional.layer_norm(x.float(), (D,), wb.float(), bb.float(), eps=1e-6)
+        assert rel_err(ops.layernorm_modulate(x, weight=wb, bias=bb), ref2) < 1e-2, off
+        w = buf[2, off:off + D] + 1
+        ref3 = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w
+        assert rel_err(ops.rmsnorm(x, w), ref3) < 1e-2, off
+    if D % 128 == 0:
+        Dh, S = 128, M // 2
+        ang = torch.randn(S * Dh // 2 + 1, device=DEV)
+        w = buf[2, :D] + 1
+        for off in (0, 1):  # tables at a 16-byte boundary, and one float past it (scalar loads)
+            cos = ang.cos()[off:off + S * Dh // 2].view(S, Dh // 2)
+            sin = ang.sin()[off:off + S * Dh // 2].view(S, Dh // 2)
+            y = ops.qk_rmsnorm_rope(x, w, cos, sin, Dh, S)
+            r = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w)
+            r = r.view(2, S, D // Dh, Dh // 2, 2)
+            re, im = r[..., 0], r[..., 1]
+            c, s = cos[None, :, None, :], sin[None, :, None, :]
+            rot = torch.stack([re * c - im * s, re * s + im * c], -1).view(M, D)
+            assert rel_err(y, rot) < 1e-2, off
+
+
 def _attn_ref(q, k, v, causal=False):
     qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
     if kf.shape[1] != qf.shape[1]:
