@@ -16,8 +16,9 @@ from flextensor_b200.ops.api import (
     tp_allgather_gemm,
     tp_gemm_reducescatter,
     tp_reduce,
+    tp_rmsnorm,
 )
 
 __all__ = ["EPI", "TP_EPI", "attention", "attention_cp", "launch_count", "layernorm_modulate", "linear",
            "linear_swiglu", "qk_rmsnorm_rope", "rmsnorm", "rope", "tp_allgather_gemm", "tp_gemm_reducescatter",
-           "tp_reduce"]
+           "tp_reduce", "tp_rmsnorm"]

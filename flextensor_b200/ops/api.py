@@ -134,7 +134,7 @@ def attention_cp(q: torch.Tensor, kv_local: torch.Tensor, *, peer_kv: list[int],
     return out
 
 
-TP_EPI = {"none": 0, "bias": 1, "swiglu": 2}
+TP_EPI = {"none": 0, "bias": 1, "swiglu": 2, "gelu": 3}
 
 
 def tp_allgather_gemm(a_full: torch.Tensor, weight: torch.Tensor, *, peer_a: list[int], flags_ptr: int,
@@ -163,14 +163,38 @@ def tp_gemm_reducescatter(a: torch.Tensor, weight: torch.Tensor, *, stage: list[
 
 def tp_reduce(stage: torch.Tensor, world: int, rows: int, out: torch.Tensor, *, flags_ptr: int, flag_stride: int,
               epoch: int, peer_acks: list[int], rank: int, residual: torch.Tensor | None = None,
-              out_peers: list[int] | None = None, row_base: int = 0, stage_rows: int = 0) -> torch.Tensor:
-    """Owner side: ``out = residual + sum of the world partial rows`` once every sender flagged.
-    ``out_peers`` (all-reduce): write the reduced rows at ``row_base`` of every rank's output
-    instead; the acknowledgements that follow also certify that the rows arrived."""
+              out_peers: list[int] | None = None, row_base: int = 0, stage_rows: int = 0,
+              bias: torch.Tensor | None = None, gate: torch.Tensor | None = None, gate_rows: int = 0,
+              grow0: int = 0) -> torch.Tensor:
+    """Owner side: ``out = residual + gate * (sum of the world partial rows + bias)`` once every
+    sender flagged (``gate``: fp32 ``[groups, N]``, one row per ``gate_rows`` global rows, the
+    first owned row being global row ``grow0``). ``out_peers`` (all-reduce): write the reduced
+    rows at ``row_base`` of every rank's output instead; the acknowledgements that follow also
+    certify that the rows arrived."""
     native.lib().tp_reduce(stage, int(world), int(rows), out, residual, int(flags_ptr), int(flag_stride), int(epoch),
                            [int(p) for p in peer_acks], int(rank), [int(p) for p in (out_peers or [])],
-                           int(row_base), int(stage_rows))
+                           int(row_base), int(stage_rows), bias, gate, int(gate_rows), int(grow0))
     _count(2)
+    return out
+
+
+def tp_rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, *, d_full: int, part_peers: list[int], stage_rows: int,
+               peer_flags: list[int], flags_ptr: int, flag_stride: int, peer_acks: list[int], rank: int, epoch: int,
+               counter: torch.Tensor, eps: float = 1e-6, cos: torch.Tensor | None = None,
+               sin: torch.Tensor | None = None, head_dim: int = 0, seq_len: int = 0,
+               out: torch.Tensor | None = None, _phases: int = 3) -> torch.Tensor:
+    """RMSNorm over a hidden dimension whose columns are split across tensor-parallel ranks:
+    per-row partial sums of squares go to every rank over peer stores, each rank then scales its
+    own columns (weight shard, optional interleaved-pair RoPE per head). ``_phases`` (tests that
+    emulate several ranks on one GPU): 1 = partial sums and publish only, 2 = wait and scale only."""
+    x2 = _2d(x)
+    if out is None:
+        out = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    native.lib().tp_rmsnorm(x2, _2d(out), weight, cos, sin, int(head_dim), int(seq_len), float(eps), int(d_full),
+                            [int(p) for p in part_peers], int(stage_rows), [int(p) for p in peer_flags],
+                            int(flags_ptr), int(flag_stride), [int(p) for p in peer_acks], int(rank), int(epoch),
+                            counter, int(_phases))
+    _count((1 if _phases & 1 else 0) + (2 if _phases & 2 else 0))
     return out
 
 

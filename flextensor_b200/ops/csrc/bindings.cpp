@@ -355,7 +355,8 @@ void tp_gemm_rs(const Tensor& a, const Tensor& w, std::vector<uint64_t> stage, s
 
 void tp_reduce(const Tensor& stage, int64_t world, int64_t rows, Tensor& out, const c10::optional<Tensor>& residual,
                uint64_t flags, int64_t flag_stride, uint64_t epoch, std::vector<uint64_t> peer_acks, int64_t rank,
-               std::vector<uint64_t> out_peers, int64_t row_base, int64_t stage_rows) {
+               std::vector<uint64_t> out_peers, int64_t row_base, int64_t stage_rows, const c10::optional<Tensor>& bias,
+               const c10::optional<Tensor>& gate, int64_t gate_rows, int64_t grow0) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "out");
   c10::cuda::CUDAGuard g(out.device());
   ft::TpReduceProblem r;
@@ -383,7 +384,75 @@ void tp_reduce(const Tensor& stage, int64_t world, int64_t rows, Tensor& out, co
     r.out_peers_n = r.world;
     r.row_base = row_base;
   }
+  if (bias && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->is_contiguous() && bias->numel() == r.N, "bias: [N] bf16");
+    r.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (gate && gate->defined()) {
+    TORCH_CHECK(gate->scalar_type() == at::kFloat && gate->stride(-1) == 1 && gate->size(-1) == r.N,
+                "gate: fp32 rows of N");
+    TORCH_CHECK(gate_rows > 0, "gate_rows: rows per gate vector");
+    r.gate = gate->data_ptr<float>();
+    r.gate_stride = gate->dim() > 1 ? gate->stride(0) : 0;
+    r.gate_rows = (int)gate_rows;
+    r.grow0 = grow0;
+  }
   check_ok(ft::tp_reduce(r, at::cuda::getCurrentCUDAStream()), "tp_reduce");
+}
+
+// Distributed RMSNorm over a column-sharded hidden dimension (optionally with RoPE). part_peers:
+// every rank's fp32 partial slot [world][stage_rows] for this call; flags/acks as in tp_reduce.
+void tp_rmsnorm(const Tensor& x, Tensor& y, const c10::optional<Tensor>& weight, const c10::optional<Tensor>& cos,
+                const c10::optional<Tensor>& sin, int64_t head_dim, int64_t seq_len, double eps, int64_t d_full,
+                std::vector<uint64_t> part_peers, int64_t stage_rows, std::vector<uint64_t> peer_flags, uint64_t flags,
+                int64_t flag_stride, std::vector<uint64_t> peer_acks, int64_t rank, uint64_t epoch, Tensor& counter,
+                int64_t phases) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x: [rows, D] bf16");
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.sizes() == x.sizes() && y.stride(1) == 1, "y like x");
+  const int world = (int)part_peers.size();
+  TORCH_CHECK(world >= 1 && world <= ft::kTpMaxRanks && (int)peer_flags.size() == world &&
+                  (int)peer_acks.size() == world && rank >= 0 && rank < world, "one pointer per rank");
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt && counter.numel() >= 1, "counter");
+  c10::cuda::CUDAGuard g(x.device());
+  ft::TpRmsProblem r;
+  r.rank = (int)rank;
+  r.world = world;
+  r.rows = x.size(0);
+  r.D_local = x.size(1);
+  r.D_full = (int)d_full;
+  r.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  r.ldx = x.stride(0);
+  r.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  r.ldy = y.stride(0);
+  if (weight && weight->defined()) {
+    TORCH_CHECK(weight->numel() == r.D_local && weight->is_contiguous(), "weight: [D_local]");
+    TORCH_CHECK(weight->scalar_type() == at::kFloat || weight->scalar_type() == at::kBFloat16, "weight dtype");
+    r.weight = weight->data_ptr();
+    r.weight_bf16 = weight->scalar_type() == at::kBFloat16;
+  }
+  if (cos && cos->defined()) {
+    TORCH_CHECK(sin && sin->defined() && cos->scalar_type() == at::kFloat && sin->scalar_type() == at::kFloat &&
+                    cos->is_contiguous() && sin->is_contiguous() && cos->numel() == seq_len * head_dim / 2 &&
+                    sin->numel() == cos->numel(), "rope tables: contiguous fp32 [seq_len, head_dim/2]");
+    r.cos = cos->data_ptr<float>();
+    r.sin = sin->data_ptr<float>();
+    r.head_dim = (int)head_dim;
+    r.seq_len = (int)seq_len;
+  }
+  r.eps = (float)eps;
+  for (int q = 0; q < world; q++) {
+    r.part_peers[q] = reinterpret_cast<float*>(part_peers[q]);
+    r.peer_flags[q] = reinterpret_cast<uint64_t*>(peer_flags[q]);
+    r.peer_acks[q] = reinterpret_cast<uint64_t*>(peer_acks[q]);
+  }
+  r.part_local = r.part_peers[rank];
+  r.stage_rows = (int)stage_rows;
+  r.flags = reinterpret_cast<const uint64_t*>(flags);
+  r.flag_stride = (int)flag_stride;
+  r.epoch = epoch;
+  r.counter = reinterpret_cast<unsigned int*>(counter.data_ptr<int>());
+  r.phases = (int)phases;
+  check_ok(ft::tp_rmsnorm(r, at::cuda::getCurrentCUDAStream()), "tp_rmsnorm");
 }
 
 // Expert-parallel MoE expert GEMMs (dispatch = gate/up with the row pull, else down with the
@@ -583,7 +652,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce", &tp_reduce, py::arg("stage"), py::arg("world"), py::arg("rows"), py::arg("out"),
         py::arg("residual"), py::arg("flags"), py::arg("flag_stride"), py::arg("epoch"), py::arg("peer_acks"),
         py::arg("rank"), py::arg("out_peers") = std::vector<uint64_t>{}, py::arg("row_base") = 0,
-        py::arg("stage_rows") = 0);
+        py::arg("stage_rows") = 0, py::arg("bias") = py::none(), py::arg("gate") = py::none(),
+        py::arg("gate_rows") = 0, py::arg("grow0") = 0);
+  m.def("tp_rmsnorm", &tp_rmsnorm, py::arg("x"), py::arg("y"), py::arg("weight"), py::arg("cos"), py::arg("sin"),
+        py::arg("head_dim"), py::arg("seq_len"), py::arg("eps"), py::arg("d_full"), py::arg("part_peers"),
+        py::arg("stage_rows"), py::arg("peer_flags"), py::arg("flags"), py::arg("flag_stride"), py::arg("peer_acks"),
+        py::arg("rank"), py::arg("epoch"), py::arg("counter"), py::arg("phases") = 3);
   m.def("moe_gemm", &moe_gemm);
   m.def("moe_reduce", &moe_reduce);
   m.def("p2p_wait_acks_raw", &p2p_wait_acks_raw);

@@ -12,6 +12,7 @@ enum TpEpilogue : int {
   TP_EPI_NONE = 0,
   TP_EPI_BIAS = 1,
   TP_EPI_SWIGLU = 2,  // weight rows interleaved (gate_j, up_j): C[:, j] = silu(g_j) * u_j, N/2 outputs
+  TP_EPI_BIAS_GELU = 3,  // tanh GELU of (acc + bias)
 };
 
 struct TpGemmProblem {
@@ -55,11 +56,46 @@ struct TpReduceProblem {
   void* out_peers[kTpMaxRanks] = {};
   int out_peers_n = 0;
   long long row_base = 0;
+  // out = residual + gate * (sum + bias): bias bf16 [N]; gate fp32 rows of gate_stride, one per
+  // group of gate_rows consecutive global rows (global row = grow0 + local row)
+  const __nv_bfloat16* bias = nullptr;
+  const float* gate = nullptr;
+  long long gate_stride = 0;
+  int gate_rows = 0;
+  long long grow0 = 0;
+};
+
+// RMSNorm over a hidden dimension split across tensor-parallel ranks (each rank holds D_local
+// consecutive columns, whole heads): y = x * rsqrt(sum over all ranks of x^2 / D_full + eps) * w
+// [then RoPE per head]. The per-row partial sums of squares travel over peer stores.
+struct TpRmsProblem {
+  int rank = 0, world = 1, rows = 0, D_local = 0, D_full = 0;
+  const __nv_bfloat16* x = nullptr;
+  int ldx = 0;
+  __nv_bfloat16* y = nullptr;           // may alias x
+  int ldy = 0;
+  const void* weight = nullptr;         // [D_local] shard (fp32 or bf16), optional
+  bool weight_bf16 = false;
+  float eps = 1e-6f;
+  const float* cos = nullptr;           // optional RoPE tables [seq_len, head_dim/2]
+  const float* sin = nullptr;
+  int head_dim = 0, seq_len = 0;
+  float* part_peers[kTpMaxRanks] = {};  // rank q's partial-sum slot: [world][stage_rows] fp32
+  const float* part_local = nullptr;    // this rank's slot
+  int stage_rows = 0;                   // multiple of 32, >= rows
+  uint64_t* peer_flags[kTpMaxRanks] = {};  // word on rank q: "our partials of this epoch are in"
+  const uint64_t* flags = nullptr;      // local flags[q * flag_stride] = epoch rank q published
+  int flag_stride = 1;
+  uint64_t* peer_acks[kTpMaxRanks] = {};   // word on rank q: "its partials in our slot are read"
+  uint64_t epoch = 0;
+  unsigned int* counter = nullptr;      // scratch, zeroed here
+  int phases = 3;                       // bit 0: sums of squares + publish; bit 1: wait, scale, acknowledge
 };
 
 cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream);
 cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream);
 cudaError_t tp_reduce(const TpReduceProblem& r, cudaStream_t stream);
+cudaError_t tp_rmsnorm(const TpRmsProblem& r, cudaStream_t stream);
 int tp_device_error(bool reset);
 
 }  // namespace ft

@@ -46,7 +46,7 @@ constexpr int NTHREADS = 224;  // warp 0 TMA, 1 MMA, 2-5 epilogue, 6 gather (AG)
 struct TpArgs {
   int M, N, K;
   int num_m_tiles, num_n_tiles, num_tiles, m_rot;
-  int epi;  // TP_EPI_NONE / TP_EPI_BIAS / TP_EPI_SWIGLU
+  int epi;  // TP_EPI_NONE / TP_EPI_BIAS / TP_EPI_SWIGLU / TP_EPI_BIAS_GELU
   const __nv_bfloat16* bias;
   __nv_bfloat16* C;
   int ldc;
@@ -179,9 +179,13 @@ __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); 
 // already offset to the tile's first output column).
 __device__ __forceinline__ void epi_row32(const TpArgs& p, float (&v)[32], int col0, __nv_bfloat16* dst,
                                           int n_out) {
-  if (p.epi == TP_EPI_BIAS && p.bias != nullptr) {
+  if ((p.epi == TP_EPI_BIAS || p.epi == TP_EPI_BIAS_GELU) && p.bias != nullptr) {
 #pragma unroll
     for (int e = 0; e < 32; e++) v[e] += (col0 + e < p.N) ? __bfloat162float(p.bias[col0 + e]) : 0.f;
+  }
+  if (p.epi == TP_EPI_BIAS_GELU) {
+#pragma unroll
+    for (int e = 0; e < 32; e++) v[e] = gelu_tanh(v[e]);
   }
   if (p.epi == TP_EPI_SWIGLU) {  // columns (2j, 2j+1) = (gate_j, up_j) -> 16 outputs
     const int o0 = col0 / 2;
@@ -422,10 +426,18 @@ struct OutList {
   int n;
 };
 
+struct ReduceEpi {
+  const __nv_bfloat16* bias;  // [N] or null
+  const float* gate;          // rows of gate_stride, one per gate_rows global rows, or null
+  long long gate_stride;
+  int gate_rows;
+  long long grow0;            // global row of local row 0
+};
+
 __global__ void __launch_bounds__(256)
     tp_reduce_kernel(const __nv_bfloat16* stage, int world, int rows, int stage_rows, int N,
                      const __nv_bfloat16* residual, int ldr, OutList outs, long long row_base, int ldo,
-                     const uint64_t* flags, int flag_stride, uint64_t epoch) {
+                     const uint64_t* flags, int flag_stride, uint64_t epoch, ReduceEpi ep) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
@@ -439,17 +451,27 @@ __global__ void __launch_bounds__(256)
        i += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(i / vec), c = (int)(i % vec) * 8;
     float acc[8];
-    if (residual != nullptr) {
-      const uint4 u = *reinterpret_cast<const uint4*>(residual + (size_t)r * ldr + c);
-      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = __bfloat162float(b[e]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = 0.f;
-    }
+    for (int e = 0; e < 8; e++) acc[e] = 0.f;
     for (int s = 0; s < world; s++) {
       const uint4 u = __ldcs(reinterpret_cast<const uint4*>(stage + ((size_t)s * stage_rows + r) * N + c));
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] += __bfloat162float(b[e]);
+    }
+    if (ep.bias != nullptr) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(ep.bias + c));
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] += __bfloat162float(b[e]);
+    }
+    if (ep.gate != nullptr) {
+      const float* g = ep.gate + ((ep.grow0 + r) / ep.gate_rows) * ep.gate_stride + c;
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] *= __ldg(g + e);
+    }
+    if (residual != nullptr) {
+      const uint4 u = *reinterpret_cast<const uint4*>(residual + (size_t)r * ldr + c);
       const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
       for (int e = 0; e < 8; e++) acc[e] += __bfloat162float(b[e]);
@@ -461,6 +483,129 @@ __global__ void __launch_bounds__(256)
     o.w = pack_bf16x2(acc[6], acc[7]);
     for (int q = 0; q < outs.n; q++)  // local output, or this owner's rows into every rank's output
       *reinterpret_cast<uint4*>(outs.ptr[q] + (size_t)(row_base + r) * ldo + c) = o;
+  }
+}
+
+// Distributed RMSNorm, phase 1: the sum of squares of this rank's columns of 32 rows per CTA
+// (one warp per 4 rows), stored as 8 16-byte vectors into every rank's partial slot at
+// [rank][row0..row0+31]; the last CTA to finish publishes the epoch to every rank.
+constexpr int RMS_ROWS = 32;
+
+struct PartList {
+  float* ptr[kTpMaxRanks];
+  uint64_t* flag[kTpMaxRanks];
+};
+
+__global__ void __launch_bounds__(256)
+    tp_sumsq_kernel(const __nv_bfloat16* x, int ldx, int rows, int D_local, int rank, int world, int stage_rows,
+                    PartList parts, uint64_t epoch, unsigned int* counter) {
+  __shared__ __align__(16) float ss[RMS_ROWS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * RMS_ROWS;
+  const int nvec = D_local / 8;
+#pragma unroll 1
+  for (int k = 0; k < RMS_ROWS / 8; k++) {
+    const int rr = warp * (RMS_ROWS / 8) + k;
+    const int row = row0 + rr;
+    float a = 0.f;
+    if (row < rows) {
+      const __nv_bfloat16* xr = x + (size_t)row * ldx;
+      for (int v = lane; v < nvec; v += 32) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + v * 8);
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float f = __bfloat162float(b[e]);
+          a = fmaf(f, f, a);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) ss[rr] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x < world * (RMS_ROWS / 4)) {
+    const int q = threadIdx.x / (RMS_ROWS / 4), j = threadIdx.x % (RMS_ROWS / 4);
+    const float4 v = reinterpret_cast<const float4*>(ss)[j];
+    *reinterpret_cast<float4*>(parts.ptr[q] + (size_t)rank * stage_rows + row0 + j * 4) = v;
+  }
+  __threadfence_system();  // this thread's peer stores before the CTA's completion count
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int old = atomicAdd(counter, 1u);
+    if (old == gridDim.x - 1) {
+      __threadfence_system();
+      for (int q = 0; q < world; q++) st_release_sys_u64(parts.flag[q], epoch);
+    }
+  }
+}
+
+// Phase 2: once every rank's partials are in (bounded wait), one warp per row: the row's scale
+// from the world partials, then y = x * scale * w (+ RoPE on interleaved pairs of each head).
+__global__ void __launch_bounds__(256)
+    tp_rms_apply_kernel(const __nv_bfloat16* x, int ldx, __nv_bfloat16* y, int ldy, int rows, int D_local,
+                        float inv_d, float eps, const void* weight, bool weight_bf16, const float* cosb,
+                        const float* sinb, int head_dim, int seq_len, const float* part, int world, int stage_rows,
+                        const uint64_t* flags, int flag_stride, uint64_t epoch) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int q = 0; q < world && ok; q++)
+      if (!wait_u64(flags + (size_t)q * flag_stride, epoch)) ok = 0;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = D_local / 8;
+  const int half = head_dim / 2;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    float a = lane < world ? __ldcg(part + (size_t)lane * stage_rows + row) : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    const float sc = rsqrtf(a * inv_d + eps);
+    const __nv_bfloat16* xr = x + (size_t)row * ldx;
+    __nv_bfloat16* yr = y + (size_t)row * ldy;
+    const int pos = seq_len > 0 ? row % seq_len : 0;
+    for (int v = lane; v < nvec; v += 32) {
+      const int c0 = v * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + c0);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[e] = __bfloat162float(b[e]) * sc;
+      if (weight != nullptr) {
+        if (weight_bf16) {
+          const uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(weight) + c0));
+          const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+          for (int e = 0; e < 8; e++) o[e] *= __bfloat162float(wb[e]);
+        } else {
+          const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(weight) + c0);
+          const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+          o[0] *= w0.x, o[1] *= w0.y, o[2] *= w0.z, o[3] *= w0.w;
+          o[4] *= w1.x, o[5] *= w1.y, o[6] *= w1.z, o[7] *= w1.w;
+        }
+      }
+      if (cosb != nullptr) {
+        const size_t t = (size_t)pos * half + (c0 % head_dim) / 2;
+        const float4 cs = __ldg(reinterpret_cast<const float4*>(cosb + t));
+        const float4 sn = __ldg(reinterpret_cast<const float4*>(sinb + t));
+        const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float re = o[2 * q], im = o[2 * q + 1];
+          o[2 * q] = re * cv[q] - im * sv[q];
+          o[2 * q + 1] = re * sv[q] + im * cv[q];
+        }
+      }
+      uint4 w;
+      w.x = pack_bf16x2(o[0], o[1]);
+      w.y = pack_bf16x2(o[2], o[3]);
+      w.z = pack_bf16x2(o[4], o[5]);
+      w.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(yr + c0) = w;
+    }
   }
 }
 
@@ -598,10 +743,57 @@ cudaError_t tp_reduce(const TpReduceProblem& r, cudaStream_t stream) {
   int grid = (int)((work + 255) / 256);
   if (grid > 4 * 148) grid = 4 * 148;
   if (grid < 1) grid = 1;
+  if (r.gate != nullptr && r.gate_rows <= 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(r.bias) & 15) != 0) return cudaErrorMisalignedAddress;
+  ReduceEpi ep{r.bias, r.gate, r.gate_stride, r.gate_rows, r.grow0};
   tp_reduce_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(r.stage), r.world, r.rows, stage_rows,
                                              r.N, static_cast<const __nv_bfloat16*>(r.residual), r.ldr, outs,
-                                             row_base, r.ldo, r.flags, r.flag_stride, r.epoch);
+                                             row_base, r.ldo, r.flags, r.flag_stride, r.epoch, ep);
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  AckList a{};
+  a.n = r.world;
+  a.epoch = r.epoch;
+  for (int q = 0; q < r.world; q++) a.ptr[q] = q == r.rank ? nullptr : r.peer_acks[q];
+  tp_ack_kernel<<<1, 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_rmsnorm(const TpRmsProblem& r, cudaStream_t stream) {
+  if (r.world < 1 || r.world > kTpMaxRanks || r.rank < 0 || r.rank >= r.world || r.rows < 0) return cudaErrorInvalidValue;
+  if (r.D_local <= 0 || r.D_local % 8 || r.D_full < r.D_local || r.x == nullptr || r.y == nullptr) return cudaErrorInvalidValue;
+  // phase 1 stores whole 32-row groups: the slot must cover them
+  if (r.ldx % 8 || r.ldy % 8 || r.stage_rows % RMS_ROWS || r.stage_rows < r.rows || r.stage_rows < RMS_ROWS)
+    return cudaErrorInvalidValue;
+  if (r.part_local == nullptr || r.flags == nullptr || r.counter == nullptr) return cudaErrorInvalidValue;
+  auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+  if (mis(r.x) || mis(r.y) || mis(r.weight) || mis(r.cos) || mis(r.sin)) return cudaErrorMisalignedAddress;
+  if (r.cos != nullptr && (r.sin == nullptr || r.head_dim % 8 || r.D_local % r.head_dim || r.seq_len <= 0))
+    return cudaErrorInvalidValue;
+  PartList parts{};
+  for (int q = 0; q < r.world; q++) {
+    if (r.part_peers[q] == nullptr || r.peer_flags[q] == nullptr || mis(r.part_peers[q])) return cudaErrorInvalidValue;
+    parts.ptr[q] = r.part_peers[q];
+    parts.flag[q] = r.peer_flags[q];
+  }
+  cudaError_t e = cudaSuccess;
+  if (r.phases & 1) {
+    e = cudaMemsetAsync(r.counter, 0, sizeof(unsigned int), stream);
+    if (e != cudaSuccess) return e;
+    const int blocks = r.rows > 0 ? (r.rows + RMS_ROWS - 1) / RMS_ROWS : 1;
+    tp_sumsq_kernel<<<blocks, 256, 0, stream>>>(r.x, r.ldx, r.rows, r.D_local, r.rank, r.world, r.stage_rows, parts,
+                                                r.epoch, r.counter);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (!(r.phases & 2)) return cudaSuccess;
+  int grid = (r.rows + 7) / 8;
+  if (grid > 8 * 148) grid = 8 * 148;
+  if (grid < 1) grid = 1;
+  tp_rms_apply_kernel<<<grid, 256, 0, stream>>>(r.x, r.ldx, r.y, r.ldy, r.rows, r.D_local, 1.f / (float)r.D_full, r.eps,
+                                                r.weight, r.weight_bf16, r.cos, r.sin, r.head_dim, r.seq_len,
+                                                r.part_local, r.world, r.stage_rows, r.flags, r.flag_stride, r.epoch);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   AckList a{};
   a.n = r.world;

@@ -12,8 +12,8 @@ from flextensor_b200.parallel.striped import (
     striping_group,
 )
 from flextensor_b200.parallel.symm import SymmetricHeap
-from flextensor_b200.parallel.tp import NcclTP, TPAllGather, TPAllReduce, TPReduceScatter
+from flextensor_b200.parallel.tp import NcclTP, TPAllGather, TPAllReduce, TPReduceScatter, TPRMSNorm, nccl_rmsnorm
 
 __all__ = ["ContextParallel", "ControlPlane", "ExpertParallel", "NcclExpertParallel", "NcclTP", "ReplicaFatalError",
-           "StripedTransferEngine", "SymmetricHeap", "TPAllGather", "TPAllReduce", "TPReduceScatter", "UlyssesAttention",
-           "disable_striped_streaming", "enable_striped_streaming", "route_topk", "striping_group"]
+           "StripedTransferEngine", "SymmetricHeap", "TPAllGather", "TPAllReduce", "TPRMSNorm", "TPReduceScatter", "UlyssesAttention",
+           "disable_striped_streaming", "enable_striped_streaming", "nccl_rmsnorm", "route_topk", "striping_group"]

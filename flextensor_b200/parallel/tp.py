@@ -10,8 +10,10 @@ partials and the residual).
 
 Both objects double-buffer their symmetric-heap slots and gate reuse with epoch flags and
 acknowledgements (bounded device-side waits), so consecutive layers never wait on the host.
-:class:`NcclTP` is the unfused baseline (``all_gather_into_tensor`` + GEMM,
-GEMM + ``reduce_scatter_tensor``).
+:class:`TPAllReduce` is the GEMM + all-reduce form for layers whose output stays replicated,
+and :class:`TPRMSNorm` the RMSNorm over a head-sharded hidden dimension (partial sums of squares
+over peer stores). :class:`NcclTP` and :func:`nccl_rmsnorm` are the unfused baselines
+(``all_gather_into_tensor`` + GEMM, GEMM + ``reduce_scatter_tensor``, ``all_reduce`` of the sums).
 """
 
 from __future__ import annotations
@@ -72,6 +74,11 @@ class TPAllGather:
         slot, e = self._cur
         native.lib().p2p_publish_raw(self.f.flags, self.f.acks, self.rank, N_SLOTS, slot, e)
 
+    def full(self) -> torch.Tensor:
+        """The current slot's ``[M, K]`` buffer: after :meth:`gemm` it holds every rank's rows,
+        so further GEMMs on the same activations (K and V after Q) need no second gather."""
+        return self._buf(self._cur[0])
+
     def gemm(self, weight: torch.Tensor, bias: torch.Tensor | None = None, epi: str = "none",
              out: torch.Tensor | None = None) -> torch.Tensor:
         from flextensor_b200.ops.api import tp_allgather_gemm
@@ -129,15 +136,18 @@ class TPReduceScatter:
                               peer_flags=[self.f.flags[p] + (self.rank * N_SLOTS + slot) * 8 for p in range(self.world)],
                               rank=self.rank, epoch=e, counters=self.counters)
 
-    def reduce(self, out: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """Owner side: ``out [R, N] = residual + sum of all ranks' partial rows``."""
+    def reduce(self, out: torch.Tensor, residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+               gate: torch.Tensor | None = None, gate_rows: int = 0) -> torch.Tensor:
+        """Owner side: ``out [R, N] = residual + gate * (sum of all ranks' partial rows + bias)``
+        (``gate``: fp32 ``[groups, N]``, one row per ``gate_rows`` rows of the full sequence)."""
         from flextensor_b200.ops.api import tp_reduce
 
         slot, e = self._cur
         return tp_reduce(self._stage(slot), self.world, self.R, out, flags_ptr=self.f.flags[self.rank] + slot * 8,
                          flag_stride=N_SLOTS, epoch=e,
                          peer_acks=[self.f.acks[q] + (self.rank * N_SLOTS + slot) * 8 for q in range(self.world)],
-                         rank=self.rank, residual=residual)
+                         rank=self.rank, residual=residual, bias=bias, gate=gate,
+                         gate_rows=gate_rows or self.M, grow0=self.rank * self.R)
 
     def close(self) -> None:
         _close(self)
@@ -201,6 +211,69 @@ class TPAllReduce:
 
     def close(self) -> None:
         _close(self)
+
+
+class TPRMSNorm:
+    """RMSNorm whose hidden dimension is split across the ranks (head-sharded Q/K norms of a
+    tensor-parallel attention): each call sends the per-row partial sums of squares of this
+    rank's columns to every rank over peer stores and scales the local columns once all ranks'
+    partials are in; optional RoPE on the way out. Up to ``max_rows`` rows per call;
+    double-buffered partial slots, reuse gated by acknowledgements (no host synchronisation)."""
+
+    def __init__(self, max_rows: int, group=None, device: int | None = None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.stage_rows = max(32, (max_rows + 31) // 32 * 32)
+        dev = torch.cuda.current_device() if device is None else device
+        hdr = 4096
+        self.slot_bytes = (self.world * self.stage_rows * 4 + 4095) // 4096 * 4096
+        self.heap = SymmetricHeap(hdr + N_SLOTS * self.slot_bytes, group, dev)
+        self.f = _Flags(self.heap, self.world)
+        self.off = [hdr + s * self.slot_bytes for s in range(N_SLOTS)]
+        self.counter = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+        self.epochs = [0] * N_SLOTS
+        self.calls = 0
+        dist.barrier(group=group)
+
+    def __call__(self, x: torch.Tensor, weight: torch.Tensor | None, d_full: int, eps: float = 1e-6,
+                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None, head_dim: int = 0,
+                 seq_len: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+        from flextensor_b200.ops.api import tp_rmsnorm
+
+        rows = x.numel() // x.shape[-1]
+        if rows > self.stage_rows:
+            raise ValueError(f"TPRMSNorm sized for {self.stage_rows} rows, got {rows}")
+        slot = self.calls % N_SLOTS
+        self.calls += 1
+        self.epochs[slot] += 1
+        e = self.epochs[slot]
+        if e > 1:  # every rank finished reading our partials of this slot's previous use
+            native.lib().p2p_wait_acks_raw(self.f.flags, self.f.acks, self.rank, N_SLOTS, slot, e - 1)
+        W = self.world
+        return tp_rmsnorm(x, weight, d_full=d_full, part_peers=[p + self.off[slot] for p in self.heap.ptrs],
+                          stage_rows=self.stage_rows,
+                          peer_flags=[self.f.flags[q] + (self.rank * N_SLOTS + slot) * 8 for q in range(W)],
+                          flags_ptr=self.f.flags[self.rank] + slot * 8, flag_stride=N_SLOTS,
+                          peer_acks=[self.f.acks[q] + (self.rank * N_SLOTS + slot) * 8 for q in range(W)],
+                          rank=self.rank, epoch=e, counter=self.counter, eps=eps, cos=cos, sin=sin,
+                          head_dim=head_dim, seq_len=seq_len, out=out)
+
+    def close(self) -> None:
+        _close(self)
+
+
+def nccl_rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, d_full: int, eps: float = 1e-6, group=None):
+    """Unfused baseline of :class:`TPRMSNorm`: partial sum of squares, NCCL all-reduce, scale."""
+    import torch.distributed as dist
+
+    ss = x.float().pow(2).sum(-1, keepdim=True)
+    dist.all_reduce(ss, group=group)
+    y = x.float() * torch.rsqrt(ss / d_full + eps)
+    if weight is not None:
+        y = y * weight.float()
+    return y.to(x.dtype)
 
 
 def _close(obj) -> None:

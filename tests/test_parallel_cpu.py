@@ -86,3 +86,53 @@ def test_striping_group_uses_default_group():
     for p in ps:
         p.join(30)
     assert res == [(0, True, True), (1, True, True)]
+
+
+def _wan_tp_shard_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from flextensor_b200.models.wan import WanDiT, init_wan_params_, tiny_config
+    from flextensor_b200.models.wan_tp import WanTensorParallel
+
+    cfg = tiny_config(dim=512, ffn_dim=1024, num_heads=4, num_layers=1)
+    m = WanDiT(cfg, impl="torch")
+    init_wan_params_(m, seed=0)
+    full = {n: p.detach().numpy().copy() for n, p in m.named_parameters()}  # numpy: pickled by value
+    WanTensorParallel(m, impl="nccl")
+    shards = {n: p.detach().numpy().copy() for n, p in m.named_parameters()}
+    q.put((rank, full, shards))
+    dist.destroy_process_group()
+
+
+def test_wan_tensor_parallel_shards_cover_the_model():
+    """Head/FFN sharding of the Wan blocks (the reference driver's col_shard / row_shard /
+    DistRMSNorm layout): concatenating the 2 ranks' shards gives back every full tensor; row-
+    parallel biases stay whole (added once after the reduction)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_wan_tp_shard_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted((q.get(timeout=120) for _ in ps), key=lambda t: t[0])
+    for p in ps:
+        p.join(30)
+    full = {n: torch.from_numpy(a) for n, a in res[0][1].items()}
+    s0 = {n: torch.from_numpy(a) for n, a in res[0][2].items()}
+    s1 = {n: torch.from_numpy(a) for n, a in res[1][2].items()}
+    for n, t in full.items():
+        if ".blocks." not in f".{n}":
+            assert torch.equal(s0[n], t) and torch.equal(s1[n], t), n
+            continue
+        leaf = n.split(".", 2)[2]
+        if leaf.endswith("to_out.weight") or leaf == "ffn_out.weight":
+            assert torch.equal(torch.cat([s0[n], s1[n]], 1), t), n
+        elif leaf.endswith("to_out.bias") or leaf == "ffn_out.bias" or leaf.startswith("norm2") \
+                or leaf == "scale_shift_table":
+            assert torch.equal(s0[n], t) and torch.equal(s1[n], t), n
+        else:
+            assert torch.equal(torch.cat([s0[n], s1[n]], 0), t), n

@@ -22,13 +22,14 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("W,R,K,N,epi,rank", [(4, 200, 256, 384, "bias", 1), (2, 256, 512, 1024, "swiglu", 0),
-                                              (8, 96, 128, 256, "none", 7), (3, 333, 192, 512, "swiglu", 2)])
+                                              (8, 96, 128, 256, "none", 7), (3, 333, 192, 512, "swiglu", 2),
+                                              (2, 150, 256, 640, "gelu", 1)])
 def test_allgather_gemm(W, R, K, N, epi, rank):
     M = W * R
     g = torch.Generator(device=DEV).manual_seed(W * 10 + rank)
     a = torch.randn(M, K, device=DEV, generator=g).bfloat16()
     w = (torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
-    bias = torch.randn(N, device=DEV, generator=g).bfloat16() if epi == "bias" else None
+    bias = torch.randn(N, device=DEV, generator=g).bfloat16() if epi in ("bias", "gelu") else None
     bufs = []
     for p in range(W):
         b = torch.zeros(M, K, device=DEV, dtype=torch.bfloat16)
@@ -49,6 +50,8 @@ def test_allgather_gemm(W, R, K, N, epi, rank):
             ref = ref + bias.float()
         if epi == "swiglu":
             ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+        if epi == "gelu":
+            ref = torch.nn.functional.gelu(ref, approximate="tanh")
         assert _rel(out, ref) < 2e-2
         assert torch.equal(bufs[rank], a), "rows not gathered"
         for p in range(W):
@@ -121,3 +124,78 @@ def test_gemm_allreduce_uneven_rows(W, M, K, N):
         for p in range(W):
             if p != q:
                 assert int(acks[q][p]) == 1
+
+
+@pytest.mark.parametrize("W,rows,D,rope", [(2, 77, 512, True), (4, 300, 1024, False), (8, 33, 5120, True), (1, 64, 256, True)])
+def test_distributed_rmsnorm_emulated(W, rows, D, rope):
+    """RMSNorm over a hidden dimension split across W emulated ranks (partial sums of squares to
+    every rank's slot, then each rank scales its columns, optional RoPE), against the fp32 norm
+    of the concatenated row. Phase 1 of every rank runs before any phase 2 (no launch waits on a
+    launch that has not run)."""
+    Dl, Dh = D // W, 128
+    stage_rows = (rows + 31) // 32 * 32
+    g = torch.Generator(device=DEV).manual_seed(W * 100 + rows)
+    xs = [torch.randn(rows, Dl, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    w = torch.randn(D, device=DEV, generator=g)
+    parts = [torch.zeros(W, stage_rows, device=DEV) for _ in range(W)]
+    flags = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cos = sin = None
+    if rope:
+        ang = torch.randn(rows, Dh // 2, device=DEV, generator=g)
+        cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    outs = [torch.empty_like(x) for x in xs]
+    for phase in (1, 2):
+        for r in range(W):
+            ops.tp_rmsnorm(xs[r], w[r * Dl:(r + 1) * Dl].contiguous(), d_full=D, part_peers=[p.data_ptr() for p in parts],
+                           stage_rows=stage_rows, peer_flags=[f.data_ptr() + 8 * r for f in flags],
+                           flags_ptr=flags[r].data_ptr(), flag_stride=1,
+                           peer_acks=[a.data_ptr() + 8 * r for a in acks], rank=r, epoch=1, counter=counter,
+                           eps=1e-6, cos=cos, sin=sin, head_dim=Dh if rope else 0, seq_len=rows if rope else 0,
+                           out=outs[r], _phases=phase)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    xf = torch.cat([x.float() for x in xs], 1)
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+    if rope:
+        rr = ref.view(rows, D // Dh, Dh // 2, 2)
+        re, im = rr[..., 0], rr[..., 1]
+        c, s = cos[:, None, :], sin[:, None, :]
+        ref = torch.stack([re * c - im * s, re * s + im * c], -1).view(rows, D)
+    for r in range(W):
+        assert _rel(outs[r], ref[:, r * Dl:(r + 1) * Dl]) < 1e-2, r
+        for q in range(W):
+            if q != r:
+                assert int(acks[q][r]) == 1
+
+
+def test_reduce_bias_gate_residual():
+    """Owner reduce with bias, per-group fp32 gate and residual: out = res + gate * (sum + bias)."""
+    W, M, K, N, S = 2, 64, 128, 256, 32
+    R = M // W
+    g = torch.Generator(device=DEV).manual_seed(3)
+    a = [torch.randn(M, K, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    w = [(torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16() for _ in range(W)]
+    bias = torch.randn(N, device=DEV, generator=g).bfloat16()
+    gate = torch.randn(M // S, N, device=DEV, generator=g)
+    res = [torch.randn(R, N, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    stage = [torch.zeros(W, R, N, device=DEV, dtype=torch.bfloat16) for _ in range(W)]
+    flags = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    counters = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for r in range(W):
+        ops.tp_gemm_reducescatter(a[r], w[r], stage=[s.data_ptr() for s in stage],
+                                  peer_flags=[f.data_ptr() + 8 * r for f in flags], rank=r, epoch=1, counters=counters)
+    outs = [x.clone() for x in res]
+    for p in range(W):
+        ops.tp_reduce(stage[p], W, R, outs[p], flags_ptr=flags[p].data_ptr(), flag_stride=1, epoch=1,
+                      peer_acks=[x.data_ptr() + 8 * p for x in acks], rank=p, residual=outs[p], bias=bias, gate=gate,
+                      gate_rows=S, grow0=p * R)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    full = sum(a[r].float() @ w[r].float().t() for r in range(W)) + bias.float()
+    full = full * gate.repeat_interleave(S, 0)
+    for p in range(W):
+        ref = res[p].float() + full[p * R:(p + 1) * R]
+        assert _rel(outs[p], ref) < 2e-2, p
