@@ -116,6 +116,13 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x <= -126.f ? 0.f : y;
 }
 
+// Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; this
+// empty asm "rewrites" them after the wait so no use is scheduled above it.
+__device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
+}
+
 // Blackwell packed fp32 pairs and 3-input max (halve the softmax's FFMA / FADD / FMNMX count)
 __device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
   unsigned long long r;
@@ -456,6 +463,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
         tc_fence_after();
         issue_PV_part(t, s, j, 0, TILE / 32);
         if (!mbar_wait(&sm.p_full[t], j & 1)) return false;
+        if (t == 0) trace_at(a, 18, j);
         tc_fence_after();
         issue_PV_part(t, s, j, TILE / 32, TILE / 16);
         umma_commit(&sm.o_done[t]);
@@ -544,6 +552,8 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; c++) tmem_ld_32x32b_x32(tS + c * 32, v[c]);
       tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 4; c++) reg_fence32(v[c]);
       if (r == 0) trace_at(a, 5 + 4 * t, j);
       if (masked) {
         // keys [kbase, kbase + lim) are visible to this row
@@ -581,6 +591,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
         m = m_new;
       }
       const float msub = (m == -INFINITY) ? 0.f : m;
+      if (r == 0) trace_at(a, 12 + 2 * t, j);
       unsigned long long rsc[4] = {0ull, 0ull, 0ull, 0ull};  // packed (even, odd) partial row sums
       const unsigned long long scale2 = f2pack(a.scale_log2, a.scale_log2);
       const unsigned long long negm2 = f2pack(-msub, -msub);
@@ -629,6 +640,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.p_half[t]);
+          if (r == 0) trace_at(a, 13 + 2 * t, j);
         }
       }
       float rs;
@@ -647,6 +659,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.p_full[t]);
       if (r == 0) trace_at(a, 7 + 4 * t, j);
+      if (t == 0 && quad > 0 && lane == 0) trace_at(a, quad == 3 ? 3 : 15 + quad, j);  // 3, 16, 17
     }
     // epilogue: O / l -> bf16
     if (active && ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (n_kv - 1) & 1))) {

@@ -202,8 +202,8 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
   p.causal = causal;
   p.diag_mode = (int)diag_mode;
   if (trace && trace->defined()) {
-    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->numel() >= 12 * 64,
-                "trace must be a CUDA int64 tensor with >= 768 entries");
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->numel() >= 20 * 64,
+                "trace must be a CUDA int64 tensor with >= 1280 entries");
     p.trace = trace->data_ptr();
   }
   p.num_sms = num_sms_for(q.get_device());

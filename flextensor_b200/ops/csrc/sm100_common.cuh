@@ -15,6 +15,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#ifndef FT_TRY_WAIT_HINT_NS
+#define FT_TRY_WAIT_HINT_NS 20000u  // mbarrier suspend hint: 20 us, far below the wait bound
+#endif
 #ifndef FT_WAIT_LIMIT_CYCLES
 #define FT_WAIT_LIMIT_CYCLES (4000000000ull)  // ~2 s at 1.9 GHz
 #endif
@@ -98,17 +101,52 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t phase)
   return ok != 0;
 }
 
-// Bounded wait for the barrier phase with parity `phase` to complete. The hot loop is
-// try_wait only (it suspends in hardware until the phase completes or a short time
-// limit passes); the clock bound and the global error word are checked every 256 spins,
-// so a completed phase is noticed without a long-latency global load in the way.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
+// try_wait with an explicit suspend-time hint (ns): the waiting warp sleeps in hardware until
+// the phase completes or the hint expires. Measured in the attention kernel: the sleeping MMA
+// warp woke ~500 cycles late on its critical path, so no kernel uses it by default.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(phase), "r"(FT_TRY_WAIT_HINT_NS)
+      : "memory");
+  return ok != 0;
+}
+
+// test_wait never suspends: a spin on it notices the phase within one probe.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+enum MbarWaitMode : int { kWaitProbe = 0, kWaitSleep = 1, kWaitSpin = 2 };
+
+// Bounded wait for the barrier phase with parity `phase` to complete. kWaitProbe: try_wait
+// (suspends for a short hardware-defined time); kWaitSleep: try_wait with the suspend hint;
+// kWaitSpin: test_wait. The clock bound and the global error word are checked every 256 probes
+// (every probe when sleeping), so a completed phase is noticed without a long-latency global
+// load in the way.
+template <int MODE>
+__device__ __forceinline__ bool mbar_wait_t(uint64_t* bar, uint32_t phase) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, phase)) return true;
+  if (MODE == kWaitSpin ? mbar_test_wait(a, phase) : mbar_try_wait(a, phase)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(a, phase)) return true;
-    if ((it & 255u) == 0u) {
+    const bool done = MODE == kWaitSleep  ? mbar_try_wait_sleep(a, phase)
+                      : MODE == kWaitSpin ? mbar_test_wait(a, phase)
+                                          : mbar_try_wait(a, phase);
+    if (done) return true;
+    if (MODE == kWaitSleep || (it & 255u) == 0u) {
       if ((unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES) {
         record_error(kErrWaitTimeout);
         return false;
@@ -117,6 +155,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
     }
   }
 }
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) { return mbar_wait_t<kWaitProbe>(bar, phase); }
 
 // ------------------------------------------------------------------ TMA (no multicast anywhere)
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
