@@ -8,9 +8,9 @@
 //                   (RMSNorm over the full H*Dh row, then complex rotation by
 //                   cos/sin tables indexed by token position)
 //
-// Statistics are two-pass in fp32 (mean, then centred variance) from the
-// register copy, which is exact-enough for bf16 activations and avoids the
-// cancellation of the one-pass E[x^2]-E[x]^2 form.
+// The row stays in registers as packed bf16. LayerNorm statistics are per-thread two-pass
+// (mean, then centred M2) merged across the block in one reduction (Chan et al.), which
+// avoids the cancellation of the one-pass E[x^2]-E[x]^2 form.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -85,41 +85,111 @@ __device__ __forceinline__ float4 ld4f(const float* p) {
   return make_float4(p[0], p[1], p[2], p[3]);
 }
 
-// VPT = 8-element vectors per thread held in registers (D <= NT*8*VPT). VEC = every per-column
-// parameter array is 16-byte aligned (vector loads; the parameter traffic is otherwise the
-// limiter of these HBM-bound kernels, not the row itself).
+// Row statistics in one block reduction: every thread holds (count, mean, M2) of its own
+// elements (exact two-pass over its registers), and the pairs merge by Chan et al.'s parallel
+// update, n = na + nb, d = mb - ma, mean = ma + d nb / n, M2 = Ma + Mb + d^2 na nb / n, which
+// keeps the centred form (no E[x^2] - E[x]^2 cancellation) with half the barriers of two sums.
+__device__ __forceinline__ void chan_merge(float& n, float& m, float& M, float nb, float mb, float Mb) {
+  const float tot = n + nb;
+  if (nb > 0.f) {
+    const float d = mb - m;
+    const float f = nb / tot;
+    m = fmaf(d, f, m);
+    M = M + Mb + d * d * n * f;
+    n = tot;
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void block_mean_m2(float n, float m, float M, float* red, float& mean, float& m2) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float nb = __shfl_xor_sync(0xffffffff, n, o);
+    const float mb = __shfl_xor_sync(0xffffffff, m, o);
+    const float Mb = __shfl_xor_sync(0xffffffff, M, o);
+    if (n == 0.f) {
+      n = nb, m = mb, M = Mb;
+    } else {
+      chan_merge(n, m, M, nb, mb, Mb);
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[3 * w] = n, red[3 * w + 1] = m, red[3 * w + 2] = M;
+  __syncthreads();
+  float tn = red[0], tm = red[1], tM = red[2];
+#pragma unroll
+  for (int i = 1; i < NT / 32; i++) {
+    if (tn == 0.f) {
+      tn = red[3 * i], tm = red[3 * i + 1], tM = red[3 * i + 2];
+    } else {
+      chan_merge(tn, tm, tM, red[3 * i], red[3 * i + 1], red[3 * i + 2]);
+    }
+  }
+  mean = tm;
+  m2 = tM;
+}
+
+// Marks the packed row registers as rewritten, so each pass converts them again instead of
+// keeping a second, fp32 copy of the row live (the point of holding it packed).
+template <int VPT>
+__device__ __forceinline__ void refresh(uint4 (&raw)[VPT]) {
+#pragma unroll
+  for (int i = 0; i < VPT; i++) asm volatile("" : "+r"(raw[i].x), "+r"(raw[i].y), "+r"(raw[i].z), "+r"(raw[i].w));
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int e = 0; e < 8; e++) f[e] = __bfloat162float(b[e]);
+}
+
+// VPT = 8-element vectors per thread, held in registers as packed bf16 (D <= NT*8*VPT). VEC =
+// every per-column parameter array is 16-byte aligned (vector loads; the parameter traffic is
+// otherwise the limiter of these HBM-bound kernels, not the row itself).
 template <int NT, int VPT, bool VEC>
 __global__ void __launch_bounds__(NT) ln_modulate_kernel(LnArgs a) {
-  __shared__ float red[NT / 32];
+  __shared__ float red[3 * (NT / 32)];
   const int row = blockIdx.x;
   const __nv_bfloat16* x = a.x + (size_t)row * a.ldx;
   __nv_bfloat16* y = a.y + (size_t)row * a.ldy;
   const int nvec = a.D / 8;
-  float v[VPT][8];
-  float s = 0.f;
+  uint4 raw[VPT];
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
     const int vi = threadIdx.x + i * NT;
-    if (vi < nvec) {
-      load8(x + vi * 8, v[i]);
+    if (vi < nvec) raw[i] = *reinterpret_cast<const uint4*>(x + vi * 8);
+  }
+  // this thread's (count, mean, M2), two passes over its registers
+  float cnt = 0.f, s = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; e++) s += v[i][e];
+  for (int i = 0; i < VPT; i++) {
+    if (threadIdx.x + i * NT < nvec) {
+      float f[8];
+      unpack8(raw[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; e++) s += f[e];
+      cnt += 8.f;
     }
   }
-  const float mean = block_sum<NT>(s, red) / a.D;
-  float ss = 0.f;
+  const float tmean = cnt > 0.f ? s / cnt : 0.f;
+  refresh(raw);
+  float tm2 = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
-    const int vi = threadIdx.x + i * NT;
-    if (vi < nvec) {
+    if (threadIdx.x + i * NT < nvec) {
+      float f[8];
+      unpack8(raw[i], f);
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        float d = v[i][e] - mean;
-        ss += d * d;
+        const float d = f[e] - tmean;
+        tm2 = fmaf(d, d, tm2);
       }
     }
   }
-  const float rstd = rsqrtf(block_sum<NT>(ss, red) / a.D + a.eps);
+  float mean, m2;
+  block_mean_m2<NT>(cnt, tmean, tm2, red, mean, m2);
+  const float rstd = rsqrtf(m2 / a.D + a.eps);
+  refresh(raw);
   const int mrow = a.mod_rows > 0 ? row / a.mod_rows : 0;
   const float* sc = a.scale ? a.scale + (size_t)mrow * a.mod_stride : nullptr;
   const float* sh = a.shift ? a.shift + (size_t)mrow * a.mod_stride : nullptr;
@@ -129,8 +199,9 @@ __global__ void __launch_bounds__(NT) ln_modulate_kernel(LnArgs a) {
     if (vi < nvec) {
       const int c0 = vi * 8;
       float o[8], p[8];
+      unpack8(raw[i], o);
 #pragma unroll
-      for (int e = 0; e < 8; e++) o[e] = (v[i][e] - mean) * rstd;
+      for (int e = 0; e < 8; e++) o[e] = (o[e] - mean) * rstd;
       if (a.weight) {
         ldp8<VEC>(a.weight, c0, a.affine_bf16, p);
 #pragma unroll
@@ -163,15 +234,20 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(RmsArgs a) {
   const __nv_bfloat16* x = a.x + (size_t)row * a.ldx;
   __nv_bfloat16* y = a.y + (size_t)row * a.ldy;
   const int nvec = a.D / 8;
-  float v[VPT][8];
-  float ss = 0.f;
+  uint4 raw[VPT];
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
     const int vi = threadIdx.x + i * NT;
-    if (vi < nvec) {
-      load8(x + vi * 8, v[i]);
+    if (vi < nvec) raw[i] = *reinterpret_cast<const uint4*>(x + vi * 8);
+  }
+  float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; e++) ss += v[i][e] * v[i][e];
+  for (int i = 0; i < VPT; i++) {
+    if (threadIdx.x + i * NT < nvec) {
+      float f[8];
+      unpack8(raw[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; e++) ss = fmaf(f[e], f[e], ss);
     }
   }
   const float r = a.no_norm ? 1.f : rsqrtf(block_sum<NT>(ss, red) / a.D + a.eps);
@@ -185,8 +261,9 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(RmsArgs a) {
     if (vi < nvec) {
       const int c0 = vi * 8;
       float o[8];
+      unpack8(raw[i], o);
 #pragma unroll
-      for (int e = 0; e < 8; e++) o[e] = v[i][e] * r;
+      for (int e = 0; e < 8; e++) o[e] *= r;
       if (a.weight) {
         float w[8];
         ldp8<VEC>(a.weight, c0, a.weight_bf16, w);

@@ -115,12 +115,14 @@ __device__ bool wait_done(const unsigned int* d, unsigned int target) {
   return true;
 }
 
-// One lane of warp 6: pull peers' A rows into the local copy (see the file comment).
+// One lane of warp 6: pull peers' A rows into the local copy (see the file comment). Two pieces
+// are in flight: piece i's peer load is issued before piece i-1's load is waited on and stored,
+// so the NVLink read of one piece overlaps the local write of the previous one.
 __device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_full) {
   const unsigned int npieces = (unsigned int)c.pieces;
   const long long rank_bytes = c.row_bytes * c.rows;
   uint32_t ph[2] = {0, 0};
-  int issued = 0, pend_p = -1;
+  bool loading[2] = {false, false};
   bool ok = true;
   auto finish = [&](int p) {
     fence_proxy_async_global();
@@ -130,12 +132,29 @@ __device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_ful
       st_release_sys_u64(c.peer_acks[p], c.epoch);
     }
   };
-  for (int d = 1; d < c.world && ok; d++) {
-    const int p = (c.rank + d) % c.world;
-    bool flagged = false;
-    for (;;) {
+  // pieces in the pipeline: [0] = the one being loaded, [1] = loaded and being stored
+  struct Piece {
+    int p;
+    long long at;
+    uint32_t n;
+    int st;
+  };
+  Piece prev{-1, 0, 0, 0};
+  int stored_p = -1;  // peer of the piece whose store was committed last (finished one step later)
+  int issued = 0;
+  int d = 1;
+  bool flagged = false;
+  while (ok) {
+    // claim the next piece, moving to the next peer when this one is exhausted
+    Piece cur{-1, 0, 0, 0};
+    while (d < c.world) {
+      const int p = (c.rank + d) % c.world;
       const unsigned int idx = atomicAdd(c.claim + p, 1u);
-      if (idx >= npieces) break;
+      if (idx >= npieces) {
+        d++;
+        flagged = false;
+        continue;
+      }
       if (!flagged) {
         if (!wait_u64(c.flags + (size_t)p * c.flag_stride, c.epoch)) {
           ok = false;
@@ -144,33 +163,46 @@ __device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_ful
         flagged = true;
       }
       const long long off = (long long)idx * TP_PIECE;
-      const uint32_t n = (uint32_t)min((long long)TP_PIECE, rank_bytes - off);
-      const long long at = (long long)p * rank_bytes + off;
-      const int st = issued & 1;
-      uint8_t* buf = stage + st * TP_PIECE;
-      mbar_arrive_expect_tx(&stage_full[st], n);
-      bulk_load_g2s(buf, c.peer_a[p] + at, n, &stage_full[st]);
-      if (!mbar_wait(&stage_full[st], ph[st])) {
-        const long long t0 = clock64();  // never leave with a load in flight
-        while (!mbar_try_wait(smem_u32(&stage_full[st]), ph[st]) &&
-               (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
-        }
+      cur = Piece{p, (long long)p * rank_bytes + off, (uint32_t)min((long long)TP_PIECE, rank_bytes - off),
+                  issued & 1};
+      break;
+    }
+    if (!ok) break;
+    if (cur.p >= 0) {
+      bulk_wait_read<0>();  // the store that last read this buffer (two pieces ago) is done with it
+      uint8_t* buf = stage + cur.st * TP_PIECE;
+      mbar_arrive_expect_tx(&stage_full[cur.st], cur.n);
+      bulk_load_g2s(buf, c.peer_a[cur.p] + cur.at, cur.n, &stage_full[cur.st]);
+      loading[cur.st] = true;
+      issued++;
+    }
+    if (prev.p >= 0) {
+      if (!mbar_wait(&stage_full[prev.st], ph[prev.st])) {
         ok = false;
         break;
       }
-      ph[st] ^= 1;
-      bulk_store_s2g(c.local_a + at, buf, n);
+      loading[prev.st] = false;
+      ph[prev.st] ^= 1;
+      bulk_store_s2g(c.local_a + prev.at, stage + prev.st * TP_PIECE, prev.n);
       bulk_commit();
-      issued++;
-      if (pend_p >= 0) {
-        bulk_wait<1>();
-        finish(pend_p);
+      bulk_wait<1>();  // the store committed one step earlier has landed
+      if (stored_p >= 0) finish(stored_p);
+      stored_p = prev.p;
+    }
+    if (cur.p < 0) break;
+    prev = cur;
+  }
+  if (!ok) {  // never leave with a load in flight
+    for (int st = 0; st < 2; st++) {
+      if (!loading[st]) continue;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(smem_u32(&stage_full[st]), ph[st]) &&
+             (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
       }
-      pend_p = p;
     }
   }
   bulk_wait<0>();
-  if (ok && pend_p >= 0) finish(pend_p);
+  if (ok && stored_p >= 0) finish(stored_p);
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }

@@ -115,6 +115,17 @@ def test_rmsnorm_and_rope():
     assert rel_err(y, rot) < 1e-2
 
 
+def test_layernorm_large_mean():
+    """Rows with |mean| >> std (mean 40, std 1; a bf16 step at 40 is 0.25): the block-merged
+    per-thread centred statistics match fp32 LayerNorm of the same bf16 values."""
+    torch.manual_seed(7)
+    M, D = 64, 5120
+    x = (torch.randn(M, D, device=DEV) + 40).bfloat16()
+    ref = torch.nn.functional.layer_norm(x.float(), (D,), eps=1e-6)
+    y = ops.layernorm_modulate(x)
+    assert float((y.float() - ref).abs().max()) < 0.05
+
+
 @pytest.mark.parametrize("D", [1000, 4096, 5120, 6144, 8192, 12288])
 def test_norm_vector_shapes_and_scalar_fallback(D):
     """Every launch shape of the row kernels (1..8 vectors per thread at 128 threads, wider CTAs
