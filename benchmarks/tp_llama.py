@@ -30,6 +30,8 @@ def main():
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--collectives", default="fused,nccl",
+                    help="comma list of fused, nccl, fused_ag (fused all-gather only), fused_rs")
     a = ap.parse_args()
     import torch.distributed as dist
 
@@ -52,7 +54,7 @@ def main():
     x0 = torch.randn(R, cfg.dim, device=dev).bfloat16()
     peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("bf16_tflops", 1590.0)
     res = {}
-    for coll in ("fused", "nccl"):
+    for coll in a.collectives.split(","):
         tp.setup(M, collective=coll)
         x = x0.clone()
 
@@ -82,8 +84,11 @@ def main():
     roof = max((gemm_flops + attn_flops) / (peak * 1e9), nvlink / 770e6)
     res.update({"n_gpus": W, "tokens": M, "layers_timed": a.layers, "flops_per_layer_per_rank": gemm_flops + attn_flops,
                 "nvlink_bytes_per_layer_per_rank": nvlink, "roofline_ms_per_layer": round(roof, 4),
-                "fused_frac_of_roofline": round(roof / res["fused_ms_per_layer"], 3),
-                "speedup_fused_vs_nccl": round(res["nccl_ms_per_layer"] / res["fused_ms_per_layer"], 3)})
+                })
+    if "fused_ms_per_layer" in res:
+        res["fused_frac_of_roofline"] = round(roof / res["fused_ms_per_layer"], 3)
+        if "nccl_ms_per_layer" in res:
+            res["speedup_fused_vs_nccl"] = round(res["nccl_ms_per_layer"] / res["fused_ms_per_layer"], 3)
     if rank == 0:
         print(json.dumps(res))
     dist.destroy_process_group()

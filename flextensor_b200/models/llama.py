@@ -149,32 +149,33 @@ class LlamaLayer(nn.Module):
 
         cfg, D = self.cfg, self.cfg.head_dim
         qn, kn = self.hq * D, self.hk * D
-        fused = tp.collective == "fused"
-        if fused:  # RMSNorm of the own rows straight into the all-gather buffer
-            ops.rmsnorm(x_local, self.attn_norm, eps=cfg.eps, out=tp._ag.begin())
-            tp._ag.publish()
-            qkv = tp._ag.gemm(self.wqkv)
-        else:
-            h = ops.rmsnorm(x_local, self.attn_norm, eps=cfg.eps)
-            qkv = ops.linear(tp._nccl.all_gather(h), self.wqkv, None, epi="none")
+        ag_fused = tp.collective in ("fused", "fused_ag")
+        rs_fused = tp.collective in ("fused", "fused_rs")
+
+        def gathered_gemm(norm_w, w, epi):
+            if ag_fused:  # RMSNorm of the own rows straight into the all-gather buffer
+                ops.rmsnorm(x_local, norm_w, eps=cfg.eps, out=tp._ag.begin())
+                tp._ag.publish()
+                return tp._ag.gemm(w, epi=epi)
+            h = tp._nccl.all_gather(ops.rmsnorm(x_local, norm_w, eps=cfg.eps))
+            return ops.linear_swiglu(h, w) if epi == "swiglu" else ops.linear(h, w, None, epi="none")
+
+        def scattered_gemm(a, w):
+            nonlocal x_local
+            if rs_fused:
+                tp._rs.gemm(a, w)
+                tp._rs.reduce(x_local, residual=x_local)
+            else:
+                x_local += tp._nccl.reduce_scatter(ops.linear(a, w, None, epi="none"))
+
+        qkv = gathered_gemm(self.attn_norm, self.wqkv, "none")
         q, k, v = qkv[:, :qn], qkv[:, qn:qn + kn], qkv[:, qn + kn:]
         ops.rope(q, *rope, D, S, out=q)
         ops.rope(k, *rope, D, S, out=k)
         o = ops.attention(q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D), causal=True)
-        o2 = o.view(B * S, -1)
-        if fused:
-            tp._rs.gemm(o2, self.wo)
-            tp._rs.reduce(x_local, residual=x_local)
-            ops.rmsnorm(x_local, self.ffn_norm, eps=cfg.eps, out=tp._ag.begin())
-            tp._ag.publish()
-            f = tp._ag.gemm(self.w_gate_up, epi="swiglu")
-            tp._rs.gemm(f, self.w_down)
-            tp._rs.reduce(x_local, residual=x_local)
-        else:
-            x_local += tp._nccl.reduce_scatter(ops.linear(o2, self.wo, None, epi="none"))
-            h = ops.rmsnorm(x_local, self.ffn_norm, eps=cfg.eps)
-            f = ops.linear_swiglu(tp._nccl.all_gather(h), self.w_gate_up)
-            x_local += tp._nccl.reduce_scatter(ops.linear(f, self.w_down, None, epi="none"))
+        scattered_gemm(o.view(B * S, -1), self.wo)
+        f = gathered_gemm(self.ffn_norm, self.w_gate_up, "swiglu")
+        scattered_gemm(f, self.w_down)
         return x_local
 
     def forward(self, x, B, S, rope, impl="fused", tp=None, cache=None, pos: int = 0):
@@ -306,14 +307,19 @@ class LlamaTP(nn.Module):
         return self
 
     def setup(self, tokens_total: int, group=None, collective: str = "fused") -> None:
+        """``collective``: ``fused`` (all-gather inside the column-parallel GEMMs, reduce-scatter
+        from the row-parallel GEMM epilogues), ``nccl`` (NCCL around plain GEMMs), or one fused
+        side only: ``fused_ag`` / ``fused_rs``."""
         from flextensor_b200.parallel.tp import NcclTP, TPAllGather, TPReduceScatter
 
+        if collective not in ("fused", "nccl", "fused_ag", "fused_rs"):
+            raise ValueError(f"unknown collective {collective!r}")
         self.collective = collective
-        if collective == "fused":
+        self._nccl = NcclTP(group)
+        if collective in ("fused", "fused_ag"):
             self._ag = TPAllGather(tokens_total, self.cfg.dim, group)
+        if collective in ("fused", "fused_rs"):
             self._rs = TPReduceScatter(tokens_total, self.cfg.dim, group)
-        else:
-            self._nccl = NcclTP(group)
 
     def close(self) -> None:
         for o in (self._ag, self._rs):

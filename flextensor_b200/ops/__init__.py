@@ -13,6 +13,7 @@ from flextensor_b200.ops.api import (
     qk_rmsnorm_rope,
     rmsnorm,
     rope,
+    tp_ag_counter_words,
     tp_allgather_gemm,
     tp_gemm_reducescatter,
     tp_reduce,
@@ -20,5 +21,5 @@ from flextensor_b200.ops.api import (
 )
 
 __all__ = ["EPI", "TP_EPI", "attention", "attention_cp", "launch_count", "layernorm_modulate", "linear",
-           "linear_swiglu", "qk_rmsnorm_rope", "rmsnorm", "rope", "tp_allgather_gemm", "tp_gemm_reducescatter",
+           "linear_swiglu", "qk_rmsnorm_rope", "rmsnorm", "rope", "tp_ag_counter_words", "tp_allgather_gemm", "tp_gemm_reducescatter",
            "tp_reduce", "tp_rmsnorm"]

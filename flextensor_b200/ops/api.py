@@ -152,6 +152,12 @@ def tp_allgather_gemm(a_full: torch.Tensor, weight: torch.Tensor, *, peer_a: lis
     return out
 
 
+def tp_ag_counter_words(rows_total: int, world: int) -> int:
+    """int32 scratch words ``tp_allgather_gemm`` needs for ``rows_total`` rows over ``world``
+    ranks: per-peer tickets plus a landed-byte count per 128-row block of every peer."""
+    return world * (2 + (rows_total // world + 127) // 128) if world > 1 else 2 * world
+
+
 def tp_gemm_reducescatter(a: torch.Tensor, weight: torch.Tensor, *, stage: list[int], peer_flags: list[int],
                           rank: int, epoch: int, counters: torch.Tensor) -> None:
     """GEMM -> reduce-scatter, sender side: partial ``a @ weight.T`` rows go straight into the

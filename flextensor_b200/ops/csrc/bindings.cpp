@@ -298,7 +298,9 @@ void tp_ag_gemm(const Tensor& a_full, const Tensor& w, Tensor& out, const c10::o
   const int world = (int)peer_a.size();
   TORCH_CHECK(world >= 1 && world <= ft::kTpMaxRanks && (int)peer_acks.size() == world, "one pointer per rank");
   TORCH_CHECK(peer_a[rank] == reinterpret_cast<uint64_t>(a_full.data_ptr()), "peer_a[rank] must be a_full");
-  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 2 * world, "counters");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt &&
+                  counters.numel() >= ft::tp_ag_counter_words((int)a_full.size(0), world),
+              "counters: tp_ag_counter_words(M, world) int32 words");
   c10::cuda::CUDAGuard g(a_full.device());
   ft::TpGemmProblem p;
   p.M = a_full.size(0);
@@ -648,6 +650,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_cp", &attention_cp);
   m.def("p2p_publish_raw", &p2p_publish_raw);
   m.def("tp_ag_gemm", &tp_ag_gemm);
+  m.def("tp_ag_counter_words", [](int64_t M, int64_t world) { return ft::tp_ag_counter_words((int)M, (int)world); });
   m.def("tp_gemm_rs", &tp_gemm_rs);
   m.def("tp_reduce", &tp_reduce, py::arg("stage"), py::arg("world"), py::arg("rows"), py::arg("out"),
         py::arg("residual"), py::arg("flags"), py::arg("flag_stride"), py::arg("epoch"), py::arg("peer_acks"),

@@ -35,7 +35,7 @@ struct TpGemmProblem {
   void* stage[kTpMaxRanks] = {};         // rank p's staging [world][M/world][N] for this slot
   uint64_t* peer_flags[kTpMaxRanks] = {};// word telling rank p our partial rows are complete
   uint64_t epoch = 0;
-  unsigned int* counters = nullptr;      // scratch: 2*world (all-gather) / 1 (reduce-scatter), zeroed here
+  unsigned int* counters = nullptr;      // scratch: tp_ag_counter_words (all-gather) / 1 (reduce-scatter), zeroed here
   int num_sms = 0;
 };
 
@@ -91,6 +91,12 @@ struct TpRmsProblem {
   unsigned int* counter = nullptr;      // scratch, zeroed here
   int phases = 3;                       // bit 0: sums of squares + publish; bit 1: wait, scale, acknowledge
 };
+
+// Scratch words the all-gather GEMM needs: per-peer claim and done tickets, plus per-peer byte
+// counts of every 128-row block (none with a single rank).
+inline int tp_ag_counter_words(int M, int world) {
+  return world > 1 ? world * (2 + (M / world + 127) / 128) : 2 * world;
+}
 
 cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream);
 cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream);

@@ -61,6 +61,8 @@ struct TpArgs {
   uint64_t epoch;
   unsigned int* claim;
   unsigned int* done;
+  unsigned int* done_blk;  // [world][nblk]: bytes of each BM-row block of each peer's rows landed
+  int nblk;                // BM-row blocks per rank
   int pieces;  // per rank
   // reduce-scatter side
   __nv_bfloat16* stage[kTpMaxRanks];  // rank p's staging base for this slot: [world][rows][N]
@@ -124,23 +126,32 @@ __device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_ful
   uint32_t ph[2] = {0, 0};
   bool loading[2] = {false, false};
   bool ok = true;
-  auto finish = [&](int p) {
-    fence_proxy_async_global();
-    const unsigned int old = atom_add_release_gpu_u32(c.done + p, 1u);
-    if (old + 1 == npieces) {
-      __threadfence_system();
-      st_release_sys_u64(c.peer_acks[p], c.epoch);
-    }
-  };
   // pieces in the pipeline: [0] = the one being loaded, [1] = loaded and being stored
   struct Piece {
     int p;
-    long long at;
+    long long at;  // byte offset in the full buffer
     uint32_t n;
     int st;
   };
+  const long long blk_bytes = (long long)BM * c.row_bytes;
+  // a landed piece: its bytes count toward the (one or two) BM-row blocks it covers, so a tile
+  // can start as soon as its own rows are in; the last piece of a peer acknowledges the peer
+  auto finish = [&](const Piece& q) {
+    fence_proxy_async_global();
+    const long long off = q.at - (long long)q.p * rank_bytes;
+    const int b0 = (int)(off / blk_bytes), b1 = (int)((off + q.n - 1) / blk_bytes);
+    for (int b = b0; b <= b1; b++) {
+      const long long lo = max(off, (long long)b * blk_bytes), hi = min(off + (long long)q.n, (long long)(b + 1) * blk_bytes);
+      atom_add_release_gpu_u32(c.done_blk + q.p * c.nblk + b, (unsigned int)(hi - lo));
+    }
+    const unsigned int old = atom_add_release_gpu_u32(c.done + q.p, 1u);
+    if (old + 1 == npieces) {
+      __threadfence_system();
+      st_release_sys_u64(c.peer_acks[q.p], c.epoch);
+    }
+  };
   Piece prev{-1, 0, 0, 0};
-  int stored_p = -1;  // peer of the piece whose store was committed last (finished one step later)
+  Piece stored{-1, 0, 0, 0};  // the piece whose store was committed last (finished one step later)
   int issued = 0;
   int d = 1;
   bool flagged = false;
@@ -186,8 +197,8 @@ __device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_ful
       bulk_store_s2g(c.local_a + prev.at, stage + prev.st * TP_PIECE, prev.n);
       bulk_commit();
       bulk_wait<1>();  // the store committed one step earlier has landed
-      if (stored_p >= 0) finish(stored_p);
-      stored_p = prev.p;
+      if (stored.p >= 0) finish(stored);
+      stored = prev;
     }
     if (cur.p < 0) break;
     prev = cur;
@@ -202,7 +213,7 @@ __device__ void gather_rows(const TpArgs& c, uint8_t* stage, uint64_t* stage_ful
     }
   }
   bulk_wait<0>();
-  if (ok && stored_p >= 0) finish(stored_p);
+  if (ok && stored.p >= 0) finish(stored);
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
@@ -310,16 +321,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       uint32_t ph = 0;
       bool ok = true;
       uint32_t pend = 0, pend_ph = 0;
-      uint32_t ready = 0;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         int mt, nt;
         tile_coords(tile, p, mt, nt);
         if constexpr (AG) {
-          const int lo = mt * BM / p.rows, hi = min(mt * BM + BM - 1, p.M - 1) / p.rows;
-          for (int q = lo; q <= hi && ok; q++) {
-            if (q == p.rank || (ready >> q & 1u)) continue;
-            ok = wait_done(p.done + q, (unsigned int)p.pieces);
-            ready |= 1u << q;
+          // wait for the BM-row blocks of each owner that this tile's rows fall in
+          const int r0 = mt * BM, r1 = min(mt * BM + BM, p.M);  // rows [r0, r1)
+          for (int q = r0 / p.rows; q <= (r1 - 1) / p.rows && ok; q++) {
+            if (q == p.rank) continue;
+            const long long qb = (long long)q * p.rows;
+            const int lo = (int)(max((long long)r0, qb) - qb), hi = (int)(min((long long)r1, qb + p.rows) - qb);
+            for (int b = lo / BM; b <= (hi - 1) / BM && ok; b++) {
+              const long long bytes = (long long)(min((b + 1) * BM, p.rows) - b * BM) * p.row_bytes;
+              ok = wait_done(p.done_blk + q * p.nblk + b, (unsigned int)bytes);
+            }
           }
           if (!ok) break;
         }
@@ -403,15 +418,55 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph))) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
-      __nv_bfloat16* rowp = nullptr;
-      if (row < p.M) {
-        if constexpr (AG) {
-          rowp = p.C + (size_t)row * p.ldc;
-        } else {
-          const int owner = row / p.rows;
-          rowp = p.stage[owner] + ((size_t)p.rank * p.rows + (row - owner * p.rows)) * p.N;
+      if constexpr (!AG) {
+        // Reduce-scatter: the partial rows go to their owners over NVLink. A thread holds one
+        // row, so direct stores would scatter 16-byte writes over 32 rows per instruction;
+        // instead each warp turns 64 columns of its 32 rows around in shared memory (the idle
+        // gather staging, 4 KB per warp, 16-byte segments XOR-swizzled by row) and stores
+        // 128 contiguous bytes per row, 4 rows per instruction.
+        uint8_t* ws = stage + q * 4096;
+#pragma unroll 1
+        for (int c2 = 0; c2 < BN / 64; c2++) {
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + (c2 * 2 + hh) * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int v = 0; v < 4; v++) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+              w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+              w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+              w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+              const int seg = hh * 4 + v;
+              *reinterpret_cast<uint4*>(ws + lane * 128 + ((seg ^ (lane & 7)) * 16)) = w;
+            }
+          }
+          __syncwarp();
+          const int col0 = nt * BN + c2 * 64;
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const int rr = k * 4 + (lane >> 3), seg = lane & 7;
+            const int grow = mt * BM + q * 32 + rr;
+            const int col = col0 + seg * 8;
+            if (grow < p.M && col < p.N) {
+              const uint4 w = *reinterpret_cast<const uint4*>(ws + rr * 128 + ((seg ^ (rr & 7)) * 16));
+              const int owner = grow / p.rows;
+              *reinterpret_cast<uint4*>(p.stage[owner] + ((size_t)p.rank * p.rows + (grow - owner * p.rows)) * p.N +
+                                        col) = w;
+            }
+          }
+          __syncwarp();
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+        continue;
       }
+      __nv_bfloat16* rowp = row < p.M ? p.C + (size_t)row * p.ldc : nullptr;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         uint32_t r[32];
@@ -718,9 +773,12 @@ cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream) {
   a.ldc = g.ldc;
   a.claim = g.counters;
   a.done = g.counters + g.world;
+  a.done_blk = g.counters + 2 * g.world;
+  a.nblk = (a.rows + BM - 1) / BM;
+  if (a.row_bytes * BM > 0xffffffffll) return cudaErrorInvalidValue;  // block byte counts are u32
   a.pieces = (int)((a.row_bytes * a.rows + TP_PIECE - 1) / TP_PIECE);
   a.m_rot = (g.rank * a.rows) / BM;
-  e = cudaMemsetAsync(g.counters, 0, 2 * sizeof(unsigned int) * g.world, stream);
+  e = cudaMemsetAsync(g.counters, 0, sizeof(unsigned int) * (size_t)tp_ag_counter_words(g.M, g.world), stream);
   if (e != cudaSuccess) return e;
   CUtensorMap tA, tB;
   if (!make_tmap_2d_bf16(&tA, local, g.K, g.M, g.K, BK, BM)) return cudaErrorInvalidValue;
@@ -734,7 +792,7 @@ cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream) {
   const int bn = g.N >= 256 ? 256 : 128;
   cudaError_t e = fill_common(g, a, bn, false);
   if (e != cudaSuccess) return e;
-  if (g.counters == nullptr || g.epi == TP_EPI_SWIGLU) return cudaErrorInvalidValue;
+  if (g.counters == nullptr || g.epi != TP_EPI_NONE) return cudaErrorInvalidValue;  // partial sums: no epilogue op
   for (int r = 0; r < g.world; r++) {
     if (g.stage[r] == nullptr || g.peer_flags[r] == nullptr) return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(g.stage[r]) & 15) return cudaErrorMisalignedAddress;

@@ -50,7 +50,10 @@ class TPAllGather:
         self.heap = SymmetricHeap(hdr + N_SLOTS * self.slot_bytes, group, dev)
         self.f = _Flags(self.heap, self.world)
         self.off = [hdr + s * self.slot_bytes for s in range(N_SLOTS)]
-        self.counters = torch.zeros(2 * self.world, dtype=torch.int32, device=f"cuda:{dev}")
+        from flextensor_b200.ops.api import tp_ag_counter_words
+
+        self.counters = torch.zeros(tp_ag_counter_words(rows_total, self.world), dtype=torch.int32,
+                                    device=f"cuda:{dev}")
         self.epochs = [0] * N_SLOTS
         self.calls = 0
         self._cur = None

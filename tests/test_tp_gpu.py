@@ -37,7 +37,7 @@ def test_allgather_gemm(W, R, K, N, epi, rank):
         bufs.append(b)
     flags = torch.zeros(W, dtype=torch.int64, device=DEV)
     acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
-    counters = torch.zeros(2 * W, dtype=torch.int32, device=DEV)
+    counters = torch.zeros(ops.tp_ag_counter_words(M, W), dtype=torch.int32, device=DEV)
     for epoch in (1, 2):
         flags.fill_(epoch)
         out = ops.tp_allgather_gemm(bufs[rank], w, peer_a=[b.data_ptr() for b in bufs], flags_ptr=flags.data_ptr(),
