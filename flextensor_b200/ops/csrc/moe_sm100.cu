@@ -392,14 +392,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
       }
+      if constexpr (DISPATCH) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = nt * BN + c * 32;
-        if (rowp != nullptr && col0 < a.N) {
-          if constexpr (DISPATCH) {  // SwiGLU: (gate, up) column pairs -> 16 outputs
+        for (int c = 0; c < BN / 32; c++) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nt * BN + c * 32;
+          if (rowp != nullptr && col0 < a.N) {  // SwiGLU: (gate, up) column pairs -> 16 outputs
             __nv_bfloat16* dst = rowp + col0 / 2;
 #pragma unroll
             for (int h = 0; h < 2; h++) {
@@ -414,18 +414,46 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               u.w = pack_bf16x2(o[6], o[7]);
               *reinterpret_cast<uint4*>(dst + h * 8) = u;
             }
-          } else {
-            __nv_bfloat16* dst = rowp + col0;
+          }
+        }
+      } else {
+        // Combine: the rows go to their token's rank over NVLink. As in the tensor-parallel
+        // reduce-scatter, each warp turns 64 columns of its 32 rows around in shared memory (the
+        // gather staging, idle in this GEMM; 4 KB per warp, 16-byte segments XOR-swizzled by row)
+        // and stores 128 contiguous bytes per row, 4 rows per instruction; a row's destination
+        // comes from the lane that owns it.
+        uint8_t* ws = &sm.stage[0][0] + q * 4096;
+        const unsigned long long mydst = reinterpret_cast<unsigned long long>(rowp);
+#pragma unroll 1
+        for (int c2 = 0; c2 < BN / 64; c2++) {
 #pragma unroll
-            for (int h = 0; h < 4; h++) {
+          for (int hh = 0; hh < 2; hh++) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + (c2 * 2 + hh) * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int v = 0; v < 4; v++) {
               uint4 u;
-              u.x = pack_bf16x2(__uint_as_float(r[h * 8 + 0]), __uint_as_float(r[h * 8 + 1]));
-              u.y = pack_bf16x2(__uint_as_float(r[h * 8 + 2]), __uint_as_float(r[h * 8 + 3]));
-              u.z = pack_bf16x2(__uint_as_float(r[h * 8 + 4]), __uint_as_float(r[h * 8 + 5]));
-              u.w = pack_bf16x2(__uint_as_float(r[h * 8 + 6]), __uint_as_float(r[h * 8 + 7]));
-              *reinterpret_cast<uint4*>(dst + h * 8) = u;
+              u.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+              u.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+              u.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+              u.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+              const int seg = hh * 4 + v;
+              *reinterpret_cast<uint4*>(ws + lane * 128 + ((seg ^ (lane & 7)) * 16)) = u;
             }
           }
+          __syncwarp();
+          const int col0 = nt * BN + c2 * 64;
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const int rr = k * 4 + (lane >> 3), seg = lane & 7;
+            const unsigned long long d = __shfl_sync(0xffffffffu, mydst, rr);
+            const int col = col0 + seg * 8;
+            if (d != 0ull && col < a.N)
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d) + col) =
+                  *reinterpret_cast<const uint4*>(ws + rr * 128 + ((seg ^ (rr & 7)) * 16));
+          }
+          __syncwarp();
         }
       }
       tc_fence_before();
