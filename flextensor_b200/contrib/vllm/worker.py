@@ -38,6 +38,8 @@ _register_env_var("FT_VLLM_FUSED_TP")
 
 from vllm.v1.worker.gpu_worker import Worker  # noqa: E402
 
+from flextensor_b200.contrib.vllm import loader as _loader  # noqa: E402,F401 - registers load_format "flextensor"
+
 _selector = os.environ.get("FT_VLLM_USE_V2_WORKER", "1")
 if _selector not in ("0", "1"):
     raise ValueError(f"FT_VLLM_USE_V2_WORKER must be '0' (legacy) or '1' (v2), got {_selector!r}")

@@ -13,6 +13,8 @@ def main():
               max_model_len=256, dtype="bfloat16", seed=0)
     if worker != "default":
         kw["worker_cls"] = worker
+    if len(sys.argv) > 3:
+        kw["load_format"] = sys.argv[3]
     llm = LLM(**kw)
     prompts = [{"prompt_token_ids": [(7 * i + 3 * j) % 2000 + 10 for j in range(24)]} for i in range(3)]
     outs = llm.generate(prompts, SamplingParams(max_tokens=16, temperature=0.0, detokenize=False))
