@@ -15,8 +15,10 @@ KV cache with the ring slots already allocated. Selection of compile/graph behav
 vLLM's: under vLLM's compile mode the trap boundaries are the opaque custom ops
 ``flextensor_b200::pre_compute`` / ``post_compute`` (``external_compile``); CUDA-graph
 replays use device-event timing (``offload_timing="cuda_graph"`` when timing is on).
+With ``FT_SHM_ENABLED=1`` (plus a read-only saved profile and ``FT_SHM_NAMESPACE``), vLLM's local
+data-parallel replicas share one host copy of the weights (``contrib/vllm/shared.py``).
 Parity: ``src/flextensor/contrib/vllm/v2/worker.py:235-616``. Rejected like the reference:
-expert parallelism / EPLB, and the shared-memory path with TP or PP > 1.
+expert parallelism / EPLB, and the shared-memory path outside its validated topology.
 """
 
 from __future__ import annotations
@@ -39,6 +41,7 @@ _register_env_var("FT_VLLM_FUSED_TP")
 from vllm.v1.worker.gpu_worker import Worker  # noqa: E402
 
 from flextensor_b200.contrib.vllm import loader as _loader  # noqa: E402,F401 - registers load_format "flextensor"
+from flextensor_b200.contrib.vllm import shared as _shared  # noqa: E402,F401 - registers "flextensor_shm"
 
 _selector = os.environ.get("FT_VLLM_USE_V2_WORKER", "1")
 if _selector not in ("0", "1"):
@@ -118,6 +121,50 @@ class FlexTensorOffloadWorker(Worker):
         max_rows = self.vllm_config.scheduler_config.max_num_batched_tokens
         patch_row_parallel(self.model_runner.get_model(), max_rows, get_tp_group().cpu_group)
 
+    def _load_shared(self, cfg, *args, **kwargs) -> None:
+        """Data-parallel replicas sharing one host copy of the weights (``contrib/vllm/shared.py``):
+        vLLM loads through the ``flextensor_shm`` format, which restores the model from the saved
+        profile through a shared session (creator loads the checkpoint, followers attach)."""
+        import atexit
+
+        from vllm.model_executor.offloader.base import NoopOffloader, get_offloader, set_offloader
+
+        import flextensor_b200 as ft
+        from flextensor_b200.contrib.vllm.shared import SHM_LOAD_FORMAT, SharedLoad, active_shared_load
+        from flextensor_b200.shared_offload import SharedOffloadSession
+
+        prev = get_offloader()
+        if not isinstance(prev, NoopOffloader):
+            raise FlexTensorWorkerError(f"another vLLM offloader is active: {type(prev).__name__}")
+        session = SharedOffloadSession(cfg.shm_namespace, wait_timeout=cfg.shm_wait_timeout)
+        lc = self.vllm_config.load_config
+        ctx = SharedLoad(session=session, config=cfg, profile_directory=cfg.profile_storage_dir, device=self.device,
+                         underlying_format=lc.load_format, manager_name=MANAGER_NAME)
+        boot = FlexTensorBootstrapOffloader()
+        set_offloader(boot)
+        orig = lc.load_format
+        try:
+            lc.load_format = SHM_LOAD_FORMAT
+            try:
+                with active_shared_load(ctx):
+                    super().load_model(*args, **kwargs)
+            finally:
+                lc.load_format = orig
+            if ctx.model is None or ctx.model is not self.model_runner.get_model():
+                raise FlexTensorWorkerError("the shared load did not hand its model to the model runner")
+            om = ft.get_offload_manager(MANAGER_NAME)
+            boot.manager = om
+            self._ft_manager = om
+            self._ft_session = session
+            atexit.register(session.close)
+            LOGGER.info("FlexTensor shared host weights: role=%s namespace=%s", ctx.role, cfg.shm_namespace)
+        except BaseException:
+            try:
+                session.close()
+            finally:
+                set_offloader(prev)
+            raise
+
     def load_model(self, *args, **kwargs) -> None:
         if self.device.index is None:
             raise FlexTensorWorkerError(f"worker device needs an explicit index, got {self.device}")
@@ -140,6 +187,13 @@ class FlexTensorOffloadWorker(Worker):
             timing = "cuda_graph" if graphs else "eager"
         cfg = cfg.model_copy(update={"include_patterns": inc, "exclude_patterns": exc,
                                      "external_compile": external_compile, "offload_timing": timing})
+
+        if cfg.shm_enabled:
+            from flextensor_b200.contrib.vllm.shared import validate_shared_topology
+
+            validate_shared_topology(self.vllm_config, cfg)
+            self._load_shared(cfg, *args, **kwargs)
+            return
 
         from vllm.model_executor.offloader.base import NoopOffloader, get_offloader, set_offloader
 
