@@ -26,10 +26,12 @@ label's ``enter`` and dropped at its ``exit`` (``src/flextensor/loaders.py:677-9
 from __future__ import annotations
 
 import logging
+import os
 from dataclasses import dataclass, field
 
 import torch
 
+from flextensor_b200.config import _register_env_var
 from flextensor_b200.core.host_store import HostBlock, PackedEntry
 from flextensor_b200.instrumentation.core import instrumentable
 
@@ -44,6 +46,23 @@ class SlotPlan:
     slot_bytes: dict[int, int]
     host_blocks: dict[str, HostBlock]      # transfer label -> packed host bytes
     preload: list[str] = field(default_factory=list)  # transfer labels to issue at construction
+
+
+# Debug switches (read once at import). FT_DEBUG_CANARY=1: every locally allocated ring slot is
+# framed by two 4 KB guard regions filled with 0xA5, verified after each forward, so a kernel or a
+# copy that writes past its slot is reported with the slot's id instead of corrupting a neighbour.
+# FT_NVTX=1: an NVTX range per trap ("ft:<label>") and per host->device block issue
+# ("ft:h2d:<label>") for nsys timelines.
+CANARY_BYTES = 4096
+CANARY_VALUE = 0xA5
+_register_env_var("FT_DEBUG_CANARY")
+_register_env_var("FT_NVTX")
+DEBUG_CANARY = os.environ.get("FT_DEBUG_CANARY", "0") == "1"
+NVTX = os.environ.get("FT_NVTX", "0") == "1"
+
+
+class SlotGuardError(RuntimeError):
+    pass
 
 
 @instrumentable
@@ -64,12 +83,31 @@ class BlockLoader:
         self.c2t = {c: t for t, c in plan.t2c.items()}
         self.compute_slot = {c: plan.transfer_slot[t] for t, c in plan.t2c.items()}
         alloc = getattr(engine, "slot_tensor", None)
-        self.slots: dict[int, torch.Tensor] = {
-            s: (alloc(s, n) if alloc is not None else torch.empty(max(n, 256), dtype=torch.uint8, device=self.device))
-            for s, n in plan.slot_bytes.items()
-        }
+        self.canary = DEBUG_CANARY and alloc is None  # symmetric-heap slots have no room for guards
+        self._guards: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        self.slots: dict[int, torch.Tensor] = {}
+        for s, n in plan.slot_bytes.items():
+            if alloc is not None:
+                self.slots[s] = alloc(s, n)
+            elif self.canary:
+                size, g = max(n, 256), CANARY_BYTES
+                buf = torch.empty(size + 2 * g, dtype=torch.uint8, device=self.device)
+                buf[:g].fill_(CANARY_VALUE)
+                buf[g + size:].fill_(CANARY_VALUE)
+                self.slots[s] = buf[g:g + size]
+                self._guards[s] = (buf[:g], buf[g + size:])
+            else:
+                self.slots[s] = torch.empty(max(n, 256), dtype=torch.uint8, device=self.device)
         self._pass_active = False
         self._closed = False
+
+    def check_canaries(self) -> list[int]:
+        """Slots whose guard regions no longer hold the fill pattern (empty without FT_DEBUG_CANARY)."""
+        bad = []
+        for s, (lo, hi) in self._guards.items():
+            if bool((lo != CANARY_VALUE).any()) or bool((hi != CANARY_VALUE).any()):
+                bad.append(s)
+        return bad
 
     # -------------------------------------------------------------- views
     def slot_view(self, transfer_label: str, e: PackedEntry) -> torch.Tensor:
@@ -114,10 +152,14 @@ class BlockLoader:
         blk = self.plan.host_blocks[t]
         n = blk.nbytes
         slot = self.plan.transfer_slot[t]
+        if NVTX:
+            torch.cuda.nvtx.range_push(f"ft:h2d:{t}")
         if blk.stripe_only:
             self.engine.submit_stripe(slot, blk.data, self.plan.t2c[t], n)
         else:
             self.engine.submit(slot, self.slots[slot][:n], blk.data, self.plan.t2c[t])
+        if NVTX:
+            torch.cuda.nvtx.range_pop()
         self.policy.on_schedule(t, self.plan.t2c[t])
 
     def preload(self) -> None:
@@ -142,6 +184,8 @@ class BlockLoader:
         self.preload()
 
     def enter(self, label: str) -> None:
+        if NVTX:
+            torch.cuda.nvtx.range_push(f"ft:{label}")
         if label == self.first:
             if self._pass_active:
                 self.recover()
@@ -164,6 +208,8 @@ class BlockLoader:
             self.engine.finish_use(self.compute_slot[label])
         if label == self.last:
             self.join_after_forward()
+        if NVTX:
+            torch.cuda.nvtx.range_pop()
 
     def join_after_forward(self) -> None:
         if self._pass_active:
@@ -172,6 +218,10 @@ class BlockLoader:
             self.policy.on_piece_join(at_last_layer=True)
             if self.timing is not None:
                 self.timing.on_pass_end(self.engine)
+            if self.canary:
+                bad = self.check_canaries()
+                if bad:
+                    raise SlotGuardError(f"ring slot(s) {bad}: a write went past the slot into its guard region")
 
     def piece_join(self) -> None:
         """A piecewise CUDA-graph boundary inside the forward: join the copy stream into the
