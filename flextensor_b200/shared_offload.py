@@ -133,6 +133,12 @@ class SharedOffloadSession:
                     pass
             raise
 
+    def __enter__(self) -> "SharedOffloadSession":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
     def close(self, name: str | None = None) -> None:
         names = [name] if name is not None else list(self._coords)
         for n in names:

@@ -14,6 +14,9 @@ def _load():
     spec = importlib.util.spec_from_file_location("ltx_serve", os.path.join(ROOT, "examples", "ltx_serving",
                                                                               "serve.py"))
     mod = importlib.util.module_from_spec(spec)
+    import sys
+
+    sys.modules[spec.name] = mod  # dataclasses resolve annotations through sys.modules
     spec.loader.exec_module(mod)
     return mod
 
@@ -45,3 +48,26 @@ def test_denoise_over_http():
     finally:
         stop.set()
         th.join(5)
+
+
+def test_profile_then_serve_from_profiles(tmp_path):
+    """``profile`` saves one profile per stage manager (text encoder, DiT); ``serve`` restores both
+    from them (no discovery / profiling) and answers a request; with ``--shm-namespace`` the
+    stages come through a shared-memory session (this single process is the creator)."""
+    import flextensor_b200 as ft
+
+    mod = _load()
+    pdir = str(tmp_path / "prof")
+    saved = mod.main(["profile", "--profile-dir", pdir, "--tiny", "--cpu"])
+    assert saved is None
+    for stage in ("text", "dit"):
+        assert os.path.exists(os.path.join(pdir, stage, "profile.json"))
+        ft.release(stage)
+    out = mod.main(["serve", "--profile-dir", pdir, "--tiny", "--cpu", "--once"])
+    assert out["ok"] and out["steps"] == 2
+    for stage in ("text", "dit"):
+        assert ft.get_offload_manager(stage).phase.value == "inference"
+        ft.release(stage)
+    ns = f"ftserve_{os.getpid()}"
+    out2 = mod.main(["serve", "--profile-dir", pdir, "--tiny", "--cpu", "--once", "--shm-namespace", ns])
+    assert out2["ok"] and out2["checksum"] == out["checksum"]
