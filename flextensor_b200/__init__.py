@@ -4,7 +4,21 @@ Public API parity with the reference facade (``src/flextensor/__init__.py:31-141
 ``import flextensor_b200 as flextensor`` gives the same names.
 """
 
-from flextensor_b200._version import __version__
+import os as _os
+
+# Runtime type checks of the whole package (beartype's import hook) before any submodule loads:
+# on with ENABLE_BEARTYPE=1, and never when DISABLE_BEARTYPE is set (the reference's switch). They
+# are off by default here because they sit on the per-trap hot path of inference.
+if _os.environ.get("ENABLE_BEARTYPE", "0") == "1" and not _os.environ.get("DISABLE_BEARTYPE"):
+    try:
+        from beartype import BeartypeConf as _BeartypeConf
+        from beartype.claw import beartype_this_package as _beartype_this_package
+
+        _beartype_this_package(conf=_BeartypeConf(is_pep484_tower=True))  # an int is a valid float
+    except ImportError:  # beartype not installed: run unchecked
+        pass
+
+from flextensor_b200._version import __version__  # noqa: E402
 from flextensor_b200.config import (
     OffloadConfig,
     PinnedMemoryMode,

@@ -40,7 +40,7 @@ _register_env_var(OUTPUT_DIR_ENV)
 _GIB = float(1 << 30)
 
 
-def device_memory(device: torch.device) -> dict[str, float]:
+def device_memory(device: torch.device) -> dict[str, int | float]:
     """Device memory figures in bytes (plus a wall-clock timestamp)."""
     free, total = torch.cuda.mem_get_info(device)
     reserved = torch.cuda.memory_reserved(device)
@@ -50,7 +50,7 @@ def device_memory(device: torch.device) -> dict[str, float]:
             "timestamp": time.time()}
 
 
-def host_memory() -> dict[str, float]:
+def host_memory() -> dict[str, int]:
     try:
         import psutil
 

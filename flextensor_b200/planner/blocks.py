@@ -28,7 +28,7 @@ from typing import Protocol
 class MemoryBlockPlanner:
     """Path-graph colouring of labels (execution order) onto slots."""
 
-    def __init__(self, layer_sizes: "OrderedDict[str, int] | dict[str, int]", cyclic: bool = False):
+    def __init__(self, layer_sizes: OrderedDict[str, int] | dict[str, int], cyclic: bool = False):
         """``cyclic``: the schedule wraps across forwards (the last transfer label feeds the first
         compute label of the next forward), so the first and last labels are adjacent too; an
         odd number of labels then needs three slots."""
@@ -125,7 +125,7 @@ class MemoryBlockPlanner:
 
 
 class AssignmentStrategy(Protocol):
-    def assign(self, label_sizes: "OrderedDict[str, int]") -> dict[str, int]: ...
+    def assign(self, label_sizes: OrderedDict[str, int]) -> dict[str, int]: ...
 
 
 def _valid(order: list[str], where: dict[str, int], cyclic: bool) -> bool:
@@ -143,7 +143,7 @@ class StrictRoundRobinAssignment:
     def __init__(self, n_blocks: int | None = None):
         self.n_blocks = n_blocks
 
-    def assign(self, label_sizes: "OrderedDict[str, int]", n_blocks: int | None = None) -> dict[str, int]:
+    def assign(self, label_sizes: OrderedDict[str, int], n_blocks: int | None = None) -> dict[str, int]:
         n = n_blocks or self.n_blocks or 2
         return {label: k % n for k, label in enumerate(label_sizes)}
 
@@ -181,7 +181,7 @@ class OptimizedRoundRobinAssignment:
             cap[best] = max(cap[best], sizes[label])
         return where
 
-    def assign(self, label_sizes: "OrderedDict[str, int]", n_blocks: int | None = None) -> dict[str, int]:
+    def assign(self, label_sizes: OrderedDict[str, int], n_blocks: int | None = None) -> dict[str, int]:
         order = list(label_sizes)
         if not order:
             return {}

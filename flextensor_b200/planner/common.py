@@ -36,7 +36,7 @@ def validate_memory_params(scale: float) -> None:
 
 def compute_label_to_size_map(
     layer_stats: list[LayerStatistics], strategy_map: dict[str, list[TensorStatistics]]
-) -> "OrderedDict[str, int]":
+) -> OrderedDict[str, int]:
     out: OrderedDict[str, int] = OrderedDict()
     for layer in layer_stats:
         size = sum(t.size_bytes for t in strategy_map.get(layer.label, ()))

@@ -29,7 +29,7 @@ _LIB.define("post_compute(Tensor(a!) carrier, str offload_unit_name, int manager
 
 @dataclass
 class _State:
-    manager: "weakref.ref | None" = None
+    manager: weakref.ref | None = None
     profiling: bool = False
     starts: dict = field(default_factory=dict)
     events: list = field(default_factory=list)

@@ -68,7 +68,7 @@ class StrategyReplanStatus:
 _ONE_SHOT = ("skip_discovery", "offload_timing", "piecewise_prefetch", "profile_mode", "transfer_mode")
 
 
-def _diagnostic_snapshot(label: str, om: "OffloadManager | None") -> None:
+def _diagnostic_snapshot(label: str, om: OffloadManager | None) -> None:
     try:
         import psutil
 
