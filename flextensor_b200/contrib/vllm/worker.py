@@ -55,6 +55,24 @@ class FlexTensorWorkerError(RuntimeError):
     pass
 
 
+def ensure_drafter_on_device(model_runner, device) -> bool:
+    """Speculative decoding: vLLM keeps the drafter at ``model_runner.drafter.model``. Its layers
+    pass through the bootstrap offloader too (host-staged) but FlexTensor takes over only the main
+    model, so the drafter must go back to the device, and BEFORE the takeover: a drafter module
+    that shares a tensor with the main model (e.g. ``embed_tokens``) would otherwise move after
+    FlexTensor recorded that tensor. Returns whether a drafter was moved."""
+    drafter = getattr(model_runner, "drafter", None)
+    if drafter is None:
+        return False
+    model = getattr(drafter, "model", None)
+    if model is None or not callable(getattr(model, "to", None)):
+        LOGGER.warning("speculative drafter without a movable .model (%s): it stays where vLLM put it",
+                       type(drafter).__name__)
+        return False
+    model.to(device)
+    return True
+
+
 def _validate(vllm_config, cfg) -> None:
     par = vllm_config.parallel_config
     if getattr(par, "enable_expert_parallel", False) or getattr(par, "enable_eplb", False):
@@ -208,6 +226,7 @@ class FlexTensorOffloadWorker(Worker):
         try:
             super().load_model(*args, **kwargs)
             raw = self.model_runner.get_model()
+            ensure_drafter_on_device(self.model_runner, self.device)
             before = torch.cuda.memory_allocated(self.device)
             prof = cfg.profile_storage_dir
             if prof and os.path.exists(os.path.join(prof, "profile.json")):

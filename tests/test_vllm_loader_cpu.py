@@ -84,3 +84,22 @@ def test_loader_registered_with_vllm():
 
     assert L.FlexTensorModelLoader is not None
     assert model_loader._LOAD_FORMAT_TO_MODEL_LOADER["flextensor"] is L.FlexTensorModelLoader
+
+
+def test_drafter_moved_before_takeover():
+    pytest.importorskip("vllm")
+    from types import SimpleNamespace
+
+    from flextensor_b200.contrib.vllm.worker import ensure_drafter_on_device
+
+    moved = []
+
+    class _M(nn.Module):
+        def to(self, *a, **k):
+            moved.append(a)
+            return self
+
+    assert ensure_drafter_on_device(SimpleNamespace(), "cuda:0") is False
+    assert ensure_drafter_on_device(SimpleNamespace(drafter=SimpleNamespace(model=None)), "cuda:0") is False
+    assert ensure_drafter_on_device(SimpleNamespace(drafter=SimpleNamespace(model=_M())), "cuda:3") is True
+    assert moved == [("cuda:3",)]
