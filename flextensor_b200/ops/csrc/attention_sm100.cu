@@ -704,6 +704,333 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Experimental variant (timing comparisons, ``_diag_mode`` 200 + EMU): ONE 128-query tile per CTA
+// with S double-buffered in TMEM, so the QK^T of block j+1 and j+2 no longer waits on the softmax
+// of block j. TMEM: S0 (columns 0-127), S1 (128-255), O (256-383). MMA issue order:
+//   S(0) S(1) | PV(0) S(2) | PV(1) S(3) | ...     S(j+2) reuses the columns PV(j) reads as P.
+// The softmax warps run block after block without waiting on the tensor core (the S they need was
+// issued one block earlier). P barriers are per S buffer, so the softmax running one block ahead
+// never completes a phase the MMA warp has not seen. 192 threads: warps 0-3 softmax/epilogue (rows),
+// warp 4 TMEM owner + MMA issuer, warp 5 TMA producer. K/V traffic from L2 is twice the 2-tile
+// kernel's (each CTA reads the whole K/V of its head for 128 queries).
+struct SmemOne {
+  uint8_t q[2 * CHUNK];
+  uint8_t k[KV_STAGES][2 * CHUNK];
+  uint8_t v[KV_STAGES][2 * CHUNK];
+  uint64_t q_full;
+  uint64_t k_full[KV_STAGES], k_empty[KV_STAGES], v_full[KV_STAGES], v_empty[KV_STAGES];
+  uint64_t s_full[2], p_half[2], p_full[2], o_done;
+  uint64_t o_final;  // committed once, after the last PV: o_done can lag two phases at the end
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+constexpr int NTHREADS1 = 192;
+
+template <int EMU>
+__global__ void __launch_bounds__(NTHREADS1, 1)
+    attn1_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemOne& sm = *reinterpret_cast<SmemOne*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x % a.n_qblocks;
+  const int h = (blockIdx.x / a.n_qblocks) % a.Hq;
+  const int b = blockIdx.x / (a.n_qblocks * a.Hq);
+  const int hk = h / (a.Hq / a.Hk);
+  const int q0 = qb * TILE;
+  int n_kv = (a.Sk + TILE - 1) / TILE;
+  if (a.causal) n_kv = min(n_kv, (q0 + TILE + TILE - 1) / TILE);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < KV_STAGES; s++) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    for (int u = 0; u < 2; u++) {
+      mbar_init(&sm.s_full[u], 1);
+      mbar_init(&sm.p_half[u], 4);
+      mbar_init(&sm.p_full[u], 4);
+    }
+    mbar_init(&sm.o_done, 1);
+    mbar_init(&sm.o_final, 1);
+    mbar_init(&sm.drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+
+  if (warp == 5) {
+    // ------------------------------------------------------------------ TMA producer
+    auto wait_tma = [](uint64_t* bar, uint32_t ph) { return mbar_wait_t<kWaitSleep>(bar, ph); };
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(&sm.q_full, 2 * CHUNK);
+      for (int c = 0; c < 2; c++) tma_load_3d(sm.q + c * CHUNK, &tmQ, &sm.q_full, h * HD + c * 64, q0, b);
+      bool ok = true;
+      uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!wait_tma(&sm.k_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.k_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++) tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, j * TILE, b);
+        kpend |= 1u << s;
+        kph = (kph & ~(1u << s)) | (ph << s);
+        if (!wait_tma(&sm.v_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.v_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++) tma_load_3d(sm.v[s] + c * CHUNK, &tmV, &sm.v_full[s], hk * HD + c * 64, j * TILE, b);
+        vpend |= 1u << s;
+        vph = (vph & ~(1u << s)) | (ph << s);
+      }
+      if (!ok) {  // unwinding: every issued load must land before the CTA exits
+        spin_drain(&sm.q_full, 0);
+        for (int s = 0; s < KV_STAGES; s++) {
+          if (kpend >> s & 1) spin_drain(&sm.k_full[s], (kph >> s) & 1);
+          if (vpend >> s & 1) spin_drain(&sm.v_full[s], (vph >> s) & 1);
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idS = umma_idesc_bf16_f32(TILE, TILE);
+      constexpr uint32_t idO = umma_idesc_bf16_f32(TILE, HD, false, true);  // V is MN-major
+      bool ok = mbar_wait(&sm.q_full, 0);
+      const uint64_t dq = umma_desc_kmajor_sw128(smem_u32(sm.q));
+      auto issue_S = [&](int j) {  // S(j) into buffer j % 2 from K stage j % KV_STAGES
+        const int s = j % KV_STAGES;
+        const uint64_t dk = umma_desc_kmajor_sw128(smem_u32(sm.k[s]));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+          const uint32_t off = ((kk >> 2) * CHUNK + (kk & 3) * 32) >> 4;
+          umma_bf16_ss(tbase + (j & 1) * 128, dq + off, dk + off, idS, kk > 0);
+        }
+        umma_commit(&sm.s_full[j & 1]);
+        umma_commit(&sm.k_empty[s]);
+      };
+      auto issue_PV_part = [&](int j, int k0, int k1) {
+        const uint64_t dv = umma_desc_mnmajor_sw128(smem_u32(sm.v[j % KV_STAGES]), CHUNK);
+#pragma unroll
+        for (int kk = k0; kk < k1; kk++)
+          umma_bf16_ts(tbase + 256, tbase + (j & 1) * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idO, (j | kk) != 0);
+      };
+      for (int j = 0; ok && j < 2 && j < n_kv; j++) {
+        ok = mbar_wait(&sm.k_full[j % KV_STAGES], (j / KV_STAGES) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_S(j);
+      }
+      for (int j = 0; ok && j < n_kv; j++) {
+        const int s = j % KV_STAGES;
+        const uint32_t pph = (j >> 1) & 1;  // phase of this S buffer's P barriers
+        if (!mbar_wait(&sm.v_full[s], (j / KV_STAGES) & 1) || !mbar_wait(&sm.p_half[j & 1], pph)) {
+          ok = false;
+          break;
+        }
+        trace_at(a, 0, j);
+        tc_fence_after();
+        issue_PV_part(j, 0, TILE / 32);
+        if (!mbar_wait(&sm.p_full[j & 1], pph)) {
+          ok = false;
+          break;
+        }
+        trace_at(a, 18, j);
+        tc_fence_after();
+        issue_PV_part(j, TILE / 32, TILE / 16);
+        umma_commit(&sm.o_done);
+        umma_commit(&sm.v_empty[s]);
+        if (j == n_kv - 1) umma_commit(&sm.o_final);
+        if (j + 2 < n_kv) {
+          if (!mbar_wait(&sm.k_full[(j + 2) % KV_STAGES], ((j + 2) / KV_STAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_S(j + 2);
+          trace_at(a, 1, j);
+        }
+      }
+      if (!ok) {
+        umma_commit(&sm.drain);
+        spin_drain(&sm.drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int quad = warp;           // TMEM lane quadrant = rows 32*quad .. +31
+    const int r = quad * 32 + lane;
+    const int qpos = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tO = tbase + 256 + lane_off;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; j++) {
+      const int kbase = j * TILE;
+      const uint32_t tS = tbase + (j & 1) * 128 + lane_off;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (r == 0) trace_at(a, 4, j);
+      const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0);
+      uint32_t v[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld_32x32b_x32(tS + c * 32, v[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 4; c++) reg_fence32(v[c]);
+      if (r == 0) trace_at(a, 5, j);
+      if (masked) {
+        const int lim = min(a.Sk, a.causal ? qpos + 1 : a.Sk) - kbase;
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+          for (int e = 0; e < 32; e++)
+            if (c * 32 + e >= lim) v[c][e] = 0xff800000u;
+      }
+      float mx;
+      {
+        float m0 = __uint_as_float(v[0][0]), m1 = __uint_as_float(v[1][0]);
+        float m2 = __uint_as_float(v[2][0]), m3 = __uint_as_float(v[3][0]);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          m0 = max3(m0, __uint_as_float(v[0][e]), __uint_as_float(v[0][e + 1]));
+          m1 = max3(m1, __uint_as_float(v[1][e]), __uint_as_float(v[1][e + 1]));
+          m2 = max3(m2, __uint_as_float(v[2][e]), __uint_as_float(v[2][e + 1]));
+          m3 = max3(m3, __uint_as_float(v[3][e]), __uint_as_float(v[3][e + 1]));
+        }
+        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+      }
+      mx *= a.scale_log2;
+      const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
+      const bool rescale = __any_sync(0xffffffffu, need);
+      float alpha = 1.f;
+      if (rescale) {
+        const float m_new = fmaxf(m, mx);
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+        l *= alpha;
+        m = m_new;
+      }
+      const float msub = (m == -INFINITY) ? 0.f : m;
+      if (r == 0) trace_at(a, 12, j);
+      unsigned long long rsc[4] = {0ull, 0ull, 0ull, 0ull};
+      const unsigned long long scale2 = f2pack(a.scale_log2, a.scale_log2);
+      const unsigned long long negm2 = f2pack(-msub, -msub);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const unsigned long long x2 =
+              fma2(f2pack(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), scale2, negm2);
+          float x0, x1;
+          f2unpack(x2, x0, x1);
+          float p0, p1;
+          if (emu_pair<EMU>(i)) {
+            p0 = exp2_fma(x0);
+            p1 = exp2_fma(x1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          rsc[i & 3] = add2(rsc[i & 3], f2pack(p0, p1));
+          v[c][i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16_lo(tS + c * 16, v[c]);
+        if (c == 1) {
+          if (rescale && j > 0) {
+            // O is quiescent once PV(j-1) completed; PV(j) waits on this block's p_half
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (j - 1) & 1))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int oc = 0; oc < 4; oc++) {
+              uint32_t o[32];
+              tmem_ld_32x32b_x32(tO + oc * 32, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st_32x32b_x32(tO + oc * 32, o);
+            }
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_half[j & 1]);
+          if (r == 0) trace_at(a, 13, j);
+        }
+      }
+      if (!ok) break;
+      float rs;
+      {
+        float a0, a1, b0, b1;
+        f2unpack(add2(rsc[0], rsc[1]), a0, a1);
+        f2unpack(add2(rsc[2], rsc[3]), b0, b1);
+        rs = (a0 + a1) + (b0 + b1);
+      }
+      if (r == 0) trace_at(a, 6, j);
+      l += rs;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[j & 1]);
+      if (r == 0) trace_at(a, 7, j);
+    }
+    if (ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_final, 0))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tO + c * 32, v);
+        tmem_ld_wait();
+        if (qpos < a.Sq) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[u * 8 + 0]) * inv, __uint_as_float(v[u * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[u * 8 + 2]) * inv, __uint_as_float(v[u * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[u * 8 + 4]) * inv, __uint_as_float(v[u * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[u * 8 + 6]) * inv, __uint_as_float(v[u * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(out + c * 32 + u * 8) = w;
+          }
+        }
+      }
+    } else if (n_kv == 0 && qpos < a.Sq) {
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD;
+      for (int d = 0; d < HD; d++) out[d] = __float2bfloat16(0.f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 bool make_tmap_3d(CUtensorMap* map, const void* base, int H, int S, int B, long long row_stride,
                   long long batch_stride) {
   // dims (inner->outer): head*dim columns, sequence rows, batch; box 64 x 128 x 1, 128-byte swizzle
@@ -735,6 +1062,20 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
   a.n_qblocks = (p.Sq + 2 * TILE - 1) / (2 * TILE);
   a.diag = p.diag_mode;
   a.trace = reinterpret_cast<unsigned long long*>(p.trace);
+  if (p.diag_mode >= 200 && p.diag_mode <= 201) {  // experimental one-tile kernel (see attn1_fwd_kernel)
+    a.n_qblocks = (p.Sq + TILE - 1) / TILE;
+    a.diag = 0;
+    const int smem1 = (int)sizeof(SmemOne) + 1024;
+    const long long grid1 = (long long)a.n_qblocks * p.Hq * p.B;
+    if (grid1 > 0x7fffffff) return cudaErrorInvalidValue;
+    auto go1 = [&](auto kern) -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
+      if (e != cudaSuccess) return e;
+      kern<<<(int)grid1, NTHREADS1, smem1, stream>>>(tq, tk, tv, a);
+      return cudaGetLastError();
+    };
+    return p.diag_mode == 200 ? go1(attn1_fwd_kernel<0>) : go1(attn1_fwd_kernel<1>);
+  }
   const int smem = (int)sizeof(SmemBase) + 1024;
   const long long grid = (long long)a.n_qblocks * p.Hq * p.B;
   if (grid > 0x7fffffff) return cudaErrorInvalidValue;
