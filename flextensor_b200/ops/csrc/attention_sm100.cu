@@ -714,12 +714,13 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
 // never completes a phase the MMA warp has not seen. 192 threads: warps 0-3 softmax/epilogue (rows),
 // warp 4 TMEM owner + MMA issuer, warp 5 TMA producer. K/V traffic from L2 is twice the 2-tile
 // kernel's (each CTA reads the whole K/V of its head for 128 queries).
+constexpr int KV1 = 3;  // K/V ring depth of the one-tile kernel (224 KB of shared memory)
 struct SmemOne {
   uint8_t q[2 * CHUNK];
-  uint8_t k[KV_STAGES][2 * CHUNK];
-  uint8_t v[KV_STAGES][2 * CHUNK];
+  uint8_t k[KV1][2 * CHUNK];
+  uint8_t v[KV1][2 * CHUNK];
   uint64_t q_full;
-  uint64_t k_full[KV_STAGES], k_empty[KV_STAGES], v_full[KV_STAGES], v_empty[KV_STAGES];
+  uint64_t k_full[KV1], k_empty[KV1], v_full[KV1], v_empty[KV1];
   uint64_t s_full[2], p_half[2], p_full[2], o_done;
   uint64_t o_final;  // committed once, after the last PV: o_done can lag two phases at the end
   uint64_t drain;
@@ -744,7 +745,7 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < KV_STAGES; s++) {
+    for (int s = 0; s < KV1; s++) {
       mbar_init(&sm.k_full[s], 1);
       mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.v_full[s], 1);
@@ -781,8 +782,8 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
       bool ok = true;
       uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
       for (int j = 0; j < n_kv && ok; j++) {
-        const int s = j % KV_STAGES;
-        const uint32_t ph = (j / KV_STAGES) & 1;
+        const int s = j % KV1;
+        const uint32_t ph = (j / KV1) & 1;
         if (!wait_tma(&sm.k_empty[s], ph ^ 1)) {
           ok = false;
           break;
@@ -802,7 +803,7 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
       }
       if (!ok) {  // unwinding: every issued load must land before the CTA exits
         spin_drain(&sm.q_full, 0);
-        for (int s = 0; s < KV_STAGES; s++) {
+        for (int s = 0; s < KV1; s++) {
           if (kpend >> s & 1) spin_drain(&sm.k_full[s], (kph >> s) & 1);
           if (vpend >> s & 1) spin_drain(&sm.v_full[s], (vph >> s) & 1);
         }
@@ -815,8 +816,8 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
       constexpr uint32_t idO = umma_idesc_bf16_f32(TILE, HD, false, true);  // V is MN-major
       bool ok = mbar_wait(&sm.q_full, 0);
       const uint64_t dq = umma_desc_kmajor_sw128(smem_u32(sm.q));
-      auto issue_S = [&](int j) {  // S(j) into buffer j % 2 from K stage j % KV_STAGES
-        const int s = j % KV_STAGES;
+      auto issue_S = [&](int j) {  // S(j) into buffer j % 2 from K stage j % KV1
+        const int s = j % KV1;
         const uint64_t dk = umma_desc_kmajor_sw128(smem_u32(sm.k[s]));
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++) {
@@ -827,21 +828,21 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
         umma_commit(&sm.k_empty[s]);
       };
       auto issue_PV_part = [&](int j, int k0, int k1) {
-        const uint64_t dv = umma_desc_mnmajor_sw128(smem_u32(sm.v[j % KV_STAGES]), CHUNK);
+        const uint64_t dv = umma_desc_mnmajor_sw128(smem_u32(sm.v[j % KV1]), CHUNK);
 #pragma unroll
         for (int kk = k0; kk < k1; kk++)
           umma_bf16_ts(tbase + 256, tbase + (j & 1) * 128 + kk * 8, dv + ((kk * 16 * 128) >> 4), idO, (j | kk) != 0);
       };
       for (int j = 0; ok && j < 2 && j < n_kv; j++) {
-        ok = mbar_wait(&sm.k_full[j % KV_STAGES], (j / KV_STAGES) & 1);
+        ok = mbar_wait(&sm.k_full[j % KV1], (j / KV1) & 1);
         if (!ok) break;
         tc_fence_after();
         issue_S(j);
       }
       for (int j = 0; ok && j < n_kv; j++) {
-        const int s = j % KV_STAGES;
+        const int s = j % KV1;
         const uint32_t pph = (j >> 1) & 1;  // phase of this S buffer's P barriers
-        if (!mbar_wait(&sm.v_full[s], (j / KV_STAGES) & 1) || !mbar_wait(&sm.p_half[j & 1], pph)) {
+        if (!mbar_wait(&sm.v_full[s], (j / KV1) & 1) || !mbar_wait(&sm.p_half[j & 1], pph)) {
           ok = false;
           break;
         }
@@ -859,7 +860,7 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
         umma_commit(&sm.v_empty[s]);
         if (j == n_kv - 1) umma_commit(&sm.o_final);
         if (j + 2 < n_kv) {
-          if (!mbar_wait(&sm.k_full[(j + 2) % KV_STAGES], ((j + 2) / KV_STAGES) & 1)) {
+          if (!mbar_wait(&sm.k_full[(j + 2) % KV1], ((j + 2) / KV1) & 1)) {
             ok = false;
             break;
           }
