@@ -1,6 +1,7 @@
 """Numerics of the sm_100a kernels against plain PyTorch fp32 references (GPU only)."""
 
 import math
+import os
 
 import pytest
 import torch
@@ -203,6 +204,26 @@ def test_attention_large_logits():
     v = torch.randn(1, 1024, 2, 128, device=DEV).bfloat16()
     o = ops.attention(q, k, v)
     assert rel_err(o, _attn_ref(q, k, v)) < 2e-2
+
+
+@pytest.mark.skipif(os.environ.get("FT_TEST_EXPERIMENTAL") != "1",
+                    reason="experimental one-tile attention kernel: opt-in (FT_TEST_EXPERIMENTAL=1)")
+@pytest.mark.parametrize("mode", [200, 201])
+@pytest.mark.parametrize("B,Sq,Sk,H,Hk,causal", [(1, 128, 128, 1, 1, False), (2, 300, 300, 4, 4, False),
+                                                 (1, 384, 1000, 8, 2, False), (2, 500, 500, 4, 4, True)])
+def test_attention_one_tile_kernel(mode, B, Sq, Sk, H, Hk, causal):
+    """The experimental one-tile kernel with double-buffered S (``_diag_mode`` 200/201) against the
+    fp32 reference and the default kernel; includes the deferred-rescale path."""
+    torch.manual_seed(9)
+    q = torch.randn(B, Sq, H, 128, device=DEV).bfloat16()
+    k = (torch.randn(B, Sk, Hk, 128, device=DEV) * torch.linspace(0.2, 3, Sk, device=DEV)[None, :, None, None]
+         ).bfloat16()
+    v = torch.randn(B, Sk, Hk, 128, device=DEV).bfloat16()
+    o = ops.attention(q, k, v, causal=causal, _diag_mode=mode)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    assert rel_err(o, _attn_ref(q, k, v, causal=causal)) < 2e-2
+    assert rel_err(o, ops.attention(q, k, v, causal=causal)) < 1e-2
 
 
 @pytest.mark.parametrize("M,N,K", [(512, 256, 64), (1000, 768, 512), (4096, 5120, 5120), (777, 384, 1024)])
