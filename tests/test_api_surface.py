@@ -37,3 +37,20 @@ def test_flextensor_facade():
     from flextensor.config import OffloadConfig
 
     assert OffloadConfig is flextensor_b200.OffloadConfig
+
+
+def test_reference_vllm_class_paths():
+    """The reference's vLLM class / module paths resolve to this package's classes."""
+    pytest = __import__("pytest")
+    pytest.importorskip("vllm")
+    import importlib
+
+    from flextensor_b200.contrib.vllm import loader, snapshot, worker
+
+    assert importlib.import_module("flextensor.contrib.vllm.worker").FlexTensorOffloadWorker is \
+        worker.FlexTensorOffloadWorker
+    snap = importlib.import_module("flextensor.contrib.vllm.snapshot")
+    assert snap.SnapshotWorker is snapshot.SnapshotWorker
+    assert snap.FlexTensorSnapshotWorker is snapshot.FlexTensorSnapshotWorker
+    assert importlib.import_module("flextensor.contrib.vllm.loader").FlexTensorModelLoader is \
+        loader.FlexTensorModelLoader
