@@ -139,15 +139,18 @@ TP_EPI = {"none": 0, "bias": 1, "swiglu": 2, "gelu": 3}
 
 def tp_allgather_gemm(a_full: torch.Tensor, weight: torch.Tensor, *, peer_a: list[int], flags_ptr: int,
                       flag_stride: int, peer_acks: list[int], rank: int, epoch: int, counters: torch.Tensor,
-                      bias: torch.Tensor | None = None, epi: str = "none", out: torch.Tensor | None = None):
+                      bias: torch.Tensor | None = None, epi: str = "none", out: torch.Tensor | None = None,
+                      _pair: bool = False):
     """All-gather -> GEMM: ``a_full [M, K]`` is this rank's full-row buffer with its own rows
     written and published; the kernel pulls peers' rows over NVLink while multiplying.
-    ``epi="swiglu"``: weight rows interleaved (gate, up) -> ``[M, N/2]``."""
+    ``epi="swiglu"``: weight rows interleaved (gate, up) -> ``[M, N/2]``. ``_pair``: the
+    experimental CTA-pair (cta_group::2) kernel, not yet run on a GPU."""
     n_out = weight.shape[0] // 2 if epi == "swiglu" else weight.shape[0]
     if out is None:
         out = torch.empty(a_full.shape[0], n_out, dtype=torch.bfloat16, device=a_full.device)
     native.lib().tp_ag_gemm(a_full, weight, out, bias, TP_EPI[epi], [int(p) for p in peer_a], int(flags_ptr),
-                            int(flag_stride), [int(p) for p in peer_acks], int(rank), int(epoch), counters)
+                            int(flag_stride), [int(p) for p in peer_acks], int(rank), int(epoch), counters,
+                            bool(_pair))
     _count()
     return out
 
@@ -159,11 +162,12 @@ def tp_ag_counter_words(rows_total: int, world: int) -> int:
 
 
 def tp_gemm_reducescatter(a: torch.Tensor, weight: torch.Tensor, *, stage: list[int], peer_flags: list[int],
-                          rank: int, epoch: int, counters: torch.Tensor) -> None:
+                          rank: int, epoch: int, counters: torch.Tensor, _pair: bool = False) -> None:
     """GEMM -> reduce-scatter, sender side: partial ``a @ weight.T`` rows go straight into the
-    owning rank's staging slot ``[world, M/world, N]`` (``stage[p]``); then flags."""
+    owning rank's staging slot ``[world, M/world, N]`` (``stage[p]``); then flags. ``_pair``:
+    the experimental CTA-pair (cta_group::2) kernel, not yet run on a GPU."""
     native.lib().tp_gemm_rs(a, weight, [int(p) for p in stage], [int(p) for p in peer_flags], int(rank), int(epoch),
-                            counters)
+                            counters, bool(_pair))
     _count()
 
 

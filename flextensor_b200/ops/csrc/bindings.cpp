@@ -290,7 +290,7 @@ void p2p_wait_acks_raw(std::vector<uint64_t> flags, std::vector<uint64_t> acks, 
 // w: [N, K] shard; out: [M, N] (or [M, N/2] with SwiGLU). Pointers of peers come as integers.
 void tp_ag_gemm(const Tensor& a_full, const Tensor& w, Tensor& out, const c10::optional<Tensor>& bias, int64_t epi,
                 std::vector<uint64_t> peer_a, uint64_t flags, int64_t flag_stride, std::vector<uint64_t> peer_acks,
-                int64_t rank, uint64_t epoch, Tensor& counters) {
+                int64_t rank, uint64_t epoch, Tensor& counters, bool pair) {
   TORCH_CHECK(a_full.is_cuda() && a_full.scalar_type() == at::kBFloat16 && a_full.dim() == 2 && a_full.is_contiguous(),
               "a_full: contiguous [M, K] bf16");
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.stride(1) == 1, "w: [N, K] bf16");
@@ -324,11 +324,12 @@ void tp_ag_gemm(const Tensor& a_full, const Tensor& w, Tensor& out, const c10::o
   p.epoch = epoch;
   p.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
   p.num_sms = num_sms_for(a_full.get_device());
+  p.pair = pair ? 1 : 0;
   check_ok(ft::tp_allgather_gemm(p, at::cuda::getCurrentCUDAStream()), "tp_allgather_gemm");
 }
 
 void tp_gemm_rs(const Tensor& a, const Tensor& w, std::vector<uint64_t> stage, std::vector<uint64_t> peer_flags,
-                int64_t rank, uint64_t epoch, Tensor& counters) {
+                int64_t rank, uint64_t epoch, Tensor& counters, bool pair) {
   TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.dim() == 2 && a.stride(1) == 1, "a: [M, K] bf16");
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.stride(1) == 1, "w: [N, K] bf16");
   const int world = (int)stage.size();
@@ -352,6 +353,7 @@ void tp_gemm_rs(const Tensor& a, const Tensor& w, std::vector<uint64_t> stage, s
   p.epoch = epoch;
   p.counters = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
   p.num_sms = num_sms_for(a.get_device());
+  p.pair = pair ? 1 : 0;
   check_ok(ft::tp_gemm_reducescatter(p, at::cuda::getCurrentCUDAStream()), "tp_gemm_reducescatter");
 }
 
@@ -649,9 +651,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_gather_raw", &p2p_gather_raw);
   m.def("attention_cp", &attention_cp);
   m.def("p2p_publish_raw", &p2p_publish_raw);
-  m.def("tp_ag_gemm", &tp_ag_gemm);
+  m.def("tp_ag_gemm", &tp_ag_gemm, py::arg("a_full"), py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("epi"),
+        py::arg("peer_a"), py::arg("flags"), py::arg("flag_stride"), py::arg("peer_acks"), py::arg("rank"),
+        py::arg("epoch"), py::arg("counters"), py::arg("pair") = false);
   m.def("tp_ag_counter_words", [](int64_t M, int64_t world) { return ft::tp_ag_counter_words((int)M, (int)world); });
-  m.def("tp_gemm_rs", &tp_gemm_rs);
+  m.def("tp_gemm_rs", &tp_gemm_rs, py::arg("a"), py::arg("w"), py::arg("stage"), py::arg("peer_flags"),
+        py::arg("rank"), py::arg("epoch"), py::arg("counters"), py::arg("pair") = false);
   m.def("tp_reduce", &tp_reduce, py::arg("stage"), py::arg("world"), py::arg("rows"), py::arg("out"),
         py::arg("residual"), py::arg("flags"), py::arg("flag_stride"), py::arg("epoch"), py::arg("peer_acks"),
         py::arg("rank"), py::arg("out_peers") = std::vector<uint64_t>{}, py::arg("row_base") = 0,

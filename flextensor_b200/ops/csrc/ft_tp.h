@@ -37,6 +37,7 @@ struct TpGemmProblem {
   uint64_t epoch = 0;
   unsigned int* counters = nullptr;      // scratch: tp_ag_counter_words (all-gather) / 1 (reduce-scatter), zeroed here
   int num_sms = 0;
+  int pair = 0;  // experimental: 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2)
 };
 
 struct TpReduceProblem {

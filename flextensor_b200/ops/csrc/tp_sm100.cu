@@ -712,6 +712,293 @@ __global__ void tp_ack_kernel(AckList a) {
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Experimental CTA-pair variant (TpGemmProblem::pair; not yet run on a GPU): 256 x 256 tiles over
+// a cluster of 2 CTAs with tcgen05.mma.cta_group::2. Each CTA loads its own 128 rows of A (and,
+// all-gather, waits for exactly those rows to land) and its own 128 rows of W; both loads count on
+// the leader's barrier (no multicast: every CTA fetches its half itself). The leader's MMA thread
+// issues M=256 x N=256 MMAs over both CTAs' shared memory, each CTA's TMEM receives its 128 rows x
+// 256 columns, and each CTA's epilogue stores them (all-gather GEMM: output rows; reduce-scatter:
+// 128-byte row segments into the owners' staging, as in the 1-SM kernel). Per k-block and CTA this
+// reads 32 KB of shared memory for twice the math of the 1-SM 128 x 256 tile.
+struct PairCfg {
+  static constexpr int BN = 256;
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = BM * BK * 2;          // this CTA's 128 A rows
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // this CTA's 128 W rows
+  static constexpr int TMEM_COLS = 2 * BN;              // two accumulators
+  static constexpr int RING = STAGES * (A_BYTES + B_BYTES);
+  static constexpr int SMEM = 1024 + RING + 2 * TP_PIECE + 512;
+};
+constexpr int GROUP_M2 = 4;  // 256-row tiles per weight-tile group
+
+__device__ __forceinline__ void pair_coords(int tile, const TpArgs& p, int& mt2, int& nt) {
+  const int num_m2 = (p.num_m_tiles + 1) / 2;
+  const int per_group = GROUP_M2 * p.num_n_tiles;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int first = g * GROUP_M2;
+  const int gsz = min(GROUP_M2, num_m2 - first);
+  mt2 = (first + r % gsz + p.m_rot) % num_m2;
+  nt = r / gsz;
+}
+
+template <bool AG>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
+    tp_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ TpArgs p) {
+  using C = PairCfg;
+  constexpr int STAGES = C::STAGES;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint8_t* stage = smem + C::RING;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage + 2 * TP_PIECE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* stage_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stage_full + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_tiles = ((p.num_m_tiles + 1) / 2) * p.num_n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs arrive on the leader's copy
+      mbar_init(&stage_full[b], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive / load completion
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 6) {
+    if constexpr (AG) {
+      if (lane == 0) gather_rows(p, stage, stage_full);
+    }
+  } else if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      uint32_t pend = 0, pend_ph = 0;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        int mt2, nt;
+        pair_coords(tile, p, mt2, nt);
+        const int arow = mt2 * 256 + (int)crank * BM;
+        const int brow = nt * BN + (int)crank * (BN / 2);
+        if constexpr (AG) {
+          // this CTA's rows [arow, arow + 128) (none past M): wait for their blocks to land
+          const int r0 = arow, r1 = min(arow + BM, p.M);
+          for (int q = r0 / p.rows; r0 < r1 && q <= (r1 - 1) / p.rows && ok; q++) {
+            if (q == p.rank) continue;
+            const long long qb = (long long)q * p.rows;
+            const int lo = (int)(max((long long)r0, qb) - qb), hi = (int)(min((long long)r1, qb + p.rows) - qb);
+            for (int b = lo / BM; b <= (hi - 1) / BM && ok; b++) {
+              const long long bytes = (long long)(min((b + 1) * BM, p.rows) - b * BM) * p.row_bytes;
+              ok = wait_done(p.done_blk + q * p.nblk + b, (unsigned int)bytes);
+            }
+          }
+          if (!ok) break;
+        }
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&empty[s], ph ^ 1)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES));
+          tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, arow);
+          tma_load_2d_pair(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, brow);
+          pend |= 1u << s;
+          pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok && leader) {  // every issued load lands before the CTA leaves
+        for (int st = 0; st < STAGES; st++) {
+          if (!(pend >> st & 1)) continue;
+          const long long t0 = clock64();
+          while (!mbar_try_wait(smem_u32(&full[st]), (pend_ph >> st) & 1) &&
+                 (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(256, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_kmajor_sw128(smem_u32(sA + s * C::A_BYTES));
+          const uint64_t db = umma_desc_kmajor_sw128(smem_u32(sB + s * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++) umma_bf16_ss_pair(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          umma_commit_pair(&empty[s], 0x3);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+      if (!ok) {
+        umma_commit_pair(drain, 0x1);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(smem_u32(drain), 0) &&
+               (unsigned long long)(clock64() - t0) < FT_WAIT_LIMIT_CYCLES / 4) {
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    const int n_out = p.epi == TP_EPI_SWIGLU ? p.N / 2 : p.N;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+      int mt2, nt;
+      pair_coords(tile, p, mt2, nt);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph))) break;
+      tc_fence_after();
+      const int row0 = mt2 * 256 + (int)crank * BM + q * 32;  // this warp's first row
+      if constexpr (!AG) {
+        uint8_t* ws = stage + q * 4096;
+#pragma unroll 1
+        for (int c2 = 0; c2 < BN / 64; c2++) {
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + (c2 * 2 + hh) * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int v = 0; v < 4; v++) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+              w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+              w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+              w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+              const int seg = hh * 4 + v;
+              *reinterpret_cast<uint4*>(ws + lane * 128 + ((seg ^ (lane & 7)) * 16)) = w;
+            }
+          }
+          __syncwarp();
+          const int col0 = nt * BN + c2 * 64;
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const int rr = k * 4 + (lane >> 3), seg = lane & 7;
+            const int grow = row0 + rr;
+            const int col = col0 + seg * 8;
+            if (grow < p.M && col < p.N) {
+              const uint4 w = *reinterpret_cast<const uint4*>(ws + rr * 128 + ((seg ^ (rr & 7)) * 16));
+              const int owner = grow / p.rows;
+              *reinterpret_cast<uint4*>(p.stage[owner] + ((size_t)p.rank * p.rows + (grow - owner * p.rows)) * p.N +
+                                        col) = w;
+            }
+          }
+          __syncwarp();
+        }
+      } else {
+        const int row = row0 + lane;
+        __nv_bfloat16* rowp = row < p.M ? p.C + (size_t)row * p.ldc : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c++) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nt * BN + c * 32;
+          if (rowp != nullptr && col0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; e++) v[e] = __uint_as_float(r[e]);
+            epi_row32(p, v, col0, rowp + (p.epi == TP_EPI_SWIGLU ? col0 / 2 : col0), n_out);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+    }
+    if constexpr (!AG) __threadfence_system();  // this thread's peer stores before the completion count
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no remote arrive or MMA may target a CTA that has left
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (!AG) {
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const unsigned int old = atomicAdd(p.cta_done, 1u);
+      if (old == gridDim.x - 1) {  // last CTA: every partial row of every CTA is stored
+        __threadfence_system();
+        for (int r = 0; r < p.world; r++) st_release_sys_u64(p.peer_flags[r], p.epoch);
+      }
+    }
+  }
+}
+
+template <bool AG>
+cudaError_t launch_pair(const TpArgs& a, const CUtensorMap& tA, const CUtensorMap& tB, int num_sms, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(tp_gemm_pair_kernel<AG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         PairCfg::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = ((a.num_m_tiles + 1) / 2) * a.num_n_tiles;
+  const int clusters = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  tp_gemm_pair_kernel<AG><<<2 * clusters, NTHREADS, PairCfg::SMEM, s>>>(tA, tB, a);
+  return cudaGetLastError();
+}
+
 template <int BN, bool AG>
 cudaError_t launch(const TpArgs& a, const CUtensorMap& tA, const CUtensorMap& tB, int num_sms, cudaStream_t s) {
   static bool attr = false;
@@ -755,7 +1042,7 @@ static cudaError_t fill_common(const TpGemmProblem& g, TpArgs& a, int bn, bool e
 
 cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream) {
   TpArgs a{};
-  const int bn = g.N >= 256 ? 256 : 128;
+  const int bn = g.pair || g.N >= 256 ? 256 : 128;
   cudaError_t e = fill_common(g, a, bn, true);
   if (e != cudaSuccess) return e;
   if (g.counters == nullptr || g.C == nullptr || g.flags == nullptr) return cudaErrorInvalidValue;
@@ -777,19 +1064,20 @@ cudaError_t tp_allgather_gemm(const TpGemmProblem& g, cudaStream_t stream) {
   a.nblk = (a.rows + BM - 1) / BM;
   if (a.row_bytes * BM > 0xffffffffll) return cudaErrorInvalidValue;  // block byte counts are u32
   a.pieces = (int)((a.row_bytes * a.rows + TP_PIECE - 1) / TP_PIECE);
-  a.m_rot = (g.rank * a.rows) / BM;
+  a.m_rot = g.pair ? (g.rank * a.rows) / 256 : (g.rank * a.rows) / BM;
   e = cudaMemsetAsync(g.counters, 0, sizeof(unsigned int) * (size_t)tp_ag_counter_words(g.M, g.world), stream);
   if (e != cudaSuccess) return e;
   CUtensorMap tA, tB;
   if (!make_tmap_2d_bf16(&tA, local, g.K, g.M, g.K, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap_2d_bf16(&tB, g.W, g.K, g.N, g.ldw, BK, bn)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tB, g.W, g.K, g.N, g.ldw, BK, g.pair ? bn / 2 : bn)) return cudaErrorInvalidValue;
   const int sms = g.num_sms > 0 ? g.num_sms : 148;
+  if (g.pair) return launch_pair<true>(a, tA, tB, sms, stream);
   return bn == 256 ? launch<256, true>(a, tA, tB, sms, stream) : launch<128, true>(a, tA, tB, sms, stream);
 }
 
 cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream) {
   TpArgs a{};
-  const int bn = g.N >= 256 ? 256 : 128;
+  const int bn = g.pair || g.N >= 256 ? 256 : 128;
   cudaError_t e = fill_common(g, a, bn, false);
   if (e != cudaSuccess) return e;
   if (g.counters == nullptr || g.epi != TP_EPI_NONE) return cudaErrorInvalidValue;  // partial sums: no epilogue op
@@ -800,13 +1088,14 @@ cudaError_t tp_gemm_reducescatter(const TpGemmProblem& g, cudaStream_t stream) {
     a.peer_flags[r] = g.peer_flags[r];
   }
   a.cta_done = g.counters;
-  a.m_rot = (((g.rank + 1) % g.world) * a.rows) / BM;
+  a.m_rot = (((g.rank + 1) % g.world) * a.rows) / (g.pair ? 256 : BM);
   e = cudaMemsetAsync(g.counters, 0, sizeof(unsigned int), stream);
   if (e != cudaSuccess) return e;
   CUtensorMap tA, tB;
   if (!make_tmap_2d_bf16(&tA, g.A, g.K, g.M, g.lda, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap_2d_bf16(&tB, g.W, g.K, g.N, g.ldw, BK, bn)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_bf16(&tB, g.W, g.K, g.N, g.ldw, BK, g.pair ? bn / 2 : bn)) return cudaErrorInvalidValue;
   const int sms = g.num_sms > 0 ? g.num_sms : 148;
+  if (g.pair) return launch_pair<false>(a, tA, tB, sms, stream);
   return bn == 256 ? launch<256, false>(a, tA, tB, sms, stream) : launch<128, false>(a, tA, tB, sms, stream);
 }
 

@@ -3,6 +3,8 @@ allocations; flags are set before the launches that read them, so no kernel wait
 launch): all-gather -> GEMM (bias / SwiGLU) and GEMM -> reduce-scatter -> reduce, against fp32
 references."""
 
+import os
+
 import pytest
 import torch
 
@@ -199,3 +201,50 @@ def test_reduce_bias_gate_residual():
     for p in range(W):
         ref = res[p].float() + full[p * R:(p + 1) * R]
         assert _rel(outs[p], ref) < 2e-2, p
+
+
+@pytest.mark.skipif(os.environ.get("FT_TEST_EXPERIMENTAL") != "1",
+                    reason="experimental CTA-pair TP kernels: opt-in (FT_TEST_EXPERIMENTAL=1)")
+@pytest.mark.parametrize("W,R,K,N,epi", [(2, 256, 512, 1024, "none"), (4, 200, 256, 640, "swiglu"),
+                                         (8, 96, 128, 384, "bias")])
+def test_pair_kernels_emulated(W, R, K, N, epi):
+    """The experimental cta_group::2 variants of the all-gather GEMM and the GEMM + reduce-scatter
+    (``_pair=True``) on emulated ranks against fp32 references."""
+    M = W * R
+    g = torch.Generator(device=DEV).manual_seed(W + N)
+    a = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    bias = torch.randn(N, device=DEV, generator=g).bfloat16() if epi == "bias" else None
+    bufs = []
+    for p in range(W):
+        b = torch.zeros(M, K, device=DEV, dtype=torch.bfloat16)
+        b[p * R:(p + 1) * R] = a[p * R:(p + 1) * R]
+        bufs.append(b)
+    flags = torch.ones(W, dtype=torch.int64, device=DEV)
+    acks = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    counters = torch.zeros(ops.tp_ag_counter_words(M, W), dtype=torch.int32, device=DEV)
+    out = ops.tp_allgather_gemm(bufs[0], w, peer_a=[b.data_ptr() for b in bufs], flags_ptr=flags.data_ptr(),
+                                flag_stride=1, peer_acks=[x.data_ptr() for x in acks], rank=0, epoch=1,
+                                counters=counters, bias=bias, epi=epi, _pair=True)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    ref = a.float() @ w.float().t() + (bias.float() if bias is not None else 0)
+    if epi == "swiglu":
+        ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+    assert _rel(out, ref) < 2e-2
+    # GEMM -> reduce-scatter, every emulated rank with the pair kernel
+    parts = [torch.randn(M, K, device=DEV, generator=g).bfloat16() for _ in range(W)]
+    stage = [torch.zeros(W, R, N, device=DEV, dtype=torch.bfloat16) for _ in range(W)]
+    rflags = [torch.zeros(W, dtype=torch.int64, device=DEV) for _ in range(W)]
+    cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for r in range(W):
+        ops.tp_gemm_reducescatter(parts[r], w, stage=[s_.data_ptr() for s_ in stage],
+                                  peer_flags=[f.data_ptr() + 8 * r for f in rflags], rank=r, epoch=1, counters=cnt,
+                                  _pair=True)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    full = sum(parts[r].float() @ w.float().t() for r in range(W))
+    for p in range(W):
+        got = stage[p].float().sum(0)
+        assert _rel(got, full[p * R:(p + 1) * R]) < 2e-2
+        assert all(int(x) == 1 for x in rflags[p])
