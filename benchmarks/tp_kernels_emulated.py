@@ -2,7 +2,9 @@
 the kernels' own structure without NVLink. Times rank 0's all-gather GEMM / GEMM + reduce-scatter
 launch against the plain GEMM of the same shape (Llama-3-70B layer shapes, 16,384 tokens).
 
-    python benchmarks/tp_kernels_emulated.py
+    python benchmarks/tp_kernels_emulated.py [--pair]
+
+``--pair``: the experimental CTA-pair (cta_group::2) kernels.
 """
 import os
 import sys
@@ -11,6 +13,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 import torch
 from flextensor_b200 import ops
 dev = "cuda"
+PAIR = "--pair" in sys.argv[1:]
 def tm(f, n=10):
     for _ in range(3): f()
     s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -32,7 +35,8 @@ for W in (2, 8):
         def rs():
             ep[0] += 1
             ops.tp_gemm_reducescatter(a, w, stage=[s.data_ptr() for s in stage],
-                                      peer_flags=[f.data_ptr() for f in flags], rank=0, epoch=ep[0], counters=counters)
+                                      peer_flags=[f.data_ptr() for f in flags], rank=0, epoch=ep[0], counters=counters,
+                                      _pair=PAIR)
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         t_rs = tm(rs)
         t_lin = tm(lambda: ops.linear(a, w, None, epi="none", out=out))
@@ -52,7 +56,7 @@ for W in (2, 8):
             flags.fill_(ep[0])
             ops.tp_allgather_gemm(bufs[0], w, peer_a=[b.data_ptr() for b in bufs], flags_ptr=flags.data_ptr(),
                                   flag_stride=1, peer_acks=[x.data_ptr() for x in acks], rank=0, epoch=ep[0],
-                                  counters=counters, epi=epi)
+                                  counters=counters, epi=epi, _pair=PAIR)
         t_ag = tm(ag)
         if epi == "swiglu":
             t_lin = tm(lambda: ops.linear_swiglu(a_full, w))

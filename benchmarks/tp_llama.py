@@ -32,6 +32,7 @@ def main():
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--collectives", default="fused,nccl",
                     help="comma list of fused, nccl, fused_ag (fused all-gather only), fused_rs")
+    ap.add_argument("--pair", action="store_true", help="experimental CTA-pair (cta_group::2) fused kernels")
     a = ap.parse_args()
     import torch.distributed as dist
 
@@ -55,7 +56,7 @@ def main():
     peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("bf16_tflops", 1590.0)
     res = {}
     for coll in a.collectives.split(","):
-        tp.setup(M, collective=coll)
+        tp.setup(M, collective=coll, pair=a.pair)
         x = x0.clone()
 
         def step():

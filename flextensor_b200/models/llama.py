@@ -306,10 +306,11 @@ class LlamaTP(nn.Module):
             mine.ffn_norm.copy_(src.ffn_norm)
         return self
 
-    def setup(self, tokens_total: int, group=None, collective: str = "fused") -> None:
+    def setup(self, tokens_total: int, group=None, collective: str = "fused", pair: bool = False) -> None:
         """``collective``: ``fused`` (all-gather inside the column-parallel GEMMs, reduce-scatter
         from the row-parallel GEMM epilogues), ``nccl`` (NCCL around plain GEMMs), or one fused
-        side only: ``fused_ag`` / ``fused_rs``."""
+        side only: ``fused_ag`` / ``fused_rs``. ``pair``: the experimental CTA-pair (cta_group::2)
+        kernels for the fused sides."""
         from flextensor_b200.parallel.tp import NcclTP, TPAllGather, TPReduceScatter
 
         if collective not in ("fused", "nccl", "fused_ag", "fused_rs"):
@@ -317,9 +318,9 @@ class LlamaTP(nn.Module):
         self.collective = collective
         self._nccl = NcclTP(group)
         if collective in ("fused", "fused_ag"):
-            self._ag = TPAllGather(tokens_total, self.cfg.dim, group)
+            self._ag = TPAllGather(tokens_total, self.cfg.dim, group, pair=pair)
         if collective in ("fused", "fused_rs"):
-            self._rs = TPReduceScatter(tokens_total, self.cfg.dim, group)
+            self._rs = TPReduceScatter(tokens_total, self.cfg.dim, group, pair=pair)
 
     def close(self) -> None:
         for o in (self._ag, self._rs):

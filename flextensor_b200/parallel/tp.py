@@ -36,10 +36,11 @@ class _Flags:
 class TPAllGather:
     """Full ``[M, K]`` activation buffers; this rank writes rows ``[rank*R, (rank+1)*R)``."""
 
-    def __init__(self, rows_total: int, k: int, group=None, device: int | None = None):
+    def __init__(self, rows_total: int, k: int, group=None, device: int | None = None, pair: bool = False):
         import torch.distributed as dist
 
         self.group = group
+        self.pair = pair  # experimental CTA-pair (cta_group::2) kernel
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         if rows_total % self.world:
             raise ValueError(f"{rows_total} rows do not split over {self.world} ranks")
@@ -91,7 +92,8 @@ class TPAllGather:
             self._buf(slot), weight, peer_a=[p + self.off[slot] for p in self.heap.ptrs],
             flags_ptr=self.f.flags[self.rank] + slot * 8, flag_stride=N_SLOTS,
             peer_acks=[self.f.acks[p] + (self.rank * N_SLOTS + slot) * 8 for p in range(self.world)],
-            rank=self.rank, epoch=e, counters=self.counters, bias=bias, epi=epi, out=out)
+            rank=self.rank, epoch=e, counters=self.counters, bias=bias, epi=epi, out=out,
+            _pair=getattr(self, "pair", False))
 
     def close(self) -> None:
         _close(self)
@@ -100,10 +102,11 @@ class TPAllGather:
 class TPReduceScatter:
     """Staging ``[world, R, N]`` per slot on every rank; rank r owns output rows ``[r*R, (r+1)*R)``."""
 
-    def __init__(self, rows_total: int, n: int, group=None, device: int | None = None):
+    def __init__(self, rows_total: int, n: int, group=None, device: int | None = None, pair: bool = False):
         import torch.distributed as dist
 
         self.group = group
+        self.pair = pair  # experimental CTA-pair (cta_group::2) kernel
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         if rows_total % self.world:
             raise ValueError(f"{rows_total} rows do not split over {self.world} ranks")
@@ -137,7 +140,7 @@ class TPReduceScatter:
         self._cur = (slot, e)
         tp_gemm_reducescatter(a, weight, stage=[p + self.off[slot] for p in self.heap.ptrs],
                               peer_flags=[self.f.flags[p] + (self.rank * N_SLOTS + slot) * 8 for p in range(self.world)],
-                              rank=self.rank, epoch=e, counters=self.counters)
+                              rank=self.rank, epoch=e, counters=self.counters, _pair=getattr(self, "pair", False))
 
     def reduce(self, out: torch.Tensor, residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
                gate: torch.Tensor | None = None, gate_rows: int = 0) -> torch.Tensor:

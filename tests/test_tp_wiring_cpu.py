@@ -39,7 +39,7 @@ def test_reduce_scatter_flags_and_acks_meet(monkeypatch, slot):
     import flextensor_b200.ops.api as api
 
     monkeypatch.setattr(api, "tp_gemm_reducescatter",
-                        lambda a, w, *, stage, peer_flags, rank, epoch, counters: sent.setdefault(rank, peer_flags))
+                        lambda a, w, *, stage, peer_flags, rank, epoch, counters, **kw: sent.setdefault(rank, peer_flags))
     monkeypatch.setattr(api, "tp_reduce", lambda stage, world, rows, out, *, flags_ptr, flag_stride, peer_acks, rank,
                         **kw: polled.setdefault(rank, (flags_ptr, flag_stride, peer_acks)))
     for r in range(W):
