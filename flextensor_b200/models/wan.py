@@ -280,6 +280,26 @@ class WanDiT(nn.Module):
             self._rope_cache[key] = t
         return t
 
+    def condition(self, timestep: torch.Tensor, context: torch.Tensor):
+        """Time embedding ``temb`` [B, dim], the six adaLN vectors ``e`` [B, 6, dim] (fp32) and
+        the projected text context ``ctx`` [B, L, dim]."""
+        cfg = self.cfg
+        dt = self.patch_embedding.weight.dtype
+        t = sinusoidal(timestep, cfg.freq_dim).to(dt)
+        temb = self._lin(F.silu(self._lin(t, self.time_embedding_1).float()).to(dt), self.time_embedding_2)
+        e = self._lin(F.silu(temb.float()).to(dt), self.time_projection).float().view(-1, 6, cfg.dim)
+        ctx = self._lin(context.to(dt), self.text_embedding_1, "gelu")
+        ctx = self._lin(ctx, self.text_embedding_2).contiguous()
+        return temb, e, ctx
+
+    def head(self, x: torch.Tensor, temb: torch.Tensor) -> torch.Tensor:
+        """Modulated final LayerNorm and the output projection (patch tokens, not yet unpatchified)."""
+        cfg = self.cfg
+        mod = self.head_scale_shift.float() + temb.float()[:, None]
+        shift, scale = mod[:, 0:1], mod[:, 1:2]
+        h = (F.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps) * (1 + scale) + shift).to(self.patch_embedding.weight.dtype)
+        return self._lin(h, self.proj_out)
+
     def forward(self, latent: torch.Tensor, timestep: torch.Tensor, context: torch.Tensor, cp=None) -> torch.Tensor:
         """``cp``: a :class:`~flextensor_b200.parallel.cp.ContextParallel` (fused path) or
         :class:`~flextensor_b200.parallel.cp.UlyssesAttention` (torch path); each rank then runs
@@ -298,20 +318,13 @@ class WanDiT(nn.Module):
             rank_rows = slice(dist.get_rank(cp.group) * shard, (dist.get_rank(cp.group) + 1) * shard)
             x = x[:, rank_rows].contiguous()
         x = self._lin(x, self.patch_embedding, "bias").contiguous()
-        t = sinusoidal(timestep, cfg.freq_dim).to(dt)
-        temb = self._lin(F.silu(self._lin(t, self.time_embedding_1).float()).to(dt), self.time_embedding_2)
-        e = self._lin(F.silu(temb.float()).to(dt), self.time_projection).float().view(-1, 6, cfg.dim)
-        ctx = self._lin(context.to(dt), self.text_embedding_1, "gelu")
-        ctx = self._lin(ctx, self.text_embedding_2).contiguous()
+        temb, e, ctx = self.condition(timestep, context)
         cos, sin = self.rope(grid, x.device)
         if rank_rows is not None:
             cos, sin = cos[rank_rows].contiguous(), sin[rank_rows].contiguous()
         for blk in self.blocks:
             x = blk(x, ctx, e, cos, sin, cp=cp) if cp is not None else blk(x, ctx, e, cos, sin)
-        mod = self.head_scale_shift.float() + temb.float()[:, None]
-        shift, scale = mod[:, 0:1], mod[:, 1:2]
-        h = (F.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps) * (1 + scale) + shift).to(dt)
-        y = self._lin(h, self.proj_out)
+        y = self.head(x, temb)
         if cp is not None:
             y = _gather_seq(y, cp.group)
         return self.unpatchify(y, grid)
