@@ -9,8 +9,10 @@ token activations ``[B, tokens, dim]`` are the only tensors that cross ranks.
 The stages are balanced by the blocks' parameter bytes unless measured costs are given.
 
 The reference has no pipeline parallelism (its shared-memory path requires PP = 1,
-``src/flextensor/contrib/vllm/v2/worker.py:112-113``). Each stage's blocks can be offloaded
-with their own manager name, like the reference's per-denoiser managers.
+``src/flextensor/contrib/vllm/v2/worker.py:112-113``). Each stage's blocks form one module,
+:class:`WanStageBlocks`, which :meth:`WanPipelineParallel.offload` hands to an offload manager
+of its own (``wan_pp<stage>``), like the reference's per-denoiser managers; every micro-batch
+is then one iteration of that manager.
 """
 
 from __future__ import annotations
@@ -30,6 +32,19 @@ def block_costs(model: WanDiT) -> list[float]:
     return [float(sum(p.numel() * p.element_size() for p in b.parameters())) for b in model.blocks]
 
 
+class WanStageBlocks(nn.Module):
+    """One stage's contiguous run of Wan blocks: the module an offload manager wraps."""
+
+    def __init__(self, blocks: nn.ModuleList):
+        super().__init__()
+        self.blocks = blocks
+
+    def forward(self, x, ctx, e, cos, sin):
+        for blk in self.blocks:
+            x = blk(x, ctx, e, cos, sin)
+        return x
+
+
 class WanPipelineParallel:
     """Keeps only this rank's stage of ``model.blocks`` (in place) and runs micro-batches
     through the pipeline. A collective constructor: every rank of ``group`` builds one."""
@@ -43,6 +58,7 @@ class WanPipelineParallel:
         b0, b1 = self.bounds[self.stage]
         model.blocks = nn.ModuleList(list(model.blocks)[b0:b1])
         self.model = model
+        self.stage_blocks: nn.Module = WanStageBlocks(model.blocks)
         self.depth = depth
         self.comm = TorchP2P(self.groups) if self.n_stages > 1 else None
 
@@ -68,8 +84,7 @@ class WanPipelineParallel:
                 x, _ = m.patchify(x.to(device=device, dtype=dt))
                 x = m._lin(x, m.patch_embedding, "bias").contiguous()
             cos, sin = m.rope(grids[i], device)
-            for blk in m.blocks:
-                x = blk(x, ctx, e, cos, sin)
+            x = self.stage_blocks(x, ctx, e, cos, sin)
             return m.head(x, temb) if last else x
 
         stage = PipelineStage(fn, self.stage, self.n_stages, self.comm, self.depth, device)
@@ -81,3 +96,11 @@ class WanPipelineParallel:
         return [m.unpatchify(y, g) for y, g in zip(outs, grids)]
 
     __call__ = forward
+
+    def offload(self, config, name: str | None = None) -> nn.Module:
+        """Stream this stage's block weights under their own offload manager (default name
+        ``wan_pp<stage>``); returns the manager's model proxy, which the pipeline then runs."""
+        import flextensor_b200 as ft
+
+        self.stage_blocks = ft.offload(self.stage_blocks, config, name=name or f"wan_pp{self.stage}")
+        return self.stage_blocks

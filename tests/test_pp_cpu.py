@@ -1,7 +1,8 @@
 """Pipeline parallelism on the CPU: the stage split, the micro-batch schedule (receives posted
 ahead of compute, sends overlapping the next micro-batch, outputs returned to the first stage)
 over an in-memory transport with one thread per stage, and the Wan DiT split over 2 and 3 gloo
-ranks against the unsplit model."""
+ranks against the unsplit model, resident and with each stage's blocks streamed by its own
+offload manager."""
 
 import itertools
 import os
@@ -170,7 +171,7 @@ def _inputs(cfg, n_micro):
     return lat, ts, ctx
 
 
-def _wan_pp_worker(rank, world, port, q):
+def _wan_pp_worker(rank, world, port, q, offload=False):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -186,14 +187,33 @@ def _wan_pp_worker(rank, world, port, q):
         lat, ts, ctx = _inputs(cfg, 4)
         if rank not in (0, world - 1):
             lat = [torch.empty(x.shape, device="meta") for x in lat]
-        outs = pp(lat, ts, ctx)
-        q.put((rank, pp.bounds, len(m.blocks), None if outs is None else [o.numpy() for o in outs]))
+        runs = 1
+        if offload:
+            import flextensor_b200 as ft
+            from flextensor_b200.planner import NthLayerStrategy
+
+            pp.offload(ft.OffloadConfig(pinned_memory=False, include_patterns=["blocks.*"], profiling_iters=1,
+                                        num_blocks=2, min_blocks=2,
+                                        load_strategy=NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2, cyclic=True)))
+            runs = 3  # 4 micro-batches a run: discovery, profiling and inference all pass
+        for _ in range(runs):
+            outs = pp(lat, ts, ctx)
+            if outs is not None:
+                outs = [o.numpy().copy() for o in outs]
+        extra = None
+        if offload:
+            om = ft.get_offload_manager(f"wan_pp{rank}")
+            extra = (om.phase.value, len(om.get_tensor_manager().loader.plan.host_blocks))
+            ft.release(f"wan_pp{rank}")
+        q.put((rank, pp.bounds, len(m.blocks), outs, extra))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_wan_pipeline_matches_unsplit_model(world):
+@pytest.mark.parametrize("world,offload", [(2, False), (3, False), (2, True)])
+def test_wan_pipeline_matches_unsplit_model(world, offload):
+    """With ``offload``, each stage streams its blocks under its own manager (``wan_pp<r>``)
+    through discovery, profiling and inference; the outputs stay bit-identical."""
     import torch.multiprocessing as mp
 
     from flextensor_b200.models.wan import WanDiT, init_wan_params_, tiny_config
@@ -207,7 +227,7 @@ def test_wan_pipeline_matches_unsplit_model(world):
     ctx_mp = mp.get_context("spawn")
     q = ctx_mp.Queue()
     port = _free_port()
-    ps = [ctx_mp.Process(target=_wan_pp_worker, args=(r, world, port, q)) for r in range(world)]
+    ps = [ctx_mp.Process(target=_wan_pp_worker, args=(r, world, port, q, offload)) for r in range(world)]
     for p in ps:
         p.start()
     res = sorted((q.get(timeout=180) for _ in ps), key=lambda t: t[0])
@@ -215,7 +235,9 @@ def test_wan_pipeline_matches_unsplit_model(world):
         p.join(30)
     bounds = res[0][1]
     assert [b - a for a, b in bounds] == [r[2] for r in res] and sum(r[2] for r in res) == 5
-    for rank, _, _, outs in res:
+    for rank, _, _, outs, extra in res:
+        if offload:
+            assert extra[0] == "inference" and extra[1] > 0, (rank, extra)
         if rank in (0, world - 1):
             assert len(outs) == 4
             for w, o in zip(want, outs):
