@@ -18,7 +18,9 @@ communicators keep the transfers from queueing behind one another:
   different internal streams): a send that waits for its receiver never holds up the receive
   of the next micro-batch;
 * outputs that go back from the last stage to the first use a third group, so that a first
-  stage still sending inputs is never blocked by a pending return.
+  stage still sending inputs is never blocked by a pending return. The first stage posts all
+  its return receives up front, and the last stage sends each output back as soon as it is
+  computed.
 
 With NCCL, ``isend`` / ``irecv`` enqueue on NCCL's own streams and ``wait()`` only orders the
 current CUDA stream after the transfer, so the host runs ahead and the GPU overlaps the
@@ -176,6 +178,12 @@ class PipelineStage:
             buf = self._buffer(recv_spec(m))
             pending.append((buf, self.comm.recv(buf, s - 1, s, "fwd")))
 
+        returning = out_spec is not None and self.n_stages > 1
+        back: list[tuple[torch.Tensor, Handle]] = []
+        if returning and self.is_first:  # the return path has its own communicator: post it all now
+            for m in range(n_micro):
+                buf = self._buffer(out_spec(m))
+                back.append((buf, self.comm.recv(buf, self.n_stages - 1, 0, "back")))
         if not self.is_first:
             for m in range(min(self.depth, n_micro)):
                 post(m)
@@ -191,23 +199,17 @@ class PipelineStage:
             y = self.fn(x, m)
             if self.is_last:
                 outs.append(y)
+                if returning:  # each output heads back while the next micro-batch computes
+                    y = y.contiguous()
+                    sends.append((self.comm.send(y, s, 0, "back"), y))
             else:
                 y = y.contiguous()
                 sends.append((self.comm.send(y, s, s + 1, "fwd"), y))
         result: list[torch.Tensor] | None = outs if self.is_last else None
-        if out_spec is not None and self.n_stages > 1:
-            if self.is_last:
-                for y in outs:
-                    y = y.contiguous()
-                    sends.append((self.comm.send(y, s, 0, "back"), y))
-            elif self.is_first:
-                back = []
-                for m in range(n_micro):
-                    buf = self._buffer(out_spec(m))
-                    back.append((buf, self.comm.recv(buf, self.n_stages - 1, 0, "back")))
-                for buf, h in back:
-                    h.wait()
-                result = [buf for buf, _ in back]
+        if back:
+            for _, h in back:
+                h.wait()
+            result = [buf for buf, _ in back]
         for h, _ in sends:
             h.wait()
         return result

@@ -136,6 +136,15 @@ def test_schedule_results_and_overlap(n_stages, n_micro, depth, back):
         for m in range(n_micro - depth):
             assert posts[m + depth] < computes[m]
         assert posts[min(depth, n_micro) - 1] < computes[0]  # the first `depth` before any compute
+    if back and n_stages > 1:  # outputs head back to stage 0 as they are computed
+        sends = [i for i, e in enumerate(log) if e == ("send", last, 0, "back")]
+        computes = [i for i, e in enumerate(log) if e[0] == "compute" and e[1] == last]
+        posts = [i for i, e in enumerate(log) if e == ("post_recv", last, 0, "back")]
+        assert len(sends) == len(posts) == n_micro
+        first_compute = min(i for i, e in enumerate(log) if e == ("compute", 0, 0))
+        assert max(posts) < first_compute
+        for m in range(n_micro - 1):
+            assert computes[m] < sends[m] < computes[m + 1]
     for s in range(n_stages - 1):  # each output leaves before the next micro-batch is computed
         sends = [i for i, e in enumerate(log) if e == ("send", s, s + 1, "fwd")]
         computes = [i for i, e in enumerate(log) if e[0] == "compute" and e[1] == s]
