@@ -54,3 +54,15 @@ def test_reference_vllm_class_paths():
     assert snap.FlexTensorSnapshotWorker is snapshot.FlexTensorSnapshotWorker
     assert importlib.import_module("flextensor.contrib.vllm.loader").FlexTensorModelLoader is \
         loader.FlexTensorModelLoader
+
+
+def test_parallel_exports_resolve():
+    """Every name in ``flextensor_b200.parallel.__all__`` resolves, and each parallelism strategy
+    (context, tensor, expert, pipeline, striped streaming) has its entry point there."""
+    import flextensor_b200.parallel as par
+
+    missing = [n for n in par.__all__ if not hasattr(par, n)]
+    assert not missing, missing
+    for name in ("ContextParallel", "UlyssesAttention", "TPAllGather", "TPReduceScatter", "TPAllReduce",
+                 "ExpertParallel", "PipelineStage", "split_stages", "pipeline_groups", "StripedTransferEngine"):
+        assert name in par.__all__, name
