@@ -13,6 +13,10 @@ from __future__ import annotations
 import math
 from bisect import bisect_left
 
+# Results are bounded at 2**62 (bytes or ms): a nearly flat end segment (noisy timings of small
+# copies) extrapolates with a huge log-log slope, and exp() of it would overflow.
+_MAX_LOG = 62 * math.log(2.0)
+
 
 class MemoryTransferInterpolator:
     def __init__(self, memory_transfers: dict[int, float]):
@@ -49,7 +53,7 @@ class MemoryTransferInterpolator:
     def bytes_to_duration(self, size_bytes: int | float) -> float:
         if size_bytes <= 0:
             raise ValueError(f"size_bytes must be positive, got {size_bytes}")
-        return math.exp(self._eval(self._lx, self._ly, math.log(float(size_bytes))))
+        return math.exp(min(self._eval(self._lx, self._ly, math.log(float(size_bytes))), _MAX_LOG))
 
     def duration_to_bytes(self, duration_ms: float) -> float:
         if duration_ms <= 0:
@@ -58,7 +62,7 @@ class MemoryTransferInterpolator:
         pairs = sorted(zip(self._ly, self._lx))
         ly = [p[0] for p in pairs]
         lx = [p[1] for p in pairs]
-        return math.exp(self._eval(ly, lx, math.log(float(duration_ms))))
+        return math.exp(min(self._eval(ly, lx, math.log(float(duration_ms))), _MAX_LOG))
 
     def get_bandwidth_mbps(self) -> float:
         return (self.bytes_array[-1] / (1024 * 1024)) / (self.duration_array[-1] / 1000.0)

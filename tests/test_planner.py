@@ -138,3 +138,14 @@ def test_tensor_selection_runs():
     layers = make_layers(n=5)
     r = GlobalTensorSelectionStrategy(n_blocks=2, pop_size=8, epoch=5, seed=0).compute(layers, MEM, None)
     _check(r, layers)
+
+
+def test_interpolator_flat_noisy_curve_does_not_overflow():
+    """Noisy timings of small copies can make an end segment nearly flat; extrapolating a long
+    duration through it must give a bounded byte count, not an OverflowError."""
+    from flextensor_b200.planner.interpolator import MemoryTransferInterpolator
+
+    interp = MemoryTransferInterpolator({1 << 20: 0.500000, 1 << 21: 0.500001})
+    big = interp.duration_to_bytes(1000.0)
+    assert 0 < big <= 2.0 ** 62 * (1 + 1e-9)
+    assert interp.bytes_to_duration(1 << 40) <= 2.0 ** 62 * (1 + 1e-9)

@@ -10,8 +10,9 @@ import pytest
 from flextensor_b200.shm.sync import MultiprocessCondition, SemaphoreLock, SharedMultiString
 
 
-def _holder(name, slots, log, hold):
+def _holder(name, slots, log, hold, start):
     s = SemaphoreLock(name, slots)
+    start.wait(timeout=60)  # all holders compete at once, however slowly the processes spawned
     s.acquire(timeout=30)
     with open(log, "a") as f:
         f.write(f"in {time.time()}\n")
@@ -49,7 +50,8 @@ def test_semaphore_bounds_concurrency(tmp_path):
     name = f"ftsem{uuid.uuid4().hex[:8]}"
     log = str(tmp_path / "log")
     ctx = _mp()
-    ps = [ctx.Process(target=_holder, args=(name, 2, log, 0.4)) for _ in range(4)]
+    start = ctx.Barrier(4)
+    ps = [ctx.Process(target=_holder, args=(name, 2, log, 1.0, start)) for _ in range(4)]
     for p in ps:
         p.start()
     for p in ps:
