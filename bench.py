@@ -26,6 +26,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -43,7 +44,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=40, help="(testing only) fewer blocks; invalid for the headline")
-    ap.add_argument("--profiling-iters", type=int, default=2)
+    ap.add_argument("--profiling-iters", type=int, default=3)
+    ap.add_argument("--placement", choices=["auto", "pinned_arena", "device", "pageable"], default="auto",
+                    help="where the weights start before offload() (auto: pinned arena at N=1, device at N>1)")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -57,7 +60,9 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.out = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        # raw samples go to FT_BENCH_CLOCKS_DIR (default: the system temp directory)
+        out_dir = os.environ.get("FT_BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        self.out = os.path.join(out_dir, f"ft_bench_clocks_rank{index}_{os.getpid()}.csv")
 
     def start(self):
         os.makedirs(os.path.dirname(self.out), exist_ok=True)
@@ -141,23 +146,36 @@ def barrier(pg):
 def build_model(impl: str, layers: int, device, seed: int, placement: str = "pinned_arena"):
     """Random-init Wan-14B-shape DiT (initialised on the GPU, then placed).
 
+    Our arm builds ``flextensor_b200.models.wan.WanDiT`` (tcgen05 kernels); the reference arm
+    builds ``baseline/wan_torch.py`` (stock PyTorch ops, nothing imported from this
+    repository's package). Both have the same parameter tree.
+
     ``placement``:
       * ``pinned_arena`` -- one pinned host arena, each parameter a view (a loaded checkpoint);
-      * ``device``       -- weights stay on the GPU (our multi-GPU runs: the runtime packs each
-        rank's stripe straight from the GPU, so no rank ever holds a whole host copy);
-      * ``pageable``     -- one pageable host tensor per parameter (the reference's multi-GPU
-        runs: it pins and packs them and frees each source as it goes, which keeps N host
-        copies within the host's RAM where a pinned arena per rank would not)."""
+      * ``device``       -- weights stay on the GPU; the runtime copies what it offloads into
+        its own pinned host blocks (our arm packs only this rank's stripe), so a rank holds no
+        second host copy;
+      * ``pageable``     -- one pageable host tensor per parameter."""
     import torch
 
-    sys.path.insert(0, ROOT)
-    from flextensor_b200.models.wan import WAN_14B, WanConfig, WanDiT, init_wan_params_
+    if impl == "ours":
+        sys.path.insert(0, ROOT)
+        from flextensor_b200.models.wan import WAN_14B, WanConfig, WanDiT, init_wan_params_
 
-    cfg = WanConfig(**{**WAN_14B.__dict__, "num_layers": layers})
-    with torch.device("meta"):
-        model = WanDiT(cfg, impl="fused" if impl == "ours" else "torch")
+        cfg = WanConfig(**{**WAN_14B.__dict__, "num_layers": layers})
+        with torch.device("meta"):
+            model = WanDiT(cfg, impl="fused")
+        init = init_wan_params_
+    else:
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        from wan_torch import WanShape, WanTorchDiT, init_params_  # noqa: PLC0415
+
+        cfg = WanShape(num_layers=layers)
+        with torch.device("meta"):
+            model = WanTorchDiT(cfg)
+        init = init_params_
     model = model.to_empty(device=device).to(torch.bfloat16)
-    init_wan_params_(model, seed=seed)
+    init(model, seed=seed)
     if placement in ("device", "pageable"):
         with torch.no_grad():
             if placement == "pageable":
@@ -189,31 +207,6 @@ def build_model(impl: str, layers: int, device, seed: int, placement: str = "pin
     model.eval()
     model.requires_grad_(False)
     return model, cfg
-
-
-def host_ram_check(impl: str, layers: int, world: int):
-    """None when the N-rank run fits the host's RAM, else the reason it cannot run.
-
-    Our arm holds 1/N of the streamed bytes per rank in pinned memory (stripe-only host
-    store). The reference arm has no striping: every process keeps a whole pinned copy of
-    its offloaded weights (~75% of 28.6 GB) plus packing transients."""
-    import psutil
-
-    from flextensor_b200.models.wan import WAN_14B, WanConfig
-
-    cfg = WanConfig(**{**WAN_14B.__dict__, "num_layers": layers})
-    d, f = cfg.dim, cfg.ffn_dim
-    per_block = 2 * (4 * d * d + 4 * d * d + 2 * d * f)  # bf16: self-attn + cross-attn + FFN
-    streamed = per_block * cfg.num_layers * (1.0 - RESIDENT_FRACTION)
-    total = per_block * cfg.num_layers
-    per_rank = streamed / world if impl == "ours" else total * 1.1
-    need = per_rank * world + world * 4e9  # + ~4 GB host per CUDA/torch process
-    avail = psutil.virtual_memory().available
-    if need > 0.85 * avail:
-        return (f"host RAM: {world} ranks x {per_rank / 1e9:.1f} GB host weights + process overhead = "
-                f"{need / 1e9:.0f} GB > 85% of {avail / 1e9:.0f} GB available "
-                f"({'stripe-only' if impl == 'ours' else 'one full host copy per process, no striping'})")
-    return None
 
 
 def weight_budget_fraction(model, device) -> float:
@@ -282,32 +275,22 @@ def _engine(om):
         return None
 
 
-def main():
-    args = parse()
+def _rss_bytes() -> int:
+    import psutil
+
+    return psutil.Process().memory_info().rss
+
+
+def _peak_rss_bytes() -> int:
+    import resource
+
+    return resource.getrusage(resource.RUSAGE_SELF).ru_maxrss * 1024  # Linux: KiB
+
+
+def setup_arm(args, ft, local: int, device, placement: str):
+    """Build the model, offload it, and run the discovery/profiling forwards into INFERENCE."""
     import torch
 
-    rank, world, local, pg = dist_setup(args.gpus)
-    device = torch.device("cuda", local)
-    ft, why = import_arm(args.impl)
-    if ft is None:
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": why}))
-        return
-    torch.manual_seed(1234 + rank)
-    if world > 1:
-        why = host_ram_check(args.impl, args.layers, world)
-        if why is not None:
-            if rank == 0:
-                print(json.dumps({"impl": args.impl, "n_gpus": world, "unavailable": why}))
-            pg.destroy_process_group()
-            return
-        if args.impl == "ours":
-            # N replicas of ONE model: each rank streams 1/N of every block over its own host
-            # link and pulls the rest from its peers over NVLink; its host keeps only that stripe
-            from flextensor_b200.parallel import enable_striped_streaming
-
-            enable_striped_streaming()
-    placement = "pinned_arena" if world == 1 else ("device" if args.impl == "ours" else "pageable")
     model, cfg = build_model(args.impl, args.layers, device, seed=0, placement=placement)
     frac, total_w, block_w, other_w = weight_budget_fraction(model, device)
     config = make_config(ft, local, frac, args.profiling_iters)
@@ -332,6 +315,63 @@ def main():
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t_setup
     assert str(om.phase).endswith("INFERENCE"), f"not in inference after warm-up forwards: {om.phase}"
+    return (model, cfg, om, (lat_h, ctx_h, ts_h, out_h, lat, ctx, ts), tokens, setup_s,
+            (total_w, block_w, other_w))
+
+
+def main():
+    args = parse()
+    import torch
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    ft, why = import_arm(args.impl)
+    if ft is None:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+        return
+    torch.manual_seed(1234 + rank)
+    if world > 1 and args.impl == "ours":
+        # N replicas of ONE model: each rank streams 1/N of every block over its own host
+        # link and pulls the rest from its peers over NVLink; its host keeps only that stripe
+        from flextensor_b200.parallel import enable_striped_streaming
+
+        enable_striped_streaming()
+    placement = args.placement
+    if placement == "auto":
+        placement = "pinned_arena" if world == 1 else "device"
+
+    if args.impl == "reference" and world > 1:
+        # The reference keeps a whole pinned copy of its offloaded weights in every process.
+        # Rank 0 sets up alone first; its MEASURED host footprint (peak RSS growth over the
+        # setup) then decides whether the other N-1 ranks fit in the RAM still available.
+        ok = torch.zeros(3, dtype=torch.float64, device=device)
+        if rank == 0:
+            rss0 = _rss_bytes()
+            arm = setup_arm(args, ft, local, device, placement)
+            foot = max(0, _peak_rss_bytes() - rss0)
+            import psutil
+
+            avail = psutil.virtual_memory().available
+            need = (world - 1) * foot * 1.10 + 8e9
+            ok[0] = 1.0 if need <= avail else -1.0
+            ok[1], ok[2] = foot, avail
+        pg.all_reduce(ok, op=pg.ReduceOp.SUM)
+        if float(ok[0]) < 0:
+            if rank == 0:
+                print(json.dumps({"impl": args.impl, "n_gpus": world, "unavailable": (
+                    f"host RAM (measured): rank 0's setup grew its resident host memory by "
+                    f"{float(ok[1]) / 1e9:.1f} GB (a whole pinned copy of its offloaded weights); "
+                    f"{world - 1} more such ranks need {(world - 1) * float(ok[1]) / 1e9:.0f} GB + margin "
+                    f"> {float(ok[2]) / 1e9:.0f} GB available")}))
+            pg.destroy_process_group()
+            return
+        if rank != 0:
+            arm = setup_arm(args, ft, local, device, placement)
+        barrier(pg)
+    else:
+        arm = setup_arm(args, ft, local, device, placement)
+    model, cfg, om, (lat_h, ctx_h, ts_h, out_h, lat, ctx, ts), tokens, setup_s, (total_w, block_w, other_w) = arm
 
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     with torch.no_grad():

@@ -543,6 +543,9 @@ void p2p_gather_raw(std::vector<uint64_t> heaps, std::vector<uint64_t> flags, st
   const int world = (int)heaps.size();
   TORCH_CHECK(world >= 1 && world <= ft::kMaxRanks && flags.size() == heaps.size() && acks.size() == heaps.size(),
               "one heap/flag/ack pointer per rank, at most ", ft::kMaxRanks);
+  TORCH_CHECK(rank >= 0 && rank < world, "rank ", rank, " outside [0, ", world, ")");
+  TORCH_CHECK(n_slots >= 1 && slot >= 0 && slot < n_slots, "slot ", slot, " outside [0, ", n_slots, ")");
+  TORCH_CHECK(ctas >= 1, "ctas must be >= 1");
   TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= n_slots,
               "counters: int32 CUDA tensor with one entry per slot");
   ft::PeerTable t;

@@ -24,3 +24,12 @@ cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t sl
 int p2p_device_error(bool reset);
 
 }  // namespace ft
+
+// No-allocation striped gather (defined in p2p.cu): the arrival counters live in a file-scope
+// device array of 256 entries instead of a caller buffer, so a call allocates no device memory.
+// heap_ptrs / flag_ptrs / ack_ptrs hold `world` device addresses each (valid in this process).
+// Returns a cudaError_t value; sizes beyond the array are rejected with cudaErrorInvalidValue.
+extern "C" int ft_p2p_gather_noalloc(const uint64_t* heap_ptrs, const uint64_t* flag_ptrs,
+                                     const uint64_t* ack_ptrs, int world, int rank, int n_slots, int slot,
+                                     uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
+                                     uint64_t total_bytes, int ctas, void* stream);

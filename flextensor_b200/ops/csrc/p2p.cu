@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "ft_p2p.h"
 #include "sm100_common.cuh"
 
@@ -156,6 +158,7 @@ cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t sl
 // for the symbol, so the kernel never receives it directly. The first call on each device
 // (with that device current) looks the address up with cudaGetSymbolAddress, checks the
 // result and caches it; make that first call on a device before any stream capture begins.
+// The cached address is not refreshed after a device reset (see the cache below).
 //
 // Every call on a device shares the one array, and the array keeps whatever the previous call
 // left. The counter of the slot in use is therefore cleared (cudaMemsetAsync on the caller's
@@ -170,8 +173,14 @@ constexpr int kGatherNoAllocMaxSlots = 256;
 constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) unsigned int g_gather_noalloc_counters[kGatherNoAllocMaxSlots];
 
+// Per-device cache of the array's device address. Entries are atomics (relaxed): two host
+// threads making the first call on one device at once may both look the address up, and both
+// store the same value. The cache does not survive a device reset: after cudaDeviceReset (or a
+// reset of the primary context) on a device, the cached address is stale, so callers that reset
+// a device must not use this entry point on it again in the same process.
+std::atomic<unsigned int*> g_noalloc_addr_cache[kNoAllocMaxDevices];
+
 unsigned int* noalloc_counters_for_current_device(cudaError_t* err) {
-  static unsigned int* cache[kNoAllocMaxDevices] = {};
   int dev = 0;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return nullptr;
@@ -179,13 +188,15 @@ unsigned int* noalloc_counters_for_current_device(cudaError_t* err) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
-  if (cache[dev] == nullptr) {
+  unsigned int* cached = g_noalloc_addr_cache[dev].load(std::memory_order_relaxed);
+  if (cached == nullptr) {
     void* p = nullptr;
     *err = cudaGetSymbolAddress(&p, g_gather_noalloc_counters);
     if (*err != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<unsigned int*>(p);
+    cached = static_cast<unsigned int*>(p);
+    g_noalloc_addr_cache[dev].store(cached, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return cached;
 }
 
 }  // namespace

@@ -47,6 +47,10 @@ class MemoryTransferInterpolator:
             i = max(0, bisect_left(xs, x) - 1)
         dx = xs[i + 1] - xs[i]
         if dx == 0:
+            # a zero-width end segment extrapolates flat from its outer point: the first point
+            # below the range, the last point above it (reference memory_transfer_interpolator.py:121-139)
+            if x >= xs[-1]:
+                return ys[-1]
             return ys[i]
         return ys[i] + (ys[i + 1] - ys[i]) * (x - xs[i]) / dx
 

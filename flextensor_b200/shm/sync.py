@@ -3,8 +3,9 @@
 Parity with ``src/flextensor/shm/sync_primitives.py`` (``SemaphoreLock``) and
 ``shm/multiprocess_condition.py`` (``SharedMultiString``, ``MultiprocessCondition``):
 
-* :class:`SemaphoreLock` -- a counting semaphore of ``slots`` permits. Each permit is an
-  ``fcntl`` byte-range lock on one byte of a lock file, so a permit held by a process that
+* :class:`SemaphoreLock` -- a counting semaphore of ``slots`` permits. Each permit is a
+  ``flock`` on its own file taken through a descriptor opened for that acquire, so handles
+  and threads in one process contend like processes do, and a permit held by a process that
   dies is released by the kernel (a POSIX named semaphore would stay decremented forever).
 * :class:`SharedMultiString` -- an append-only journal of names (e.g. the segments a session
   owns) with a ready marker; writers serialise on a file lock; readers see complete records.
@@ -20,40 +21,58 @@ import errno
 import fcntl
 import os
 import struct
+import threading
 import time
 
 from flextensor_b200.shm.segment import ProcessFileLock, shm_path
 
 
 class SemaphoreLock:
+    """Counting semaphore of ``slots`` permits shared by every process that opens ``name``.
+
+    Permit ``i`` is an exclusive ``flock`` on its own file ``<name>.sem.<i>``, taken on a file
+    descriptor opened for that one acquire. ``flock`` locks belong to the open file
+    description, not to the process, so two handles in one process, or two threads sharing a
+    handle, contend for permits exactly as two processes do, and closing one descriptor frees
+    only the permit taken through it. A permit held by a process that dies is released by the
+    kernel. One handle may hold several permits (one per acquire, e.g. from several threads);
+    ``release`` returns the most recent one.
+    """
+
     def __init__(self, name: str, slots: int = 1):
         if slots < 1:
             raise ValueError("slots must be >= 1")
         self.name, self.slots = name, slots
         self.path = shm_path(name) + ".sem"
-        self._fd = os.open(self.path, os.O_RDWR | os.O_CREAT, 0o600)
-        if os.fstat(self._fd).st_size < slots:
-            os.ftruncate(self._fd, slots)
-        self._held: int | None = None
+        fd = os.open(self.path, os.O_RDWR | os.O_CREAT, 0o600)  # marker: lets unlink find the set
+        os.close(fd)
+        self._permits = [f"{self.path}.{i}" for i in range(slots)]
+        self._held: list[tuple[int, int]] = []  # (permit index, fd holding its flock)
+        self._mutex = threading.Lock()
+        self._closed = False
 
-    def _try(self, i: int) -> bool:
+    def _try(self, i: int) -> int:
+        fd = os.open(self._permits[i], os.O_RDWR | os.O_CREAT, 0o600)
         try:
-            fcntl.lockf(self._fd, fcntl.LOCK_EX | fcntl.LOCK_NB, 1, i, os.SEEK_SET)
-            return True
+            fcntl.flock(fd, fcntl.LOCK_EX | fcntl.LOCK_NB)
+            return fd
         except OSError as e:
-            if e.errno in (errno.EAGAIN, errno.EACCES):
-                return False
+            os.close(fd)
+            if e.errno in (errno.EAGAIN, errno.EACCES, errno.EWOULDBLOCK):
+                return -1
             raise
 
     def acquire(self, non_blocking: bool = False, timeout: float | None = None) -> None:
-        if self._held is not None:
-            raise RuntimeError("this handle already holds a permit")
+        if self._closed:
+            raise RuntimeError(f"semaphore {self.name!r} is closed")
         deadline = None if timeout is None else time.monotonic() + timeout
         delay = 0.001
         while True:
             for i in range(self.slots):
-                if self._try(i):
-                    self._held = i
+                fd = self._try(i)
+                if fd >= 0:
+                    with self._mutex:
+                        self._held.append((i, fd))
                     return
             if non_blocking:
                 raise BlockingIOError(f"no free permit on {self.path}")
@@ -63,12 +82,20 @@ class SemaphoreLock:
             delay = min(delay * 2, 0.05)
 
     def release(self) -> None:
-        if self._held is None:
-            raise RuntimeError("release() without a held permit")
-        fcntl.lockf(self._fd, fcntl.LOCK_UN, 1, self._held, os.SEEK_SET)
-        self._held = None
+        with self._mutex:
+            if not self._held:
+                raise RuntimeError("release() without a held permit")
+            _, fd = self._held.pop()
+        fcntl.flock(fd, fcntl.LOCK_UN)
+        os.close(fd)
 
     signal = release
+
+    @property
+    def held(self) -> int:
+        """Permits this handle holds now."""
+        with self._mutex:
+            return len(self._held)
 
     def __enter__(self):
         self.acquire()
@@ -78,21 +105,21 @@ class SemaphoreLock:
         self.release()
 
     def close(self) -> None:
-        if self._fd >= 0:
-            if self._held is not None:
-                self.release()
-            os.close(self._fd)
-            self._fd = -1
+        """Release the permits this handle holds (no other handle's) and retire the handle."""
+        while self.held:
+            self.release()
+        self._closed = True
 
     def unlink(self) -> None:
         self.close()
         self.unlink_name()
 
     def unlink_name(self) -> None:
-        try:
-            os.unlink(self.path)
-        except FileNotFoundError:
-            pass
+        for p in [*self._permits, self.path]:
+            try:
+                os.unlink(p)
+            except FileNotFoundError:
+                pass
 
 
 class SharedMultiString:

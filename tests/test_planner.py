@@ -149,3 +149,13 @@ def test_interpolator_flat_noisy_curve_does_not_overflow():
     big = interp.duration_to_bytes(1000.0)
     assert 0 < big <= 2.0 ** 62 * (1 + 1e-9)
     assert interp.bytes_to_duration(1 << 40) <= 2.0 ** 62 * (1 + 1e-9)
+
+
+def test_interpolator_tied_end_durations_extrapolate_to_the_outer_point():
+    # last two points take the same time: above the range the reference returns the larger
+    # byte count (flat extrapolation from the last point); below a tied first segment it
+    # returns the smaller one
+    it = MemoryTransferInterpolator({1 << 20: 1.0, 2 << 20: 2.0, 4 << 20: 2.0})
+    assert it.duration_to_bytes(5.0) == pytest.approx(4 << 20)
+    lo = MemoryTransferInterpolator({1 << 20: 1.0, 2 << 20: 1.0, 4 << 20: 2.0})
+    assert lo.duration_to_bytes(0.5) == pytest.approx(1 << 20)

@@ -103,3 +103,56 @@ def test_journal_and_condition():
     with pytest.raises(TimeoutError):
         MultiprocessCondition(f"ftcv{uuid.uuid4().hex[:8]}").wait_for_ready(timeout=0.2)
     cond.unlink()
+
+
+def test_two_handles_in_one_process_contend():
+    name = f"ftsem{uuid.uuid4().hex[:8]}"
+    a, b = SemaphoreLock(name, 1), SemaphoreLock(name, 1)
+    a.acquire(timeout=5)
+    with pytest.raises(BlockingIOError):
+        b.acquire(non_blocking=True)
+    a.release()
+    b.acquire(non_blocking=True)
+    b.release()
+    a.unlink()
+
+
+def test_closing_one_handle_keeps_the_others_permit():
+    name = f"ftsem{uuid.uuid4().hex[:8]}"
+    holder, other, probe = SemaphoreLock(name, 1), SemaphoreLock(name, 1), SemaphoreLock(name, 1)
+    holder.acquire(timeout=5)
+    other.close()  # closing a handle that holds nothing must not free holder's permit
+    with pytest.raises(BlockingIOError):
+        probe.acquire(non_blocking=True)
+    holder.close()  # frees it
+    probe.acquire(non_blocking=True)
+    probe.unlink()
+
+
+def test_threads_sharing_a_handle_are_bounded():
+    import threading
+
+    name = f"ftsem{uuid.uuid4().hex[:8]}"
+    s = SemaphoreLock(name, 2)
+    lock = threading.Lock()
+    state = {"inside": 0, "peak": 0}
+    go = threading.Barrier(6)
+
+    def worker():
+        go.wait(timeout=10)
+        s.acquire(timeout=30)
+        with lock:
+            state["inside"] += 1
+            state["peak"] = max(state["peak"], state["inside"])
+        time.sleep(0.05)
+        with lock:
+            state["inside"] -= 1
+        s.release()
+
+    ts = [threading.Thread(target=worker) for _ in range(6)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(60)
+    assert state["peak"] == 2 and s.held == 0
+    s.unlink()
