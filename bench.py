@@ -60,8 +60,8 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        # raw samples go to FT_BENCH_CLOCKS_DIR (default: the system temp directory)
-        out_dir = os.environ.get("FT_BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        # raw samples go to BENCH_CLOCKS_DIR (default: the system temp directory)
+        out_dir = os.environ.get("BENCH_CLOCKS_DIR") or tempfile.gettempdir()
         self.out = os.path.join(out_dir, f"ft_bench_clocks_rank{index}_{os.getpid()}.csv")
 
     def start(self):

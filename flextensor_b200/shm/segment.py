@@ -6,6 +6,9 @@ process that knows the name attaches to the same pages. Locks are ``fcntl``
 advisory locks on a lock file (released by the kernel if the holder dies, so a
 crashed creator can never wedge an election).
 
+NUMA: with ``FT_SHM_NUMA_INTERLEAVE=1`` (or ``auto``) a creator interleaves its segment's
+pages over the memory nodes before writing them (``flextensor_b200.shm.numa``).
+
 Pinning: ``pin()`` page-locks the mapping in place with ``cudaHostRegister``
 (native helper) so every local worker's copy engine DMAs from the SAME host
 pages -- one host copy of the weights for all ranks.
@@ -45,6 +48,7 @@ class ShmSegment:
         self.name = name.lstrip("/")
         self.path = shm_path(self.name)
         self.created = create
+        self._tensor = None
         flags = os.O_RDWR | (os.O_CREAT | os.O_EXCL if create else 0)
         self._fd = os.open(self.path, flags, 0o600)
         try:
@@ -52,13 +56,18 @@ class ShmSegment:
                 os.ftruncate(self._fd, max(size, 1))
             self.size = os.fstat(self._fd).st_size if not create else max(size, 1)
             self._mm = mmap.mmap(self._fd, self.size, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
+            self.numa_interleaved = False
+            if create:
+                # before the first write: the pages take the policy when they are first allocated
+                from flextensor_b200.shm.numa import apply_to_new_mapping
+
+                self.numa_interleaved = apply_to_new_mapping(self.tensor().data_ptr(), self.size)
         except BaseException:
             os.close(self._fd)
             if create:
                 shm_unlink(self.name)
             raise
         self._pinned_ptr = 0
-        self._tensor = None
 
     @classmethod
     def create(cls, name: str, size: int) -> "ShmSegment":
