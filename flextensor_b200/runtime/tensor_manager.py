@@ -230,29 +230,27 @@ class TensorManager:
             self._move_attribute_tensors()
 
     def _move_attribute_tensors(self) -> None:
-        """Plain tensor attributes of modules (not registered as parameter or buffer, e.g. a
-        cached frequency table) follow the model to the device, as the reference's unmapped-
-        tensor processor does (``tensor_processors.py:686``); lists/tuples/dicts of tensors
-        held as attributes are handled one level deep."""
+        """Tensors the model holds outside its registered parameters and buffers follow it to
+        the device, as the reference's unmapped-tensor processor does
+        (``tensor_processors.py:686-744``): plain module attributes (a cached frequency table),
+        tensors nested in lists / tuples / dicts / sets / helper objects at any depth, and the
+        tensor-valued inner fields of parameters (``weight.weight_scale`` of a quantized layer).
+        A tensor reachable from several places is moved once and every place gets the copy."""
+        from flextensor_b200.core.visitor import TensorVisitor, carry_inner_fields
+
         moved: dict[int, torch.Tensor] = {}
+        offloaded = {id(p) for tid, p in self.params_by_tid.items() if tid in self.owner}
 
         def to_dev(t: torch.Tensor) -> torch.Tensor:
-            if t.device == self.device or t.is_meta:
+            if t.is_meta or t.device == self.device or id(t) in offloaded:
                 return t
             if id(t) not in moved:
                 moved[id(t)] = t.to(self.device)
             return moved[id(t)]
 
-        for m in self.model.modules():
-            for k, v in list(vars(m).items()):
-                if k.startswith("_") or isinstance(v, nn.Parameter):
-                    continue
-                if isinstance(v, torch.Tensor):
-                    setattr(m, k, to_dev(v))
-                elif isinstance(v, (list, tuple)) and v and all(isinstance(x, torch.Tensor) for x in v):
-                    setattr(m, k, type(v)(to_dev(x) for x in v))
-                elif isinstance(v, dict) and v and all(isinstance(x, torch.Tensor) for x in v.values()):
-                    setattr(m, k, {kk: to_dev(x) for kk, x in v.items()})
+        TensorVisitor(to_dev, params=False, buffers=False, attributes=True).apply(self.model)
+        for p in self.params_by_tid.values():
+            carry_inner_fields(p, p, to_dev)
 
     # ================================================================== phases
     def _striping(self):
@@ -677,6 +675,9 @@ class TensorManager:
             p.data = t
             return
         newp = nn.Parameter(t, requires_grad=False)
+        from flextensor_b200.core.visitor import carry_inner_fields
+
+        carry_inner_fields(p, newp)  # loader metadata (weight_loader, output_dim, ...) stays
         name = self.id_to_name[tid]
         for n, q in list(self.model.named_parameters(remove_duplicate=False)):
             if q is p:
