@@ -133,7 +133,7 @@ class WanTorchBlock(nn.Module):
         v = a.to_v(h).view(B, S, H, Dh)
         x = (x.float() + a.to_out(_sdpa(q, k, v)).float() * g1).to(x.dtype)
         a = self.attn2
-        h = self.norm2(x.float()).to(x.dtype)
+        h = F.layer_norm(x.float(), (D,), self.norm2.weight.float(), self.norm2.bias.float(), cfg.eps).to(x.dtype)
         L = ctx.shape[1]
         q = a.norm_q(a.to_q(h)).view(B, S, H, Dh)
         k = a.norm_k(a.to_k(ctx)).view(B, L, H, Dh)

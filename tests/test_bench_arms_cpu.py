@@ -50,6 +50,21 @@ def test_same_function_on_same_weights():
     torch.testing.assert_close(yb, ya, rtol=1e-4, atol=1e-5)
 
 
+def test_bf16_forward_matches_ours():
+    cfg, ours, ref = _pair()
+    init_wan_params_(ours, seed=4)
+    ref.load_state_dict(ours.state_dict())
+    ours, ref = ours.to(torch.bfloat16), ref.to(torch.bfloat16)
+    torch.manual_seed(1)
+    lat = torch.randn(1, cfg.in_channels, 2, 4, 6)
+    ts = torch.tensor([500.0])
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim)
+    with torch.no_grad():
+        ya = ours(lat, ts, ctx).float()
+        yb = ref(lat, ts, ctx).float()
+    torch.testing.assert_close(yb, ya, rtol=2e-2, atol=2e-2)
+
+
 def test_reference_init_is_seeded():
     _, _, ref = _pair()
     init_params_(ref, seed=5)
