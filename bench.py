@@ -380,6 +380,9 @@ def main():
     torch.cuda.synchronize()
     torch.cuda.reset_peak_memory_stats(device)
 
+    eng0 = _engine(om) if args.impl == "ours" else None
+    if eng0 is not None and hasattr(eng0, "take_phase_samples"):
+        eng0.take_phase_samples()  # drop the warm-up steps' phases
     launches0 = _launches(args.impl, om)
     clocks = ClockSampler(local)
     clocks.start()
@@ -396,6 +399,12 @@ def main():
         torch.cuda.synchronize()
     barrier(pg)
     step_ms = [s.elapsed_time(e) for s, e in times]
+    striped = None
+    if eng0 is not None and hasattr(eng0, "take_phase_samples"):
+        ph = eng0.take_phase_samples()
+        striped = {"gather": eng0.gather, "copy_stream_ms_per_step": {
+            k: round(ph[k] / max(1, args.steps), 2) for k in ("wait_acks", "h2d_stripe", "gather")},
+            "transfers_per_step": ph["transfers"] // max(1, args.steps)}
     launches = (_launches(args.impl, om) - launches0) // max(1, args.steps) if launches0 is not None else None
     # ring slots in the symmetric heap (striped runs) live outside torch's allocator: add them
     eng = _engine(om) if args.impl == "ours" else None
@@ -465,6 +474,7 @@ def main():
         "e2e": None if e2e_max is None else {"value": round(e2e_max, 5), "unit": "s/step", "h2d_bytes_per_step": h2d,
                                               "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
+        "striped": striped,
         "config": {"model": MODEL if args.layers == 40 else f"{MODEL} [layers={args.layers}: NOT the headline]",
                    "global_batch": world, "seq_len": tokens,
                    "parallelism": f"dp{world}" + (" + striped host streaming (1/N per rank, NVLink gather)"

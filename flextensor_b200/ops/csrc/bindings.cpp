@@ -594,7 +594,8 @@ struct PyEngine {
   void finish_use(int slot) { e->finish_use(slot, cs()); }
   void join() { e->join(cs()); }
   void enable_striping(std::vector<uintptr_t> heaps, std::vector<uintptr_t> flags, std::vector<uintptr_t> acks,
-                       int rank, int n_slots, std::vector<uint64_t> slot_offsets, uintptr_t counters, int ctas) {
+                       int rank, int n_slots, std::vector<uint64_t> slot_offsets, uintptr_t counters, int ctas,
+                       int gather_mode) {
     const int world = (int)heaps.size();
     TORCH_CHECK(world >= 1 && world <= ft::kMaxRanks, "world size must be in [1, 8]");
     TORCH_CHECK((int)flags.size() == world && (int)acks.size() == world, "per-rank pointer lists differ in length");
@@ -607,7 +608,10 @@ struct PyEngine {
     t.rank = rank;
     t.world = world;
     t.n_slots = n_slots;
-    e->enable_striping(t, slot_offsets, reinterpret_cast<unsigned int*>(counters), ctas);
+    TORCH_CHECK(rank >= 0 && rank < world, "rank outside [0, world)");
+    TORCH_CHECK(n_slots >= 1 && (int)slot_offsets.size() == n_slots, "one heap offset per slot");
+    TORCH_CHECK(ctas >= 1, "ctas must be >= 1");
+    e->enable_striping(t, slot_offsets, reinterpret_cast<unsigned int*>(counters), ctas, gather_mode);
   }
   // total_bytes < 0: src is the whole packed block. Otherwise src holds only this rank's
   // stripe of a packed block of total_bytes bytes.
@@ -629,6 +633,11 @@ struct PyEngine {
     e->drain_striped();
   }
   void synchronize() { e->synchronize(); }
+  std::vector<std::tuple<int, float, float, float>> take_phase_samples() {
+    std::vector<std::tuple<int, float, float, float>> out;
+    for (auto& s : e->take_phase_samples()) out.emplace_back(s.key, s.acks_ms, s.h2d_ms, s.gather_ms);
+    return out;
+  }
   std::vector<std::tuple<int, size_t, float, float>> take_samples() {
     std::vector<std::tuple<int, size_t, float, float>> out;
     for (auto& s : e->take_samples()) out.emplace_back(s.key, s.bytes, s.transfer_ms, s.wait_ms);
@@ -693,5 +702,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("drain_striped", &PyEngine::drain_striped)
       .def("kernel_launches", [](const PyEngine& p) { return p.e->kernel_launches(); })
       .def("synchronize", &PyEngine::synchronize)
-      .def("take_samples", &PyEngine::take_samples);
+      .def("take_samples", &PyEngine::take_samples)
+      .def("take_phase_samples", &PyEngine::take_phase_samples);
 }

@@ -21,6 +21,8 @@ cudaError_t p2p_publish(const PeerTable& t, int slot, uint64_t epoch, cudaStream
 cudaError_t p2p_wait_acks(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s);
 cudaError_t p2p_gather(const PeerTable& t, int slot, uint64_t epoch, uint64_t slot_offset, uint64_t stripe_bytes,
                        uint64_t total_bytes, unsigned int* done_counter, int ctas, cudaStream_t s);
+cudaError_t p2p_wait_flags(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s);
+cudaError_t p2p_ack(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s);
 int p2p_device_error(bool reset);
 
 }  // namespace ft

@@ -20,6 +20,16 @@ struct TransferSample {
   float wait_ms = 0.f;
 };
 
+// Striped transfers, per phase on the copy stream (timing mode only): waiting for the peers'
+// acknowledgements of the slot's previous epoch, this rank's H2D stripe, and the gather of the
+// peers' stripes (including the wait for their publish flags).
+struct PhaseSample {
+  int key = 0;
+  float acks_ms = 0.f;
+  float h2d_ms = 0.f;
+  float gather_ms = 0.f;
+};
+
 // Symmetric heap: cudaMalloc'd on this device, exported with CUDA IPC.
 void* device_malloc(size_t bytes);
 void device_free(void* p);
@@ -41,8 +51,11 @@ class TransferEngine {
   cudaStream_t copy_stream() const { return copy_; }
   // Striped mode: slot `s` lives at heap offset slot_offsets[s] of every rank's symmetric heap;
   // submit() then copies only this rank's stripe and gathers the others from peers.
+  // gather_mode 0: the SM pull kernel (gather_ctas CTAs); 1: copy engine (one cudaMemcpyAsync
+  // per peer stripe between a bounded flag-wait kernel and an ack kernel).
   void enable_striping(const PeerTable& t, const std::vector<uint64_t>& slot_offsets, unsigned int* counters,
-                       int gather_ctas);
+                       int gather_ctas, int gather_mode = 0);
+  std::vector<PhaseSample> take_phase_samples();
   // host_src is the whole packed block, or (stripe_only) just this rank's stripe of it.
   void submit_striped(int slot, const void* host_src, size_t bytes, int key, bool stripe_only);
   // Wait (bounded, on the copy stream) until every peer acknowledged the latest epoch of every
@@ -73,6 +86,11 @@ class TransferEngine {
   std::vector<uint64_t> epochs_;
   unsigned int* counters_ = nullptr;
   int gather_ctas_ = 32;
+  int gather_mode_ = 0;
+  std::vector<cudaEvent_t> ph_acked_, ph_h2d_;  // per key: after wait_acks, after the H2D stripe
+  std::vector<char> ph_valid_;
+  std::vector<PhaseSample> phase_pending_;
+  void collect_phase(size_t k);
 };
 
 }  // namespace ft

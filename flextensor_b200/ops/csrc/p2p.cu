@@ -11,6 +11,9 @@
 //              every peer (so p may overwrite its slot for the next epoch);
 //   wait_acks: before the next H2D into a slot, wait until every peer acked the previous
 //              epoch of that slot.
+// Copy-engine variant of the gather (gather mode 1): wait_flags (one warp, bounded) ->
+// one cudaMemcpyAsync per peer stripe on the copy stream (DMA over NVLink, no SM time) ->
+// ack (one thread stores the acknowledgements).
 // These kernels wait on OTHER GPUs only (never on another launch on the same GPU). No
 // TMA and no multicast is used: plain peer loads and stores. Every wait has a clock64
 // bound; on timeout the kernel records kErrPeerTimeout in the device error word and returns.
@@ -116,7 +119,38 @@ gather_kernel(PeerTable t, int slot, uint64_t epoch, uint64_t slot_offset, uint6
   }
 }
 
+// Copy-engine gather, step 1: one warp waits (bounded) until every peer published `epoch` for
+// `slot`, so the copies queued behind it on the stream read complete stripes.
+__global__ void wait_flags_kernel(PeerTable t, int slot, uint64_t epoch) {
+  if (blockIdx.x == 0 && threadIdx.x < t.world && threadIdx.x != t.rank)
+    wait_geq(t.flags[t.rank] + (size_t)threadIdx.x * t.n_slots + slot, epoch);
+}
+
+// Copy-engine gather, step 3 (after the peer copies on the stream): tell every peer we are done
+// reading its stripe of this epoch.
+__global__ void ack_kernel(PeerTable t, int slot, uint64_t epoch) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < t.world; p++) {
+      if (p == t.rank) continue;
+      st_release_sys(t.acks[p] + (size_t)t.rank * t.n_slots + slot, epoch);
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t p2p_wait_flags(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s) {
+  if (t.world <= 1) return cudaSuccess;
+  wait_flags_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t p2p_ack(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s) {
+  if (t.world <= 1) return cudaSuccess;
+  ack_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
+  return cudaGetLastError();
+}
 
 cudaError_t p2p_publish(const PeerTable& t, int slot, uint64_t epoch, cudaStream_t s) {
   publish_kernel<<<1, 32, 0, s>>>(t, slot, epoch);

@@ -171,7 +171,7 @@ TransferEngine::~TransferEngine() {
   cudaStreamSynchronize(copy_);
   for (auto e : slot_free_) cudaEventDestroy(e);
   for (auto e : ready_) cudaEventDestroy(e);
-  for (auto* v : {&t_start_, &t_end_, &w_start_, &w_end_})
+  for (auto* v : {&t_start_, &t_end_, &w_start_, &w_end_, &ph_acked_, &ph_h2d_})
     for (auto e : *v) cudaEventDestroy(e);
   cudaEventDestroy(fork_);
   cudaEventDestroy(join_);
@@ -231,13 +231,26 @@ void TransferEngine::join(cudaStream_t compute) {
 void TransferEngine::synchronize() { FT_CHECK(cudaStreamSynchronize(copy_)); }
 
 void TransferEngine::enable_striping(const PeerTable& t, const std::vector<uint64_t>& slot_offsets,
-                                     unsigned int* counters, int gather_ctas) {
+                                     unsigned int* counters, int gather_ctas, int gather_mode) {
+  if (gather_mode != 0 && gather_mode != 1) throw std::runtime_error("gather_mode must be 0 (SM) or 1 (copy engine)");
   peers_ = t;
   slot_offsets_ = slot_offsets;
   epochs_.assign(slot_offsets.size(), 0);
   counters_ = counters;
   gather_ctas_ = gather_ctas;
+  gather_mode_ = gather_mode;
   striped_ = t.world > 1;
+  if (timing_ && ph_acked_.empty()) {
+    int prev;
+    FT_CHECK(cudaGetDevice(&prev));
+    FT_CHECK(cudaSetDevice(device_));
+    ph_acked_.resize(t_start_.size());
+    ph_h2d_.resize(t_start_.size());
+    ph_valid_.assign(t_start_.size(), 0);
+    for (auto& e : ph_acked_) FT_CHECK(cudaEventCreate(&e));
+    for (auto& e : ph_h2d_) FT_CHECK(cudaEventCreate(&e));
+    cudaSetDevice(prev);
+  }
 }
 
 void TransferEngine::drain_striped() {
@@ -266,7 +279,8 @@ void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes
   if (t) FT_CHECK(cudaEventRecord(t_start_[key], copy_));
   // peers must have finished reading this slot's previous contents (our stripe) before we overwrite it
   FT_CHECK(p2p_wait_acks(peers_, slot, epoch - 1, copy_));
-  kernel_launches_ += (epoch > 1) ? 3 : 2;  // [wait_acks], publish, gather
+  const bool ph = t && !ph_acked_.empty();
+  if (ph) FT_CHECK(cudaEventRecord(ph_acked_[key], copy_));
   const int r = peers_.rank;
   const uint64_t stripe = stripe_len(bytes);
   const uint64_t b0 = std::min<uint64_t>((uint64_t)r * stripe, bytes);
@@ -275,8 +289,26 @@ void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes
   if (b1 > b0)
     FT_CHECK(cudaMemcpyAsync(dst + b0, static_cast<const uint8_t*>(host_src) + (stripe_only ? 0 : b0), b1 - b0,
                              cudaMemcpyHostToDevice, copy_));
+  if (ph) FT_CHECK(cudaEventRecord(ph_h2d_[key], copy_));
   FT_CHECK(p2p_publish(peers_, slot, epoch, copy_));
-  FT_CHECK(p2p_gather(peers_, slot, epoch, slot_offsets_[slot], stripe, bytes, counters_, gather_ctas_, copy_));
+  if (gather_mode_ == 0) {
+    kernel_launches_ += (epoch > 1) ? 3 : 2;  // [wait_acks], publish, gather
+    FT_CHECK(p2p_gather(peers_, slot, epoch, slot_offsets_[slot], stripe, bytes, counters_, gather_ctas_, copy_));
+  } else {
+    // copy engine: wait for every peer's stripe, DMA each one over NVLink, acknowledge
+    kernel_launches_ += (epoch > 1) ? 4 : 3;  // [wait_acks], publish, wait_flags, ack
+    FT_CHECK(p2p_wait_flags(peers_, slot, epoch, copy_));
+    for (int pi = 1; pi < peers_.world; pi++) {
+      const int p = (r + pi) % peers_.world;  // staggered like the SM gather
+      const uint64_t c0 = std::min<uint64_t>((uint64_t)p * stripe, bytes);
+      const uint64_t c1 = std::min<uint64_t>(c0 + stripe, bytes);
+      if (c1 > c0)
+        FT_CHECK(cudaMemcpyAsync(dst + c0, peers_.heap[p] + slot_offsets_[slot] + c0, c1 - c0,
+                                 cudaMemcpyDeviceToDevice, copy_));
+    }
+    FT_CHECK(p2p_ack(peers_, slot, epoch, copy_));
+  }
+  if (ph) ph_valid_[key] = 1;
   FT_CHECK(cudaEventRecord(ready_[key], copy_));
   ready_recorded_[key] = 1;
   if (t) {
@@ -284,6 +316,30 @@ void TransferEngine::submit_striped(int slot, const void* host_src, size_t bytes
     bytes_[key] = bytes;
     t_valid_[key] = 1;
   }
+}
+
+// Moves the phase timings of key k (whose transfer events are valid) into phase_pending_.
+void TransferEngine::collect_phase(size_t k) {
+  if (k >= ph_valid_.size() || !ph_valid_[k]) return;
+  PhaseSample s;
+  s.key = (int)k;
+  FT_CHECK(cudaEventSynchronize(t_end_[k]));
+  FT_CHECK(cudaEventElapsedTime(&s.acks_ms, t_start_[k], ph_acked_[k]));
+  FT_CHECK(cudaEventElapsedTime(&s.h2d_ms, ph_acked_[k], ph_h2d_[k]));
+  FT_CHECK(cudaEventElapsedTime(&s.gather_ms, ph_h2d_[k], t_end_[k]));
+  phase_pending_.push_back(s);
+  ph_valid_[k] = 0;
+}
+
+std::vector<PhaseSample> TransferEngine::take_phase_samples() {
+  if (!ph_valid_.empty()) {
+    FT_CHECK(cudaStreamSynchronize(copy_));
+    for (size_t k = 0; k < ph_valid_.size(); k++)
+      if (t_valid_[k]) collect_phase(k);
+  }
+  std::vector<PhaseSample> out;
+  out.swap(phase_pending_);
+  return out;
 }
 
 std::vector<TransferSample> TransferEngine::take_samples() {
@@ -302,6 +358,7 @@ std::vector<TransferSample> TransferEngine::take_samples() {
       FT_CHECK(cudaEventElapsedTime(&s.wait_ms, w_start_[k], w_end_[k]));
     }
     out.push_back(s);
+    collect_phase(k);  // before the transfer events are recycled
     t_valid_[k] = 0;
     w_valid_[k] = 0;
   }

@@ -2,9 +2,10 @@
 
 With N ranks each running a replica of the same offloaded model, every ring slot
 lives in a symmetric heap. When a trap's weights are prefetched, rank r copies
-only stripe r (1/N of the packed host block) over its own PCIe link, then a pull
-kernel gathers the other N-1 stripes from the peers' slots over NVLink (see
-``ops/csrc/p2p.cu``). Host-link bytes per rank drop N-fold, so the node's
+only stripe r (1/N of the packed host block) over its own PCIe link, then the
+other N-1 stripes come from the peers' slots over NVLink: by a pull kernel of small
+CTAs (``FT_STRIPED_GATHER=sm``, the default) or by the copy engines between two
+one-warp signalling kernels (``FT_STRIPED_GATHER=ce``; see ``ops/csrc/p2p.cu``). Host-link bytes per rank drop N-fold, so the node's
 aggregate PCIe bandwidth -- and, with the shared-memory store, one host copy of
 the weights -- serves all ranks.
 
@@ -27,6 +28,22 @@ from flextensor_b200.parallel.symm import SymmetricHeap
 from flextensor_b200.instrumentation.core import instrumentable
 
 _register_env_var("FT_STRIPED_STREAMING")
+_register_env_var("FT_STRIPED_GATHER")
+_register_env_var("FT_STRIPED_GATHER_CTAS")
+
+GATHER_MODES = {"sm": 0, "ce": 1}
+
+
+def gather_mode() -> str:
+    """How the peers' stripes cross NVLink: ``sm`` (default) -- a pull kernel of small CTAs
+    on the copy stream; ``ce`` -- the copy engines (one cudaMemcpyAsync per peer stripe between
+    a one-warp bounded flag wait and an acknowledgement kernel), which leaves the SMs to the
+    compute kernels. ``FT_STRIPED_GATHER`` selects it."""
+    m = os.environ.get("FT_STRIPED_GATHER", "sm").strip().lower() or "sm"
+    if m not in GATHER_MODES:
+        raise ValueError(f"FT_STRIPED_GATHER={m!r}: expected one of {sorted(GATHER_MODES)}")
+    return m
+
 
 _STATE = {"enabled": False, "group": None}
 HEADER_ALIGN = 4096
@@ -59,7 +76,12 @@ class StripedTransferEngine:
     """Native engine in striped mode; owns the symmetric heap that backs the ring slots."""
 
     def __init__(self, device: torch.device, slot_bytes: dict[int, int], group=None, timing: bool = False,
-                 gather_ctas: int = 16, max_keys: int = 4096):
+                 gather_ctas: int | None = None, max_keys: int = 4096, gather: str | None = None):
+        if gather_ctas is None:
+            gather_ctas = int(os.environ.get("FT_STRIPED_GATHER_CTAS", "16"))
+        self.gather = gather or gather_mode()
+        if self.gather not in GATHER_MODES:
+            raise ValueError(f"gather={self.gather!r}: expected one of {sorted(GATHER_MODES)}")
         self.device = torch.device(device)
         n_slots = max(slot_bytes) + 1 if slot_bytes else 1
         import torch.distributed as dist
@@ -83,7 +105,7 @@ class StripedTransferEngine:
         self._names: list[str] = []
         self._e = native.lib().TransferEngine(self.device.index or 0, n_slots, max_keys, bool(timing))
         self._e.enable_striping(list(self.heap.ptrs), flags, acks, self.heap.rank, n_slots, offs, counters,
-                                gather_ctas)
+                                gather_ctas, GATHER_MODES[self.gather])
         self.timing = timing
         dist.barrier(group=group)  # every rank's heap is open before anyone publishes into it
 
@@ -117,6 +139,19 @@ class StripedTransferEngine:
     def submit_stripe(self, slot: int, stripe: torch.Tensor, key: str, total_bytes: int) -> None:
         """``stripe`` holds only this rank's stripe of a packed block of ``total_bytes``."""
         self._e.submit_striped(int(slot), stripe, self._k(key), int(total_bytes))
+
+    def take_phase_samples(self) -> dict[str, float]:
+        """Copy-stream time per phase (ms) summed over the transfers since the last call, in
+        timing mode: ``wait_acks`` (peers still reading the slot's previous stripe),
+        ``h2d_stripe`` (this rank's host-link copy), ``gather`` (publish + the peers' stripes
+        over NVLink, including the wait for their flags); ``transfers`` counts them."""
+        out = {"wait_acks": 0.0, "h2d_stripe": 0.0, "gather": 0.0, "transfers": 0}
+        for _, a, h, g in self._e.take_phase_samples():
+            out["wait_acks"] += a
+            out["h2d_stripe"] += h
+            out["gather"] += g
+            out["transfers"] += 1
+        return out
 
     def wait_ready(self, key: str) -> None:
         k = self._keys.get(key)

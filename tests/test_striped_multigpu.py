@@ -21,12 +21,12 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, on_device):
+def _worker(rank, world, port, q, on_device, gather="sm"):
     import datetime
 
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", FT_STRIPED_GATHER=gather)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
@@ -62,7 +62,7 @@ def _worker(rank, world, port, q, on_device):
             ok &= bool(torch.equal(mm(lat, ts, ctx), want))
     torch.cuda.synchronize()
     loader = om.get_tensor_manager().loader
-    engine = type(loader.engine).__name__
+    engine = f"{type(loader.engine).__name__}/{loader.engine.gather}"
     stripe_only = all(b.stripe_only for b in loader.plan.host_blocks.values()) and bool(loader.plan.host_blocks)
     err = native.device_error(reset=True)
     dist.barrier()
@@ -74,22 +74,23 @@ def _worker(rank, world, port, q, on_device):
     q.put((rank, ok, engine, err, stripe_only, restored))
 
 
+@pytest.mark.parametrize("gather", ["sm", "ce"])
 @pytest.mark.parametrize("on_device", [False, True], ids=["host_source", "device_source_stripe_only"])
-def test_striped_streaming_two_ranks(on_device):
+def test_striped_streaming_two_ranks(on_device, gather):
     import torch.multiprocessing as mp
 
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, q, on_device)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q, on_device, gather)) for r in range(world)]
     for p in ps:
         p.start()
     res = sorted(q.get(timeout=300) for _ in ps)
     for p in ps:
         p.join(60)
     for rank, ok, engine, err, stripe_mode_ok, restored in res:
-        assert engine == "StripedTransferEngine"
+        assert engine == f"StripedTransferEngine/{gather}"
         assert err == 0
         assert ok, f"rank {rank} output differs from the resident model"
         assert stripe_mode_ok, f"rank {rank}: host blocks are not stripe-only"
