@@ -1032,6 +1032,375 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Split-row variant (``_diag_mode`` 300 + EMU): the default kernel's two ping-ponging 128-query
+// tiles, with every query row's softmax shared by TWO warps, one per 64-key half of the S row.
+// 18 warps (576 threads):
+//   warps 0-7   tile A: warps 0-3 keys 0-63, warps 4-7 keys 64-127 (warp w: TMEM lanes 32(w%4)..+31)
+//   warps 8-15  tile B, same split
+//   warp 16     TMEM owner + MMA issuer;  warp 17  TMA producer
+// Each softmax warp's chain per KV block is half the default one (64 instead of 128 values per
+// thread), and four softmax warps per scheduler keep the MUFU and FMA pipes busier, which
+// shortens the softmax -> PV -> QK^T chain that sets the default kernel's period.
+// The two halves of a row agree on its running max by exchanging their partial maxima through
+// shared memory (double-buffered by block parity, a 64-thread named barrier per warp pair), so
+// they take identical rescale decisions. The exchange is an mbarrier per warp pair (64 arrivals,
+// bounded waits), never a hardware named barrier, so a warp that unwinds on an error cannot leave
+// its partner blocked. P of keys 0-63 is packed into S columns 0-31 and P of
+// keys 64-127 into columns 64-95 (each half overwrites only S columns it has already read).
+// Barriers per tile: p_lo (8 arrivals: half-0 warps once their P is stored, half-1 warps once
+// their share of any O rescale is done) gates PV over keys 0-63; p_hi (4 arrivals, half-1 warps'
+// P) gates PV over keys 64-127. O rescales (rare: stale-max threshold 2^8) are split by column
+// halves and finish before p_lo, i.e. before any PV of the block.
+constexpr int NTHREADS2X = 576;
+struct Smem2x : SmemBase {
+  float xmax[2][2][2][TILE];  // [block parity][tile][half][row]: partial row maxima
+  float lsum[2][2][TILE];     // [tile][half][row]: partial row sums for the epilogue
+  uint64_t p_lo[2], p_hi[2];
+  uint64_t xbar[2][4];        // [tile][quad]: the two warps that share rows 32*quad..+31
+};
+
+// Both warps of a pair arrive (all lanes, after their shared-memory writes) and wait, bounded,
+// for the phase of this exchange.
+__device__ __forceinline__ bool pair_exchange(uint64_t* bar, uint32_t parity) {
+  mbar_arrive(bar);
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+template <int EMU>
+__global__ void __maxnreg__(112)
+    attn2x_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem2x& sm = *reinterpret_cast<Smem2x*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int qb = blockIdx.x % a.n_qblocks;
+  const int h = (blockIdx.x / a.n_qblocks) % a.Hq;
+  const int b = blockIdx.x / (a.n_qblocks * a.Hq);
+  const int hk = h / (a.Hq / a.Hk);
+  const int q0 = qb * 2 * TILE;
+  int n_kv = (a.Sk + TILE - 1) / TILE;
+  if (a.causal) n_kv = min(n_kv, (q0 + 2 * TILE + TILE - 1) / TILE);
+  const bool has_b = q0 + TILE < a.Sq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < KV_STAGES; s++) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; t++) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_lo[t], 8);
+      mbar_init(&sm.p_hi[t], 4);
+      mbar_init(&sm.o_done[t], 1);
+      for (int q = 0; q < 4; q++) mbar_init(&sm.xbar[t][q], 64);
+    }
+    mbar_init(&sm.drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 16) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+
+  if (warp == 17) {
+    // ------------------------------------------------------------------ TMA producer
+    auto wait_tma = [](uint64_t* bar, uint32_t ph) { return mbar_wait_t<kWaitSleep>(bar, ph); };
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(&sm.q_full, 4 * CHUNK);
+      for (int t = 0; t < 2; t++)
+        for (int c = 0; c < 2; c++)
+          tma_load_3d(sm.q[t] + c * CHUNK, &tmQ, &sm.q_full, h * HD + c * 64, q0 + t * TILE, b);
+      bool ok = true;
+      uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!wait_tma(&sm.k_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.k_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++) tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, j * TILE, b);
+        kpend |= 1u << s;
+        kph = (kph & ~(1u << s)) | (ph << s);
+        if (!wait_tma(&sm.v_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.v_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++) tma_load_3d(sm.v[s] + c * CHUNK, &tmV, &sm.v_full[s], hk * HD + c * 64, j * TILE, b);
+        vpend |= 1u << s;
+        vph = (vph & ~(1u << s)) | (ph << s);
+      }
+      if (!ok) {  // unwinding: every issued load must land before the CTA exits
+        spin_drain(&sm.q_full, 0);
+        for (int s = 0; s < KV_STAGES; s++) {
+          if (kpend >> s & 1) spin_drain(&sm.k_full[s], (kph >> s) & 1);
+          if (vpend >> s & 1) spin_drain(&sm.v_full[s], (vph >> s) & 1);
+        }
+      }
+    }
+  } else if (warp == 16) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idS = umma_idesc_bf16_f32(TILE, TILE);
+      constexpr uint32_t idO = umma_idesc_bf16_f32(TILE, HD, false, true);  // V is MN-major
+      bool ok = mbar_wait(&sm.q_full, 0);
+      auto issue_S = [&](int t, int s) {
+        const uint64_t dq = umma_desc_kmajor_sw128(smem_u32(sm.q[t]));
+        const uint64_t dk = umma_desc_kmajor_sw128(smem_u32(sm.k[s]));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+          const uint32_t off = ((kk >> 2) * CHUNK + (kk & 3) * 32) >> 4;
+          umma_bf16_ss(tbase + t * 128, dq + off, dk + off, idS, kk > 0);
+        }
+        umma_commit(&sm.s_full[t]);
+      };
+      // O += P V over keys [16*k0, 16*k1): P of keys 0-63 in S columns 0-31, of keys 64-127 in 64-95
+      auto issue_PV_part = [&](int t, int s, int j, int k0, int k1) {
+        const uint64_t dv = umma_desc_mnmajor_sw128(smem_u32(sm.v[s]), CHUNK);
+#pragma unroll
+        for (int kk = k0; kk < k1; kk++)
+          umma_bf16_ts(tbase + 256 + t * 128, tbase + t * 128 + kk * 8 + (kk >= 4 ? 32 : 0),
+                       dv + ((kk * 16 * 128) >> 4), idO, (j | kk) != 0);
+      };
+      auto issue_PV = [&](int t, int s, int j) -> bool {
+        if (!mbar_wait(&sm.p_lo[t], j & 1)) return false;
+        tc_fence_after();
+        issue_PV_part(t, s, j, 0, TILE / 32);
+        if (!mbar_wait(&sm.p_hi[t], j & 1)) return false;
+        tc_fence_after();
+        issue_PV_part(t, s, j, TILE / 32, TILE / 16);
+        umma_commit(&sm.o_done[t]);
+        return true;
+      };
+      if (ok && n_kv > 0) {
+        ok = mbar_wait(&sm.k_full[0], 0);
+        if (ok) {
+          tc_fence_after();
+          issue_S(0, 0);
+          if (has_b) issue_S(1, 0);
+          umma_commit(&sm.k_empty[0]);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; j++) {
+        const int s = j % KV_STAGES, s1 = (j + 1) % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1, ph1 = ((j + 1) / KV_STAGES) & 1;
+        const bool more = j + 1 < n_kv;
+        if (!mbar_wait(&sm.v_full[s], ph)) {
+          ok = false;
+          break;
+        }
+        if (!issue_PV(0, s, j)) {
+          ok = false;
+          break;
+        }
+        if (more) {
+          if (!mbar_wait(&sm.k_full[s1], ph1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_S(0, s1);
+        }
+        if (has_b) {
+          if (!issue_PV(1, s, j)) {
+            ok = false;
+            break;
+          }
+          if (more) issue_S(1, s1);
+        }
+        umma_commit(&sm.v_empty[s]);
+        if (more) umma_commit(&sm.k_empty[s1]);
+      }
+      if (!ok) {
+        umma_commit(&sm.drain);
+        spin_drain(&sm.drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int t = warp >> 3;            // tile
+    const int half = (warp >> 2) & 1;   // key half of the S row (and column half of O)
+    const int quad = warp & 3;          // TMEM lane quadrant
+    const int r = quad * 32 + lane;     // row in tile
+    const int qpos = q0 + t * TILE + r;
+    uint64_t* xbar = &sm.xbar[t][quad];  // exchange barrier shared with the other half's warp
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tbase + t * 128 + lane_off;
+    const uint32_t tO = tbase + 256 + t * 128 + lane_off;
+    const bool active = (t == 0) || has_b;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; active && j < n_kv; j++) {
+      const int kbase = j * TILE + half * 64;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool masked = (kbase + 64 > a.Sk) || (a.causal && kbase + 64 > q0 + t * TILE);
+      uint32_t v[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; c++) tmem_ld_32x32b_x32(tS + half * 64 + c * 32, v[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 2; c++) reg_fence32(v[c]);
+      if (masked) {
+        const int lim = min(a.Sk, a.causal ? qpos + 1 : a.Sk) - kbase;  // keys [kbase, kbase+lim) visible
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+#pragma unroll
+          for (int e = 0; e < 32; e++)
+            if (c * 32 + e >= lim) v[c][e] = 0xff800000u;
+      }
+      float mx;
+      {
+        float m0 = __uint_as_float(v[0][0]), m1 = __uint_as_float(v[0][1]);
+        float m2 = __uint_as_float(v[1][0]), m3 = __uint_as_float(v[1][1]);
+#pragma unroll
+        for (int e = 2; e < 32; e += 4) {
+          m0 = max3(m0, __uint_as_float(v[0][e]), __uint_as_float(v[0][e + 1]));
+          m1 = max3(m1, __uint_as_float(v[0][e + 2]), __uint_as_float(v[0][e + 3]));
+          m2 = max3(m2, __uint_as_float(v[1][e]), __uint_as_float(v[1][e + 1]));
+          m3 = max3(m3, __uint_as_float(v[1][e + 2]), __uint_as_float(v[1][e + 3]));
+        }
+        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+      }
+      // both halves of the row see the same full-row max
+      sm.xmax[j & 1][t][half][r] = mx;
+      if (!pair_exchange(xbar, j & 1)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, sm.xmax[j & 1][t][half ^ 1][r]) * a.scale_log2;
+      const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
+      const bool rescale = __any_sync(0xffffffffu, need);  // same rows in both warps: same decision
+      float alpha = 1.f;
+      if (rescale) {
+        const float m_new = fmaxf(m, mx);
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+        l *= alpha;
+        m = m_new;
+        if (j > 0) {
+          // this half's 64 columns of O, once PV(j-1) completed (its commit precedes S(j)'s)
+          if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int oc = 0; oc < 4; oc++) {
+            uint32_t o[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3]), "=r"(o[4]), "=r"(o[5]), "=r"(o[6]), "=r"(o[7]),
+                  "=r"(o[8]), "=r"(o[9]), "=r"(o[10]), "=r"(o[11]), "=r"(o[12]), "=r"(o[13]), "=r"(o[14]),
+                  "=r"(o[15])
+                : "r"(tO + half * 64 + oc * 16));
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x16(tO + half * 64 + oc * 16, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      if (half == 1) {  // O (this half) is ready for PV over keys 0-63
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_lo[t]);
+      }
+      const float msub = (m == -INFINITY) ? 0.f : m;
+      unsigned long long rsc[4] = {0ull, 0ull, 0ull, 0ull};
+      const unsigned long long scale2 = f2pack(a.scale_log2, a.scale_log2);
+      const unsigned long long negm2 = f2pack(-msub, -msub);
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const unsigned long long x2 =
+              fma2(f2pack(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), scale2, negm2);
+          float x0, x1;
+          f2unpack(x2, x0, x1);
+          float p0, p1;
+          if (emu_pair<EMU>(i)) {
+            p0 = exp2_fma(x0);
+            p1 = exp2_fma(x1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          rsc[i & 3] = add2(rsc[i & 3], f2pack(p0, p1));
+          v[c][i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16_lo(tS + half * 64 + c * 16, v[c]);
+      }
+      {
+        float a0, a1, b0, b1;
+        f2unpack(add2(rsc[0], rsc[1]), a0, a1);
+        f2unpack(add2(rsc[2], rsc[3]), b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(half == 0 ? &sm.p_lo[t] : &sm.p_hi[t]);
+    }
+    // epilogue: the row sum is the two halves' sums; each half writes its 64 output columns
+    if (active && ok) {
+      sm.lsum[t][half][r] = l;
+      ok = pair_exchange(xbar, n_kv & 1);
+      l += sm.lsum[t][half ^ 1][r];
+    }
+    if (active && ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (n_kv - 1) & 1))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD + half * 64;
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tO + half * 64 + c * 32, v);
+        tmem_ld_wait();
+        if (qpos < a.Sq) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[u * 8 + 0]) * inv, __uint_as_float(v[u * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[u * 8 + 2]) * inv, __uint_as_float(v[u * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[u * 8 + 4]) * inv, __uint_as_float(v[u * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[u * 8 + 6]) * inv, __uint_as_float(v[u * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(out + c * 32 + u * 8) = w;
+          }
+        }
+      }
+    } else if (active && n_kv == 0 && qpos < a.Sq) {
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD + half * 64;
+      for (int d = 0; d < 64; d++) out[d] = __float2bfloat16(0.f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 16) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 bool make_tmap_3d(CUtensorMap* map, const void* base, int H, int S, int B, long long row_stride,
                   long long batch_stride) {
   // dims (inner->outer): head*dim columns, sequence rows, batch; box 64 x 128 x 1, 128-byte swizzle
@@ -1076,6 +1445,20 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
       return cudaGetLastError();
     };
     return p.diag_mode == 200 ? go1(attn1_fwd_kernel<0>) : go1(attn1_fwd_kernel<1>);
+  }
+  if (p.diag_mode >= 300 && p.diag_mode <= 302) {  // split-row variant (see attn2x_fwd_kernel)
+    a.diag = 0;
+    const int smem2 = (int)sizeof(Smem2x) + 1024;
+    const long long grid2 = (long long)a.n_qblocks * p.Hq * p.B;
+    if (grid2 > 0x7fffffff) return cudaErrorInvalidValue;
+    auto go2 = [&](auto kern) -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
+      if (e != cudaSuccess) return e;
+      kern<<<(int)grid2, NTHREADS2X, smem2, stream>>>(tq, tk, tv, a);
+      return cudaGetLastError();
+    };
+    return p.diag_mode == 300 ? go2(attn2x_fwd_kernel<0>)
+                              : (p.diag_mode == 301 ? go2(attn2x_fwd_kernel<1>) : go2(attn2x_fwd_kernel<2>));
   }
   const int smem = (int)sizeof(SmemBase) + 1024;
   const long long grid = (long long)a.n_qblocks * p.Hq * p.B;

@@ -226,6 +226,25 @@ def test_attention_one_tile_kernel(mode, B, Sq, Sk, H, Hk, causal):
     assert rel_err(o, ops.attention(q, k, v, causal=causal)) < 1e-2
 
 
+@pytest.mark.parametrize("mode", [300, 301, 302])
+@pytest.mark.parametrize("B,Sq,Sk,H,Hk,causal", [(1, 128, 128, 1, 1, False), (2, 300, 300, 4, 4, False),
+                                                 (1, 384, 1000, 8, 2, False), (2, 500, 500, 4, 4, True),
+                                                 (1, 1024, 2048, 2, 1, False)])
+def test_attention_split_row_kernel(mode, B, Sq, Sk, H, Hk, causal):
+    """The split-row kernel (two warps per query row, ``_diag_mode`` 300-302) against the fp32
+    reference and the default kernel; keys with growing scale exercise the rescale path."""
+    torch.manual_seed(11)
+    q = torch.randn(B, Sq, H, 128, device=DEV).bfloat16()
+    k = (torch.randn(B, Sk, Hk, 128, device=DEV) * torch.linspace(0.2, 3, Sk, device=DEV)[None, :, None, None]
+         ).bfloat16()
+    v = torch.randn(B, Sk, Hk, 128, device=DEV).bfloat16()
+    o = ops.attention(q, k, v, causal=causal, _diag_mode=mode)
+    torch.cuda.synchronize()
+    assert native.device_error(reset=True) == 0
+    assert rel_err(o, _attn_ref(q, k, v, causal=causal)) < 2e-2
+    assert rel_err(o, ops.attention(q, k, v, causal=causal)) < 1e-2
+
+
 @pytest.mark.parametrize("M,N,K", [(512, 256, 64), (1000, 768, 512), (4096, 5120, 5120), (777, 384, 1024)])
 def test_gemm_pair_kernel(M, N, K):
     """2-SM (cta_group::2, 256x256 tiles) kernel, forced."""
