@@ -113,8 +113,8 @@ class LlamaLayer(nn.Module):
             kc, vc = cache
             kc[:, pos:pos + S].copy_(kv_)
             vc[:, pos:pos + S].copy_(vv)
-            if S == 1:  # decode: one query per sequence over every cached key
-                o = ops.attention(qv, kc[:, :pos + 1], vc[:, :pos + 1], causal=False)
+            if S == 1:  # decode: one query per sequence over the cached keys [0, pos]
+                o = ops.decode_attention(qv, kc, vc, pos + 1)
             else:
                 o = ops.attention(qv, kv_, vv, causal=True)
         ops.linear(o.reshape(B * S, -1), self.wo, None, epi="res", residual=x, out=x)

@@ -88,12 +88,18 @@ class MixtralLayer(nn.Module):
         out.copy_(acc.to(out.dtype))
         return out
 
-    def forward(self, x, B, S, rope, impl: str = "fused", ep=None):
+    def forward(self, x, B, S, rope, impl: str = "fused", ep=None, cache=None, pos: int = 0):
+        """``cache`` = (k_cache, v_cache) of this layer: prefill (``pos == 0``) fills positions
+        [0, S); a decode step (S == 1) appends position ``pos`` and attends over [0, pos] with the
+        split-KV decode kernel (native path only)."""
         from flextensor_b200 import ops
         from flextensor_b200.parallel.ep import NcclExpertParallel, route_topk
 
         cfg = self.cfg
-        x = self.attn.attention_fused(x, B, S, rope) if impl == "fused" else self.attn.attention_torch(x, B, S, rope)
+        if impl == "fused":
+            x = self.attn.attention_fused(x, B, S, rope, cache, pos)
+        else:
+            x = self.attn.attention_torch(x, B, S, rope)
         h = ops.rmsnorm(x, self.ffn_norm, eps=cfg.eps) if impl == "fused" else _rms_torch(x, self.ffn_norm, cfg.eps)
         ids, wts = route_topk(h, self.router, cfg.topk)
         if ep is None:
@@ -137,6 +143,53 @@ class MixtralModel(nn.Module):
         x = self.hidden(tokens, ep)
         h = _rms_torch(x.view(B, S, -1)[:, -1], self.norm, self.cfg.eps)
         return F.linear(h, self.lm_head)
+
+    # ---------------------------------------------------------------- KV-cache generation
+    def new_cache(self, batch: int, max_len: int, device=None, dtype=torch.bfloat16):
+        cfg = self.cfg
+        dev = device or self.lm_head.device
+        return [(torch.empty(batch, max_len, cfg.n_kv_heads, cfg.head_dim, device=dev, dtype=dtype),
+                 torch.empty(batch, max_len, cfg.n_kv_heads, cfg.head_dim, device=dev, dtype=dtype))
+                for _ in self.layers]
+
+    def _logits(self, h_last):
+        return F.linear(_rms_torch(h_last, self.norm, self.cfg.eps), self.lm_head)
+
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor, cache, ep=None) -> torch.Tensor:
+        """Run the prompts (native path), fill the cache, return last-position logits."""
+        B, S = tokens.shape
+        x = self.embed(tokens).reshape(B * S, -1).contiguous()
+        cos, sin = self.rope(cache[0][0].shape[1], x.device)
+        rope_s = (cos[:S], sin[:S])
+        for layer, c in zip(self.layers, cache):
+            x = layer(x, B, S, rope_s, self.impl, ep=ep, cache=c, pos=0)
+        return self._logits(x.view(B, S, -1)[:, -1])
+
+    @torch.no_grad()
+    def decode_step(self, token: torch.Tensor, cache, pos: int, ep=None) -> torch.Tensor:
+        """One new token per sequence at position ``pos``; returns its logits ``[B, vocab]``."""
+        B = token.shape[0]
+        x = self.embed(token.view(B)).contiguous()
+        cos, sin = self.rope(cache[0][0].shape[1], x.device)
+        rope_p = (cos[pos:pos + 1].contiguous(), sin[pos:pos + 1].contiguous())
+        for layer, c in zip(self.layers, cache):
+            x = layer(x, B, 1, rope_p, self.impl, ep=ep, cache=c, pos=pos)
+        return self._logits(x)
+
+    @torch.no_grad()
+    def generate(self, tokens: torch.Tensor, max_new: int, ep=None) -> torch.Tensor:
+        """Greedy continuation ``[B, max_new]`` with a KV cache."""
+        B, S = tokens.shape
+        cache = self.new_cache(B, S + max_new, tokens.device)
+        logits = self.prefill(tokens, cache, ep)
+        out = []
+        for i in range(max_new):
+            nxt = logits.argmax(-1)
+            out.append(nxt)
+            if i + 1 < max_new:
+                logits = self.decode_step(nxt, cache, S + i, ep)
+        return torch.stack(out, dim=1)
 
 
 @torch.no_grad()

@@ -115,6 +115,32 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float
     return out
 
 
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: int | torch.Tensor, *,
+                     max_len: int | None = None, scale: float | None = None, out: torch.Tensor | None = None,
+                     n_split: int = 0) -> torch.Tensor:
+    """One decode step of attention: ``q [B, Hq, 128]`` (or ``[B, 1, Hq, 128]``), one query per
+    sequence, over the KV cache ``k_cache`` / ``v_cache [B, L, Hk, 128]`` (GQA when Hk < Hq).
+    ``kv_len``: keys per sequence, an int (every sequence) or an int32 CUDA tensor ``[B]`` (then
+    ``max_len`` bounds it, default L). Keys are split over CTAs and the splits merged in a second
+    pass (``n_split``: 0 = about two CTAs per SM)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    if isinstance(kv_len, torch.Tensor):
+        seqlens, n = kv_len, 0
+        ml = int(max_len) if max_len is not None else int(k_cache.shape[1])
+    else:
+        seqlens, n = None, int(kv_len)
+        ml = n
+    if n_split <= 0:
+        sms = torch.cuda.get_device_properties(q.device).multi_processor_count
+        n_split = native.lib().decode_splits(int(k_cache.shape[0]), int(k_cache.shape[2]), ml, sms)
+    native.lib().decode_attention(q, k_cache, v_cache, out, seqlens, n, ml, float(scale), int(n_split))
+    _count(1 if n_split == 1 else 2)  # the split kernel, plus the combine pass when split
+    return out
+
+
 def attention_cp(q: torch.Tensor, kv_local: torch.Tensor, *, peer_kv: list[int], flags_ptr: int, flag_stride: int,
                  peer_acks: list[int], rank: int, shard_rows: int, epoch: int, counters: torch.Tensor,
                  scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -25,6 +25,7 @@ SOURCES = [
     "p2p.cu",
     "tp_sm100.cu",
     "moe_sm100.cu",
+    "decode_sm100.cu",
 ]
 
 CUDA_FLAGS = [

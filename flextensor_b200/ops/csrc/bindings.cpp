@@ -212,6 +212,62 @@ void attention(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& o, dou
 
 // Context-parallel attention: q [B, Sq, Hq, 128] local queries, o like q; kv_local is this
 // rank's [B, 2, Sk, Hk, 128] K/V buffer (own rows written and published before the call).
+// q [B, Hq, 128] (or [B, 1, Hq, 128]), caches [B, L, Hk, 128] with packed heads; keys [0, len_b).
+void decode_attention(const Tensor& q, const Tensor& kc, const Tensor& vc, Tensor& o,
+                      const c10::optional<Tensor>& seqlens, int64_t kv_len, int64_t max_len, double scale,
+                      int64_t n_split) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && o.scalar_type() == at::kBFloat16,
+              "decode attention: bf16 CUDA q / out");
+  TORCH_CHECK(kc.is_cuda() && vc.is_cuda() && kc.scalar_type() == at::kBFloat16 && vc.scalar_type() == at::kBFloat16 &&
+                  kc.dim() == 4 && vc.dim() == 4 && kc.sizes() == vc.sizes(),
+              "decode attention: k/v caches must be bf16 CUDA [B, L, Hk, 128] of one shape");
+  const int64_t B = kc.size(0), L = kc.size(1), Hk = kc.size(2);
+  TORCH_CHECK(kc.size(3) == 128 && kc.stride(3) == 1 && kc.stride(2) == 128 && vc.stride(3) == 1 && vc.stride(2) == 128,
+              "caches: head_dim 128, contiguous, heads packed");
+  const Tensor q3 = q.dim() == 4 ? q.squeeze(1) : q;
+  const Tensor o3 = o.dim() == 4 ? o.squeeze(1) : o;
+  TORCH_CHECK(q3.dim() == 3 && q3.size(0) == B && q3.size(2) == 128 && q3.stride(2) == 1 && q3.stride(1) == 128,
+              "q must be [B, Hq, 128] with packed heads");
+  TORCH_CHECK(o3.sizes() == q3.sizes() && o3.stride(2) == 1 && o3.stride(1) == 128, "out must match q");
+  const int64_t Hq = q3.size(1);
+  TORCH_CHECK(Hq % Hk == 0, "query heads must be a multiple of kv heads");
+  TORCH_CHECK(max_len >= 0 && max_len <= L && kv_len >= 0 && kv_len <= L, "lengths must lie in [0, L]");
+  c10::cuda::CUDAGuard g(q.device());
+  ft::DecodeProblem p;
+  p.B = (int)B;
+  p.Hq = (int)Hq;
+  p.Hk = (int)Hk;
+  p.L = (int)L;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q3.data_ptr());
+  p.q_b = q3.stride(0);
+  p.k = reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr());
+  p.k_tok = kc.stride(1);
+  p.k_batch = kc.stride(0);
+  p.v_tok = vc.stride(1);
+  p.v_batch = vc.stride(0);
+  p.o = reinterpret_cast<__nv_bfloat16*>(o3.data_ptr());
+  p.o_b = o3.stride(0);
+  if (seqlens && seqlens->defined()) {
+    TORCH_CHECK(seqlens->is_cuda() && seqlens->scalar_type() == at::kInt && seqlens->numel() == B &&
+                    seqlens->is_contiguous(),
+                "seqlens: int32 CUDA tensor with one length per sequence");
+    p.seqlens = seqlens->data_ptr<int>();
+  }
+  p.kv_len = (int)kv_len;
+  p.max_len = (int)(p.seqlens ? max_len : kv_len);
+  p.scale = (float)scale;
+  p.n_split = n_split > 0 ? (int)n_split : ft::decode_splits(p.B, p.Hk, p.max_len, num_sms_for(q.get_device()));
+  Tensor scratch;
+  if (p.n_split > 1) {
+    scratch = at::empty({(int64_t)ft::decode_scratch_floats(p.B, p.Hq, p.n_split)},
+                        q.options().dtype(at::kFloat));
+    p.scratch = scratch.data_ptr<float>();
+  }
+  const cudaError_t e = ft::decode_attention(p, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(e == cudaSuccess, "decode_attention: ", cudaGetErrorString(e));
+}
+
 void attention_cp(const Tensor& q, const Tensor& kv_local, Tensor& o, double scale, std::vector<uint64_t> peer_kv,
                   uint64_t flags, int64_t flag_stride, std::vector<uint64_t> peer_acks, int64_t rank,
                   int64_t shard_rows, uint64_t epoch, Tensor& counters) {
@@ -571,7 +627,8 @@ int device_error(bool reset) {
   int p = ft::p2p_device_error(reset);
   int t = ft::tp_device_error(reset);
   int m = ft::moe_device_error(reset);
-  return e ? e : (n ? n : (a ? a : (p ? p : (t ? t : m))));
+  int d = ft::decode_device_error(reset);
+  return e ? e : (n ? n : (a ? a : (p ? p : (t ? t : (m ? m : d)))));
 }
 
 struct PyEngine {
@@ -662,6 +719,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("device_error", &device_error, py::arg("reset") = false);
   m.def("p2p_gather_raw", &p2p_gather_raw);
   m.def("attention_cp", &attention_cp);
+  m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("out"),
+        py::arg("seqlens"), py::arg("kv_len"), py::arg("max_len"), py::arg("scale"), py::arg("n_split") = 0);
+  m.def("decode_splits", [](int B, int Hk, int max_len, int num_sms) { return ft::decode_splits(B, Hk, max_len, num_sms); });
   m.def("p2p_publish_raw", &p2p_publish_raw);
   m.def("tp_ag_gemm", &tp_ag_gemm, py::arg("a_full"), py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("epi"),
         py::arg("peer_a"), py::arg("flags"), py::arg("flag_stride"), py::arg("peer_acks"), py::arg("rank"),

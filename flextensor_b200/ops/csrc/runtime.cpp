@@ -81,6 +81,21 @@ bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_4d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3,
+                       uint64_t s1, uint64_t s2, uint64_t s3, int b0, int b1, int b2, int b3) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((s1 * 2) & 15) || ((s2 * 2) & 15) || ((s3 * 2) & 15)) return false;
+  cuuint64_t dims[4] = {d0, d1, d2, d3};
+  cuuint64_t strides[3] = {s1 * 2, s2 * 2, s3 * 2};
+  cuuint32_t box[4] = {(cuuint32_t)b0, (cuuint32_t)b1, (cuuint32_t)b2, (cuuint32_t)b3};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, b0 * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------------ host registration
 void host_register(void* ptr, size_t bytes) {
   cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
