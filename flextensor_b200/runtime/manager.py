@@ -139,6 +139,9 @@ class OffloadManager:
         self._pending_state: TensorManagerState | None = None
         self._compile_fn = None
         self._compiled: dict[str, Callable] = {}
+        from flextensor_b200.runtime.compiled import CompiledOffload
+
+        self._compiled_offload = CompiledOffload(self)
         self._skip_discovery_honored: bool | None = None
         self._manual_blocks = False
         self._replan_status = StrategyReplanStatus()
@@ -200,10 +203,11 @@ class OffloadManager:
         if self.phase == OffloadPhase.INFERENCE:
             return 0
         prof = max(1, self.config.profiling_iters)
+        warm = self._compiled_offload.extra_forwards_before_inference()
         if self.phase == OffloadPhase.PROFILING:
-            return max(0, prof - self._profile_iter())
+            return max(0, prof - self._profile_iter()) + warm
         disc = 0 if self._skip_discovery_honored else self.config.discovery_iters
-        return disc + prof
+        return disc + prof + warm
 
     def _profile_iter(self) -> int:
         return self.iteration - (0 if self._skip_discovery_honored else self.config.discovery_iters)
@@ -263,6 +267,7 @@ class OffloadManager:
             self._tm.join_after_forward()
         if not self._manual_update_state:
             self.update_state()
+        self._compiled_offload.on_forward_end()
         if self._tail is not None and self.phase == OffloadPhase.INFERENCE:
             self._advance_tail()
         return None
@@ -309,6 +314,7 @@ class OffloadManager:
         if self.model is not None and self.model is not model:
             raise RuntimeError(f"manager {self.name!r} already manages another model; release() it first")
         self._compile_fn = compile_fn
+        self._compiled_offload.resolve(c, compile_fn)
         if not c.enabled:
             dev = torch.device("cuda", c.gpu_device) if torch.cuda.is_available() else torch.device("cpu")
             self.model = model.to(dev)
@@ -409,6 +415,7 @@ class OffloadManager:
     def _to_profiling(self) -> None:
         self._tm.initialize_profile()
         self.phase = OffloadPhase.PROFILING
+        self._compiled_offload.on_enter_profiling()
 
     def _enter_inference(self) -> None:
         self.phase = OffloadPhase.INFERENCE
@@ -416,10 +423,7 @@ class OffloadManager:
             from flextensor_b200.runtime import custom_ops
 
             self._carrier = custom_ops.carrier_for(self._tm.device)
-        if self._compile_fn is not None:
-            for u in self.units:
-                core = _UnitCore(self._orig_forwards[u.label])
-                self._compiled[u.label] = self._compile_fn(core)
+        self._compiled_offload.on_enter_inference()
         self._dump_instrumentation()
 
     def _dump_instrumentation(self) -> None:
@@ -589,6 +593,7 @@ class OffloadManager:
                 tm.release_memory()
                 tm.shutdown(preserve_model=preserve_model)
         finally:
+            self._compiled_offload.teardown()
             self._unpatch()
             self.phase = OffloadPhase.NOT_INITIALIZED
             self.iteration = 0
