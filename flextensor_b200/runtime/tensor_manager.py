@@ -315,8 +315,28 @@ class TensorManager:
         if self.profile_mode == "view":
             need = max((self._trap_bytes(l) for l in self.labels), default=0)
             self._staging = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+        elif self.profile_mode == "getter":
+            from flextensor_b200.runtime.getter_profile import GetterProfile
+
+            self._getter = GetterProfile(self)
+            self._getter.install()
         self.phase = TMPhase.PROFILING
         return self.model
+
+    def promote_resident(self, tid: int) -> None:
+        """Keep tensor ``tid`` on the device for good (read outside its own trap)."""
+        with torch.no_grad():
+            self._to_device(tid)
+        for label in list(self.unit_tids):
+            if tid in self.unit_tids[label]:
+                self.unit_tids[label].remove(tid)
+        self.owner.pop(tid, None)
+
+    def _drop_getters(self) -> None:
+        g = getattr(self, "_getter", None)
+        if g is not None:
+            g.uninstall()
+            self._getter = None
 
     def _offloadable(self, label: str) -> list[int]:
         return [t for t in self.unit_tids.get(label, []) if t in self.host]
@@ -399,8 +419,11 @@ class TensorManager:
     def _profile_trap(self, label: str):
         tids = self._offloadable(label)
         cuda = self.device.type == "cuda"
+        getter = getattr(self, "_getter", None)
         with torch.no_grad():
-            if self.profile_mode == "view" and self._staging is not None:
+            if getter is not None:
+                getter.load(tids)  # served by the module's property getters; Parameters untouched
+            elif self.profile_mode == "view" and self._staging is not None:
                 from flextensor_b200.core.host_store import packed_layout
 
                 offs, _ = packed_layout([tensor_nbytes(self.host[t]) for t in tids])
@@ -426,8 +449,11 @@ class TensorManager:
                 ms = start.elapsed_time(end)
             else:
                 ms = (time.perf_counter() - t0) * 1e3
-            for t in tids:
-                self.params_by_tid[t].data = self.host[t]
+            if getter is not None:
+                getter.unload(tids)
+            else:
+                for t in tids:
+                    self.params_by_tid[t].data = self.host[t]
             if not self.is_profiling_suspended():
                 self.collector.record_duration(label, ms)
 
@@ -497,6 +523,7 @@ class TensorManager:
 
     def initialize_inference(self) -> nn.Module:
         self._staging = None
+        self._drop_getters()
         rows = [r for r in self.collector.get_layer_stats() if r.label in self.unit_tids]
         from flextensor_b200.runtime.profiling_quality import report_profiling_quality
 
@@ -858,6 +885,7 @@ class TensorManager:
 
     def shutdown(self, *, preserve_model: bool = True) -> None:
         """Tear down the loader; with ``preserve_model`` every parameter ends up on the host."""
+        self._drop_getters()
         with torch.no_grad():
             if self.loader is not None:
                 if preserve_model:

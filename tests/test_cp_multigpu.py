@@ -54,12 +54,28 @@ def _worker_body(rank, world, port, q):
         want_t = m(lat, t, ctx).float()
         got_u = m(lat, t, ctx, cp=UlyssesAttention()).float()
         err_u = float((got_u - want_t).abs().max())
+        # gather-KV cross-attention: 200 replicated "audio" queries over the sequence-sharded
+        # keys / values (each rank contributes its shard; the kernel gathers the rest)
+        gk = torch.Generator(device=dev).manual_seed(9)
+        Hk = cfg.num_heads
+        k_full = torch.randn(1, tokens, Hk, 128, device=dev, generator=gk).bfloat16()
+        v_full = torch.randn(1, tokens, Hk, 128, device=dev, generator=gk).bfloat16()
+        qa = torch.randn(1, 200, Hk, 128, device=dev, generator=gk).bfloat16()
+        sh = tokens // world
+        rows = slice(rank * sh, (rank + 1) * sh)
+        errs_g = []
+        for _ in range(2):
+            og = cp.gather_kv_attention(qa, k_full[0, rows], v_full[0, rows]).float()
+            ref = torch.nn.functional.scaled_dot_product_attention(
+                qa.float().transpose(1, 2), k_full.float().transpose(1, 2), v_full.float().transpose(1, 2)
+            ).transpose(1, 2)
+            errs_g.append(float((og - ref).abs().max()))
     torch.cuda.synchronize()
     err_word = native.device_error(reset=True)
     cp.close()
     dist.barrier()
     dist.destroy_process_group()
-    q.put((rank, max(errs), err_u, err_word, float(want.abs().max())))
+    q.put((rank, max(errs), err_u, err_word, float(want.abs().max()), max(errs_g)))
 
 
 def _worker(rank, world, port, q):
@@ -86,7 +102,8 @@ def test_cp_dit_two_ranks():
         assert r[1] != "error", f"rank {r[0]} failed:\n{r[2]}"
     for p in ps:
         p.join(60)
-    for rank, err, err_u, word, scale in res:
+    for rank, err, err_u, word, scale, err_g in res:
         assert word == 0, f"rank {rank}: device error word {word}"
+        assert err_g < 2e-2, f"rank {rank}: gather-KV cross-attention max abs err {err_g}"
         assert err < 0.03 * max(1.0, scale), f"rank {rank}: fused CP max abs err {err} (output scale {scale})"
         assert err_u < 0.03 * max(1.0, scale), f"rank {rank}: Ulysses max abs err {err_u}"

@@ -182,3 +182,34 @@ def test_offload_keeps_quantized_weight_metadata():
             assert torch.allclose(mm(x), ref)
     assert net.q1.weight.output_dim == 0 and net.q1.weight.weight_scale.shape == (8, 1)
     ft.get_offload_manager().release()
+
+
+def test_getter_profile_serves_trap_copies_without_touching_parameters():
+    """profile_mode='getter': during PROFILING the modules read their weights through property
+    getters of a per-module subclass; the Parameter objects keep their host tensors (no .data
+    rebinding) and the original classes come back for INFERENCE."""
+    torch.manual_seed(3)
+    net = Net()
+    x = torch.randn(3, 8)
+    ref = net(x).detach()
+    w = net.q1.weight
+    w_data_ptr = w.data_ptr()
+    om = ft.get_offload_manager("getter")
+    mm = om.offload(net, ft.OffloadConfig(pinned_memory=False, include_patterns=["q1", "q2"], profiling_iters=2,
+                                          num_blocks=2, min_blocks=2, profile_mode="getter",
+                                          load_strategy=NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2,
+                                                                         cyclic=True)))
+    seen_classes = []
+    with torch.no_grad():
+        assert torch.allclose(mm(x), ref)  # discovery
+        assert str(om.phase).endswith("PROFILING")
+        seen_classes.append(type(net.q1))
+        assert type(net.q1) is not QuantLike and isinstance(net.q1, QuantLike)
+        assert torch.allclose(mm(x), ref)
+        assert w.data_ptr() == w_data_ptr or w.device.type == "cpu"  # the Parameter object kept its storage
+        for _ in range(3):
+            assert torch.allclose(mm(x), ref)
+    assert str(om.phase).endswith("INFERENCE")
+    assert type(net.q1) is QuantLike and type(net.q2) is QuantLike
+    assert net.q1.weight is w and w.output_dim == 0
+    om.release()
