@@ -80,6 +80,10 @@ class _ForeignReadMode(TorchFunctionMode):
                 d = self.cache.get(tid)
                 if d is None:
                     d = x.to(self.tm.device, non_blocking=True)
+                    if self.tm.use_trace_tensor:
+                        from flextensor_b200.runtime.benchmark_modes import wrap_trace_tensor
+
+                        d = wrap_trace_tensor(d, self.tm.id_to_name.get(tid))
                     self.cache[tid] = d
                 return d
         return x
@@ -167,6 +171,10 @@ class TensorManager:
         self.load_from_shm = False
         self._state_restored_from_profile = False
         self._stripe = None
+        self.use_trace_tensor = bool(_use_trace_tensor)
+        if self.use_trace_tensor and profile_mode == "view":
+            raise ValueError("profile_mode='view' is incompatible with _use_trace_tensor=True "
+                             "(view profiling rebinds parameters into a staging buffer)")
 
     # ================================================================== model / units
     def set_model(self, model: nn.Module) -> None:
@@ -322,6 +330,17 @@ class TensorManager:
             self._getter.install()
         self.phase = TMPhase.PROFILING
         return self.model
+
+    def is_traced(self, t) -> bool:
+        """Whether ``t`` is a tensor this manager manages: with ``_use_trace_tensor`` a
+        :class:`~flextensor_b200.runtime.benchmark_modes.TraceTensor` mark, otherwise one of the
+        model's offloadable parameters (by identity)."""
+        if self.use_trace_tensor:
+            from flextensor_b200.runtime.benchmark_modes import is_trace_tensor
+
+            if is_trace_tensor(t):
+                return True
+        return any(t is self.params_by_tid[tid] for tid in self.owner)
 
     def promote_resident(self, tid: int) -> None:
         """Keep tensor ``tid`` on the device for good (read outside its own trap)."""

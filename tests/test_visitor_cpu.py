@@ -213,3 +213,35 @@ def test_getter_profile_serves_trap_copies_without_touching_parameters():
     assert type(net.q1) is QuantLike and type(net.q2) is QuantLike
     assert net.q1.weight is w and w.output_dim == 0
     om.release()
+
+
+def test_trace_tensor_marks_do_not_spread():
+    from flextensor_b200.runtime.benchmark_modes import BenchmarkReplace, TraceTensor, is_trace_tensor, \
+        wrap_trace_tensor
+
+    w = wrap_trace_tensor(torch.ones(3, 3), "blk.weight")
+    assert isinstance(w, TraceTensor) and w.trace_name == "blk.weight"
+    y = w @ torch.ones(3)
+    assert not is_trace_tensor(y) and type(y) is torch.Tensor   # results are plain tensors
+    w.mul_(2.0)
+    assert is_trace_tensor(w) and float(w[0, 0]) == 2.0          # in-place keeps the mark
+    assert wrap_trace_tensor(w) is w
+    # on a CPU-only device nothing moves; the mode passes calls through and counts them
+    with BenchmarkReplace("cpu", trace=True) as m:
+        torch.add(torch.ones(2), 1)
+    assert m.calls["add"] == 1 and m.moved_bytes == 0
+
+
+def test_trace_tensor_flag_validation_and_is_traced():
+    from flextensor_b200.runtime.tensor_manager import TensorManager
+
+    strat = NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2, cyclic=True)
+    import pytest as _pt
+
+    with _pt.raises(ValueError, match="incompatible"):
+        TensorManager("cpu", strat, profile_mode="view", _use_trace_tensor=True)
+    tm = TensorManager("cpu", strat, profile_mode="getter", _use_trace_tensor=True)
+    from flextensor_b200.runtime.benchmark_modes import wrap_trace_tensor
+
+    assert tm.is_traced(wrap_trace_tensor(torch.ones(1)))
+    assert not tm.is_traced(torch.ones(1))
