@@ -108,6 +108,41 @@ def _sdpa(q, k, v):
     return o.transpose(1, 2).flatten(2)
 
 
+class Ulysses:
+    """Sequence-parallel self-attention over a process group with NCCL all-to-alls (the scheme of
+    the reference's LTX example, ``examples/ltx23/outpaint/context_parallel.py:628-686``): each
+    rank holds 1/P of the tokens; q/k/v go sequence -> heads, attention runs over the full
+    sequence on H/P heads, and the output comes back heads -> sequence."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def _a2a(self, x, scatter_dim, gather_dim):
+        import torch.distributed as dist
+
+        send = torch.stack(x.chunk(self.world, dim=scatter_dim)).contiguous()
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        return torch.cat(recv.unbind(0), dim=gather_dim)
+
+    def attention(self, q, k, v):
+        """q/k/v [B, S/P, H, Dh] -> [B, S/P, H*Dh]."""
+        qh, kh, vh = (self._a2a(t, 2, 1) for t in (q, k, v))
+        o = F.scaled_dot_product_attention(qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2))
+        return self._a2a(o.transpose(1, 2), 1, 2).flatten(2)
+
+    def gather(self, y):
+        import torch.distributed as dist
+
+        parts = [torch.empty_like(y) for _ in range(self.world)]
+        dist.all_gather(parts, y.contiguous(), group=self.group)
+        return torch.cat(parts, dim=1)
+
+
 class WanTorchBlock(nn.Module):
     def __init__(self, cfg: WanShape):
         super().__init__()
@@ -120,7 +155,7 @@ class WanTorchBlock(nn.Module):
         self.ffn_in = nn.Linear(d, cfg.ffn_dim)
         self.ffn_out = nn.Linear(cfg.ffn_dim, d)
 
-    def forward(self, x, ctx, e, cos, sin):
+    def forward(self, x, ctx, e, cos, sin, cp=None):
         cfg = self.cfg
         B, S, D = x.shape
         H, Dh = cfg.num_heads, cfg.head_dim
@@ -131,7 +166,8 @@ class WanTorchBlock(nn.Module):
         q = _rotate(a.norm_q(a.to_q(h)).view(B, S, H, Dh), cos, sin)
         k = _rotate(a.norm_k(a.to_k(h)).view(B, S, H, Dh), cos, sin)
         v = a.to_v(h).view(B, S, H, Dh)
-        x = (x.float() + a.to_out(_sdpa(q, k, v)).float() * g1).to(x.dtype)
+        o = cp.attention(q, k, v) if cp is not None else _sdpa(q, k, v)
+        x = (x.float() + a.to_out(o).float() * g1).to(x.dtype)
         a = self.attn2
         h = F.layer_norm(x.float(), (D,), self.norm2.weight.float(), self.norm2.bias.float(), cfg.eps).to(x.dtype)
         L = ctx.shape[1]
@@ -161,7 +197,9 @@ class WanTorchDiT(nn.Module):
         self.proj_out = nn.Linear(d, cfg.out_channels * pf * ph * pw)
         self._angles = {}
 
-    def forward(self, latent, timestep, context):
+    def forward(self, latent, timestep, context, cp: Ulysses | None = None):
+        """``cp``: sequence parallelism over a group -- this rank runs the blocks on its 1/P of
+        the tokens (Ulysses self-attention) and the output is all-gathered after the head."""
         cfg = self.cfg
         dt = self.patch_embedding.weight.dtype
         B, C, Fr, Hh, Ww = latent.shape
@@ -169,6 +207,13 @@ class WanTorchDiT(nn.Module):
         grid = (Fr // pf, Hh // ph, Ww // pw)
         x = latent.to(dt).view(B, C, grid[0], pf, grid[1], ph, grid[2], pw)
         x = x.permute(0, 2, 4, 6, 1, 3, 5, 7).reshape(B, -1, C * pf * ph * pw)
+        rows = None
+        if cp is not None:
+            shard = x.shape[1] // cp.world
+            if shard * cp.world != x.shape[1]:
+                raise ValueError(f"{x.shape[1]} tokens do not split over {cp.world} ranks")
+            rows = slice(cp.rank * shard, (cp.rank + 1) * shard)
+            x = x[:, rows].contiguous()
         x = self.patch_embedding(x)
         t = _timestep_features(timestep, cfg.freq_dim).to(dt)
         temb = self.time_embedding_2(F.silu(self.time_embedding_1(t)))
@@ -178,11 +223,15 @@ class WanTorchDiT(nn.Module):
         if key not in self._angles:
             self._angles[key] = _rope_angles(grid, cfg.head_dim, x.device)
         cos, sin = self._angles[key]
+        if rows is not None:
+            cos, sin = cos[rows].contiguous(), sin[rows].contiguous()
         for blk in self.blocks:
-            x = blk(x, ctx, e, cos, sin)
+            x = blk(x, ctx, e, cos, sin, cp) if cp is not None else blk(x, ctx, e, cos, sin)
         mod = self.head_scale_shift.float() + temb.float()[:, None]
         h = (F.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps) * (1 + mod[:, 1:2]) + mod[:, 0:1]).to(dt)
         y = self.proj_out(h)
+        if cp is not None:
+            y = cp.gather(y)
         C = cfg.out_channels
         y = y.view(B, grid[0], grid[1], grid[2], C, pf, ph, pw).permute(0, 4, 1, 5, 2, 6, 3, 7)
         return y.reshape(B, C, grid[0] * pf, grid[1] * ph, grid[2] * pw)

@@ -92,3 +92,46 @@ def test_reference_arm_imports_nothing_of_ours():
     r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
+
+
+def _ulysses_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    from wan_torch import Ulysses, WanShape, WanTorchDiT, init_params_
+
+    torch.manual_seed(0)
+    cfg = WanShape(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_dim=128, text_len=16, freq_dim=64,
+                   in_channels=16, out_channels=16, patch=(1, 1, 1))
+    m = WanTorchDiT(cfg)
+    init_params_(m, seed=2)
+    lat = torch.randn(1, 16, 2, 4, 4, generator=torch.Generator().manual_seed(3))
+    ctx = torch.randn(1, 16, 128, generator=torch.Generator().manual_seed(4))
+    ts = torch.tensor([100.0])
+    with torch.no_grad():
+        want = m(lat, ts, ctx)
+        got = m(lat, ts, ctx, cp=Ulysses())
+    q.put((rank, float((got - want).abs().max())))
+    dist.destroy_process_group()
+
+
+def test_reference_ulysses_matches_unsharded_over_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_ulysses_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(30)
+    assert all(err < 1e-4 for _, err in res), res
