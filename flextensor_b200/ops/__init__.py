@@ -6,6 +6,7 @@ from flextensor_b200.ops.api import (
     TP_EPI,
     attention,
     attention_cp,
+    decode_attention,
     launch_count,
     layernorm_modulate,
     linear,
@@ -20,6 +21,6 @@ from flextensor_b200.ops.api import (
     tp_rmsnorm,
 )
 
-__all__ = ["EPI", "TP_EPI", "attention", "attention_cp", "launch_count", "layernorm_modulate", "linear",
+__all__ = ["EPI", "TP_EPI", "attention", "attention_cp", "decode_attention", "launch_count", "layernorm_modulate", "linear",
            "linear_swiglu", "qk_rmsnorm_rope", "rmsnorm", "rope", "tp_ag_counter_words", "tp_allgather_gemm", "tp_gemm_reducescatter",
            "tp_reduce", "tp_rmsnorm"]

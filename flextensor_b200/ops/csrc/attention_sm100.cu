@@ -1068,7 +1068,7 @@ __device__ __forceinline__ bool pair_exchange(uint64_t* bar, uint32_t parity) {
 }
 
 template <int EMU>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(NTHREADS2X, 1)
     attn2x_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -1294,32 +1294,9 @@ __global__ void __maxnreg__(112)
         alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
         l *= alpha;
         m = m_new;
-        if (j > 0) {
-          // this half's 64 columns of O, once PV(j-1) completed (its commit precedes S(j)'s)
-          if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int oc = 0; oc < 4; oc++) {
-            uint32_t o[16];
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-                "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3]), "=r"(o[4]), "=r"(o[5]), "=r"(o[6]), "=r"(o[7]),
-                  "=r"(o[8]), "=r"(o[9]), "=r"(o[10]), "=r"(o[11]), "=r"(o[12]), "=r"(o[13]), "=r"(o[14]),
-                  "=r"(o[15])
-                : "r"(tO + half * 64 + oc * 16));
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st_32x32b_x16(tO + half * 64 + oc * 16, o);
-          }
-          tmem_st_wait();
-        }
       }
-      if (half == 1) {  // O (this half) is ready for PV over keys 0-63
+      const bool o_fix = rescale && j > 0;  // O holds earlier blocks' sums: rescale it before PV(j)
+      if (half == 1 && !o_fix) {  // nothing of O to fix here: PV over keys 0-63 may start
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_lo[t]);
@@ -1355,10 +1332,31 @@ __global__ void __maxnreg__(112)
         f2unpack(add2(rsc[2], rsc[3]), b0, b1);
         l += (a0 + a1) + (b0 + b1);
       }
+      if (o_fix) {
+        // this half's 64 columns of O, once PV(j-1) completed (its commit precedes S(j)'s); the
+        // S registers are dead by now, so the O round trip adds no register pressure
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int oc = 0; oc < 2; oc++) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + half * 64 + oc * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + half * 64 + oc * 32, o);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(half == 0 ? &sm.p_lo[t] : &sm.p_hi[t]);
+      if (lane == 0) {
+        if (half == 0 || o_fix) mbar_arrive(&sm.p_lo[t]);
+        if (half == 1) mbar_arrive(&sm.p_hi[t]);
+      }
     }
     // epilogue: the row sum is the two halves' sums; each half writes its 64 output columns
     if (active && ok) {

@@ -95,7 +95,7 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 template <int G>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
     decode_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, DecArgs a) {
   constexpr int HPT = (G + 3) / 4;  // heads per thread in q K^T
   constexpr int GP = (G + 3) / 4 * 4;
