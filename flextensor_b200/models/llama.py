@@ -144,27 +144,31 @@ class LlamaLayer(nn.Module):
         return x
 
     # ---------------------------------------------------------------- tensor parallel (one rank's shard)
-    def forward_tp(self, x_local, B, S, rope, tp):
+    def forward_tp(self, x_local, B, S, rope, tp, cache=None, pos: int = 0):
+        """One rank's shard. ``cache`` = this rank's (k_cache, v_cache) ``[B, L_max, hk, 128]``:
+        prefill (``pos == 0``) stores positions [0, S); a decode step (S == 1) appends position
+        ``pos`` and attends over [0, pos] with the split-KV decode kernel."""
         from flextensor_b200 import ops
 
         cfg, D = self.cfg, self.cfg.head_dim
         qn, kn = self.hq * D, self.hk * D
         ag_fused = tp.collective in ("fused", "fused_ag")
         rs_fused = tp.collective in ("fused", "fused_rs")
+        _ag, _rs = tp.buffers(B * S)
 
         def gathered_gemm(norm_w, w, epi):
             if ag_fused:  # RMSNorm of the own rows straight into the all-gather buffer
-                ops.rmsnorm(x_local, norm_w, eps=cfg.eps, out=tp._ag.begin())
-                tp._ag.publish()
-                return tp._ag.gemm(w, epi=epi)
+                ops.rmsnorm(x_local, norm_w, eps=cfg.eps, out=_ag.begin())
+                _ag.publish()
+                return _ag.gemm(w, epi=epi)
             h = tp._nccl.all_gather(ops.rmsnorm(x_local, norm_w, eps=cfg.eps))
             return ops.linear_swiglu(h, w) if epi == "swiglu" else ops.linear(h, w, None, epi="none")
 
         def scattered_gemm(a, w):
             nonlocal x_local
             if rs_fused:
-                tp._rs.gemm(a, w)
-                tp._rs.reduce(x_local, residual=x_local)
+                _rs.gemm(a, w)
+                _rs.reduce(x_local, residual=x_local)
             else:
                 x_local += tp._nccl.reduce_scatter(ops.linear(a, w, None, epi="none"))
 
@@ -172,7 +176,15 @@ class LlamaLayer(nn.Module):
         q, k, v = qkv[:, :qn], qkv[:, qn:qn + kn], qkv[:, qn + kn:]
         ops.rope(q, *rope, D, S, out=q)
         ops.rope(k, *rope, D, S, out=k)
-        o = ops.attention(q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D), causal=True)
+        qv, kv_, vv = q.view(B, S, self.hq, D), k.view(B, S, self.hk, D), v.view(B, S, self.hk, D)
+        if cache is not None:
+            kc, vc = cache
+            kc[:, pos:pos + S].copy_(kv_)
+            vc[:, pos:pos + S].copy_(vv)
+        if cache is not None and S == 1:
+            o = ops.decode_attention(qv, cache[0], cache[1], pos + 1)
+        else:
+            o = ops.attention(qv, kv_, vv, causal=True)
         scattered_gemm(o.view(B * S, -1), self.wo)
         f = gathered_gemm(self.ffn_norm, self.w_gate_up, "swiglu")
         scattered_gemm(f, self.w_down)
@@ -180,7 +192,7 @@ class LlamaLayer(nn.Module):
 
     def forward(self, x, B, S, rope, impl="fused", tp=None, cache=None, pos: int = 0):
         if tp is not None:
-            return self.forward_tp(x, B, S, rope, tp)
+            return self.forward_tp(x, B, S, rope, tp, cache, pos)
         if cache is not None:
             return self.forward_fused(x, B, S, rope, cache, pos)
         return self.forward_fused(x, B, S, rope) if impl == "fused" else self.forward_torch(x, B, S, rope)
@@ -316,21 +328,56 @@ class LlamaTP(nn.Module):
         if collective not in ("fused", "nccl", "fused_ag", "fused_rs"):
             raise ValueError(f"unknown collective {collective!r}")
         self.collective = collective
+        self._group, self._pair = group, pair
         self._nccl = NcclTP(group)
-        if collective in ("fused", "fused_ag"):
-            self._ag = TPAllGather(tokens_total, self.cfg.dim, group, pair=pair)
-        if collective in ("fused", "fused_rs"):
-            self._rs = TPReduceScatter(tokens_total, self.cfg.dim, group, pair=pair)
+        self._by_rows: dict[int, tuple] = {}
+        self._ag, self._rs = self._make(tokens_total)
+        self._by_rows[tokens_total] = (self._ag, self._rs)
+
+    def _make(self, rows: int):
+        from flextensor_b200.parallel.tp import TPAllGather, TPReduceScatter
+
+        ag = rs = None
+        if self.collective in ("fused", "fused_ag"):
+            ag = TPAllGather(rows, self.cfg.dim, self._group, pair=self._pair)
+        if self.collective in ("fused", "fused_rs"):
+            rs = TPReduceScatter(rows, self.cfg.dim, self._group, pair=self._pair)
+        return ag, rs
+
+    def add_rows(self, tokens_total: int) -> None:
+        """Fused-collective buffers for another row count (e.g. the decode step's B rows next to
+        the prefill's B*S); every rank must call it, in the same order."""
+        if tokens_total not in self._by_rows:
+            self._by_rows[tokens_total] = self._make(tokens_total)
+
+    def buffers(self, rows: int):
+        """(all-gather, reduce-scatter) objects sized for ``rows`` token rows."""
+        if rows not in self._by_rows:
+            raise ValueError(f"no fused TP buffers for {rows} rows: call setup()/add_rows() on every rank first")
+        return self._by_rows[rows]
 
     def close(self) -> None:
-        for o in (self._ag, self._rs):
-            if o is not None:
-                o.close()
+        for ag, rs in getattr(self, "_by_rows", {}).values():
+            for o in (ag, rs):
+                if o is not None:
+                    o.close()
+        self._by_rows = {}
         self._ag = self._rs = None
 
-    def forward(self, x_local: torch.Tensor, B: int, S: int, rope) -> torch.Tensor:
+    def new_cache(self, batch: int, max_len: int, device=None, dtype=torch.bfloat16):
+        """This rank's KV cache: its ``n_kv_heads / world`` heads of every layer."""
+        D = self.cfg.head_dim
+        hk = self.cfg.n_kv_heads // self.world
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        return [(torch.empty(batch, max_len, hk, D, device=dev, dtype=dtype),
+                 torch.empty(batch, max_len, hk, D, device=dev, dtype=dtype)) for _ in self.layers]
+
+    def forward(self, x_local: torch.Tensor, B: int, S: int, rope, cache=None, pos: int = 0) -> torch.Tensor:
         """x_local ``[B*S/world, dim]`` (this rank's token rows) -> same rows after all layers.
-        Each layer is called as a module (``layers.*`` are offload units)."""
-        for L in self.layers:
-            x_local = L(x_local, B, S, rope, tp=self)
+        Each layer is called as a module (``layers.*`` are offload units). ``cache``: from
+        :meth:`new_cache` (prefill at ``pos == 0``, then one decode step per call with S == 1)."""
+        single = self.world == 1  # one rank: plain native layers, no collectives
+        for i, L in enumerate(self.layers):
+            x_local = L(x_local, B, S, rope, tp=None if single else self, cache=None if cache is None else cache[i],
+                        pos=pos)
         return x_local

@@ -159,11 +159,9 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
     const int key = tid & (KT - 1), hg = tid >> 6;      // q K^T: thread = (key, head group)
     const int hs = warp;                                // softmax: warp = head (and head + 8)
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    float acc[G][4];
+    unsigned long long acc[G][2];  // (dims 4l, 4l+1) and (4l+2, 4l+3) of every head, fp32 pairs
 #pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-      for (int e = 0; e < 4; e++) acc[g][e] = 0.f;
+    for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = 0ull;
     bool ok = true;
     for (int i = 0; i < n_tiles; i++) {
       const int s = i % DSTAGES;
@@ -249,17 +247,23 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
 #pragma unroll
         for (int g = 0; g < G; g++) {
           const float al = sm.alpha[g];
+          const unsigned long long al2 = ((unsigned long long)__float_as_uint(al) << 32) | __float_as_uint(al);
 #pragma unroll
-          for (int e = 0; e < 4; e++) acc[g][e] *= al;
+          for (int e = 0; e < 2; e++) asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(acc[g][e]) : "l"(al2));
         }
         const uint8_t* vt = sm.v[s] + (lane >> 4) * BOX_BYTES;
         const int cc = (lane & 15) >> 1, sub = (lane & 1) * 8;
+        const int nvalid = len - key0;  // keys past the length: P is 0, but their V rows may be
+                                        // uninitialised cache memory (0 * NaN = NaN), so skip them
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) {
           const int kr = warp * 8 + kk;
+          if (kr >= nvalid) break;
           const uint2 w = *reinterpret_cast<const uint2*>(vt + swz(kr, cc) + sub);
-          const float v0 = __uint_as_float(w.x << 16), v1 = __uint_as_float(w.x & 0xffff0000u);
-          const float v2 = __uint_as_float(w.y << 16), v3 = __uint_as_float(w.y & 0xffff0000u);
+          const unsigned long long v01 =
+              ((unsigned long long)(w.x & 0xffff0000u) << 32) | (unsigned long long)(w.x << 16);
+          const unsigned long long v23 =
+              ((unsigned long long)(w.y & 0xffff0000u) << 32) | (unsigned long long)(w.y << 16);
 #pragma unroll
           for (int g4 = 0; g4 < GP; g4 += 4) {
             const float4 pp = *reinterpret_cast<const float4*>(&sm.p[kr][g4]);
@@ -267,10 +271,10 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
 #pragma unroll
             for (int u = 0; u < 4; u++) {
               if (g4 + u < G) {
-                acc[g4 + u][0] = fmaf(pv[u], v0, acc[g4 + u][0]);
-                acc[g4 + u][1] = fmaf(pv[u], v1, acc[g4 + u][1]);
-                acc[g4 + u][2] = fmaf(pv[u], v2, acc[g4 + u][2]);
-                acc[g4 + u][3] = fmaf(pv[u], v3, acc[g4 + u][3]);
+                const unsigned long long p2 =
+                    ((unsigned long long)__float_as_uint(pv[u]) << 32) | __float_as_uint(pv[u]);
+                asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[g4 + u][0]) : "l"(p2), "l"(v01));
+                asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[g4 + u][1]) : "l"(p2), "l"(v23));
               }
             }
           }
@@ -286,7 +290,8 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
 #pragma unroll
     for (int g = 0; g < G; g++)
       *reinterpret_cast<float4*>(&red[(warp * G + g) * DHD + lane * 4]) =
-          make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+          make_float4(__uint_as_float((uint32_t)acc[g][0]), __uint_as_float((uint32_t)(acc[g][0] >> 32)),
+                      __uint_as_float((uint32_t)acc[g][1]), __uint_as_float((uint32_t)(acc[g][1] >> 32)));
 #pragma unroll
     for (int hh = 0; hh < 2; hh++) {
       const int g = hs + 8 * hh;

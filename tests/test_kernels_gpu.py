@@ -293,6 +293,10 @@ def test_decode_attention(B, L, Hq, Hk, n_split):
     assert rel_err(o, _decode_ref(q, kc, vc, [L] * B)) < 1e-2
     lens = torch.randint(0, L + 1, (B,), device=DEV, dtype=torch.int32)
     lens[0] = L
+    # cache rows past each length hold garbage (NaN / Inf) that must not reach the output
+    for b in range(B):
+        kc[b, int(lens[b]):] = float("nan")
+        vc[b, int(lens[b]):] = float("inf")
     o2 = ops.decode_attention(q.view(B, 1, Hq, 128), kc, vc, lens, max_len=L, n_split=n_split).view(B, Hq, 128)
     torch.cuda.synchronize()
     assert native.device_error(reset=True) == 0
