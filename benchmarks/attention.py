@@ -6,7 +6,7 @@
 100 + k = k exp2 pairs in 8 on the FMA pipe instead of MUFU, 200 / 201 = the experimental
 one-tile kernel with double-buffered S (0 / 1 exp2 pair in 8 on the FMA pipe; not yet run on a
 GPU), 300 + k = the split-row kernel (two warps per query row, k exp2 pairs in 8 on the FMA
-pipe). Each mode is timed with CUDA events
+pipe), 400 + k = P through shared memory with event-driven MMA issue. Each mode is timed with CUDA events
 (5 launches after 2 warm-ups, median of ``--reps`` repetitions, all modes in one process)
 against ``torch.nn.functional.scaled_dot_product_attention`` (cuDNN on B200). ``--trace``
 prints the clock64 timeline of CTA 0, in cycles per 128-key block (median over blocks 4..57):

@@ -1399,6 +1399,374 @@ __global__ void __launch_bounds__(NTHREADS2X, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// P-through-shared-memory variant (``_diag_mode`` 400 + EMU). The default kernel keeps P in TMEM
+// over the S columns, so QK^T of block j+1 can only be issued after P.V of block j has consumed
+// P: per tile the period is softmax + handoff + P.V + QK^T. Here each softmax warp releases S
+// as soon as the row is in registers (s_free), and writes P as a 128-byte-swizzled K-major tile
+// into shared memory; the MMA warp issues S(j+1) on s_free and P.V(j) on p_full, whichever is
+// ready first (it polls both tiles' barriers), so QK^T of the next block overlaps the softmax
+// of the current one. Shared memory: Q (2 tiles) + K and V (2 stages each) + ONE P tile shared
+// by tiles A and B in turn (224 KB): a tile's softmax writes P once the other tile's P.V that
+// last read the buffer completed (p_free_a / p_free_b, one phase per block each).
+struct SmemP : SmemBase {
+  alignas(1024) uint8_t p[2 * CHUNK];  // [128 rows x 128 keys] bf16, two 64-key swizzled chunks
+  uint64_t s_free[2], p_free[2];       // p_free[t]: P.V of tile t finished reading the P buffer
+};
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int EMU>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    attnP_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemP& sm = *reinterpret_cast<SmemP*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int qb = blockIdx.x % a.n_qblocks;
+  const int h = (blockIdx.x / a.n_qblocks) % a.Hq;
+  const int b = blockIdx.x / (a.n_qblocks * a.Hq);
+  const int hk = h / (a.Hq / a.Hk);
+  const int q0 = qb * 2 * TILE;
+  int n_kv = (a.Sk + TILE - 1) / TILE;
+  if (a.causal) n_kv = min(n_kv, (q0 + 2 * TILE + TILE - 1) / TILE);
+  const bool has_b = q0 + TILE < a.Sq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < KV_STAGES; s++) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; t++) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.s_free[t], 4);
+      mbar_init(&sm.p_full[t], 4);
+      mbar_init(&sm.o_done[t], 1);
+      mbar_init(&sm.p_free[t], 1);
+    }
+    mbar_init(&sm.drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------------ TMA producer
+    auto wait_tma = [](uint64_t* bar, uint32_t ph) { return mbar_wait_t<kWaitSleep>(bar, ph); };
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(&sm.q_full, 4 * CHUNK);
+      for (int t = 0; t < 2; t++)
+        for (int c = 0; c < 2; c++)
+          tma_load_3d(sm.q[t] + c * CHUNK, &tmQ, &sm.q_full, h * HD + c * 64, q0 + t * TILE, b);
+      bool ok = true;
+      uint32_t kpend = 0, kph = 0, vpend = 0, vph = 0;
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!wait_tma(&sm.k_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.k_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++) tma_load_3d(sm.k[s] + c * CHUNK, &tmK, &sm.k_full[s], hk * HD + c * 64, j * TILE, b);
+        kpend |= 1u << s;
+        kph = (kph & ~(1u << s)) | (ph << s);
+        if (!wait_tma(&sm.v_empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.v_full[s], 2 * CHUNK);
+        for (int c = 0; c < 2; c++) tma_load_3d(sm.v[s] + c * CHUNK, &tmV, &sm.v_full[s], hk * HD + c * 64, j * TILE, b);
+        vpend |= 1u << s;
+        vph = (vph & ~(1u << s)) | (ph << s);
+      }
+      if (!ok) {
+        spin_drain(&sm.q_full, 0);
+        for (int s = 0; s < KV_STAGES; s++) {
+          if (kpend >> s & 1) spin_drain(&sm.k_full[s], (kph >> s) & 1);
+          if (vpend >> s & 1) spin_drain(&sm.v_full[s], (vph >> s) & 1);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------ MMA issuer (event driven)
+    if (elect_one()) {
+      constexpr uint32_t idS = umma_idesc_bf16_f32(TILE, TILE);
+      constexpr uint32_t idO = umma_idesc_bf16_f32(TILE, HD, false, true);  // P K-major, V MN-major
+      bool ok = mbar_wait(&sm.q_full, 0);
+      const int nt = has_b ? 2 : 1;
+      auto issue_S = [&](int t, int j) {
+        const int s = j % KV_STAGES;
+        const uint64_t dq = umma_desc_kmajor_sw128(smem_u32(sm.q[t]));
+        const uint64_t dk = umma_desc_kmajor_sw128(smem_u32(sm.k[s]));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+          const uint32_t off = ((kk >> 2) * CHUNK + (kk & 3) * 32) >> 4;
+          umma_bf16_ss(tbase + t * 128, dq + off, dk + off, idS, kk > 0);
+        }
+        umma_commit(&sm.s_full[t]);
+      };
+      auto issue_PV = [&](int t, int j) {
+        const int s = j % KV_STAGES;
+        const uint64_t dp = umma_desc_kmajor_sw128(smem_u32(sm.p));
+        const uint64_t dv = umma_desc_mnmajor_sw128(smem_u32(sm.v[s]), CHUNK);
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; kk++) {
+          const uint32_t off = ((kk >> 2) * CHUNK + (kk & 3) * 32) >> 4;
+          umma_bf16_ss(tbase + 256 + t * 128, dp + off, dv + ((kk * 16 * 128) >> 4), idO, (j | kk) != 0);
+        }
+        umma_commit(&sm.o_done[t]);
+        umma_commit(&sm.p_free[t]);
+      };
+      // per tile: next block whose S to issue (needs s_free of the block before), next P.V
+      int sj[2] = {0, 0}, pj[2] = {0, 0};
+      int s_cnt[KV_STAGES] = {0, 0}, v_cnt[KV_STAGES] = {0, 0};  // issues per stage of the current use
+      const long long t0 = clock64();
+      while (ok && (pj[0] < n_kv || (nt == 2 && pj[1] < n_kv))) {
+        bool progress = false;
+        for (int t = 0; t < nt; t++) {
+          // S(sj): block 0 needs nothing but K; later blocks need the softmax to have read S(sj-1)
+          if (sj[t] < n_kv) {
+            const int j = sj[t];
+            const bool free_ok = j == 0 || mbar_test_wait(smem_u32(&sm.s_free[t]), (j - 1) & 1);
+            if (free_ok && mbar_test_wait(smem_u32(&sm.k_full[j % KV_STAGES]), (j / KV_STAGES) & 1)) {
+              tc_fence_after();
+              issue_S(t, j);
+              sj[t]++;
+              progress = true;
+              if (++s_cnt[j % KV_STAGES] == nt) {
+                umma_commit(&sm.k_empty[j % KV_STAGES]);
+                s_cnt[j % KV_STAGES] = 0;
+              }
+            }
+          }
+          // P.V(pj): P in shared memory and V landed
+          if (pj[t] < n_kv && pj[t] < sj[t]) {
+            const int j = pj[t];
+            if (mbar_test_wait(smem_u32(&sm.p_full[t]), j & 1) &&
+                mbar_test_wait(smem_u32(&sm.v_full[j % KV_STAGES]), (j / KV_STAGES) & 1)) {
+              tc_fence_after();
+              issue_PV(t, j);
+              pj[t]++;
+              progress = true;
+              if (++v_cnt[j % KV_STAGES] == nt) {
+                umma_commit(&sm.v_empty[j % KV_STAGES]);
+                v_cnt[j % KV_STAGES] = 0;
+              }
+            }
+          }
+        }
+        if (!progress && (unsigned long long)(clock64() - t0) > FT_WAIT_LIMIT_CYCLES * 4) {
+          record_error(kErrWaitTimeout);
+          ok = false;
+        }
+        if (!progress && error_raised()) ok = false;
+      }
+      if (!ok) {
+        umma_commit(&sm.drain);
+        spin_drain(&sm.drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int t = warp >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qpos = q0 + t * TILE + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tbase + t * 128 + lane_off;
+    const uint32_t tO = tbase + 256 + t * 128 + lane_off;
+    const bool active = (t == 0) || has_b;
+    uint8_t* prow = sm.p + r * 128;  // this thread's row in both 64-key chunks
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; active && j < n_kv; j++) {
+      const int kbase = j * TILE;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool masked = (kbase + TILE > a.Sk) || (a.causal && kbase + TILE > q0 + t * TILE);
+      uint32_t v[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld_32x32b_x32(tS + c * 32, v[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 4; c++) reg_fence32(v[c]);
+      // S is in registers: the MMA warp may overwrite it with the next block's S right away
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_free[t]);
+      if (masked) {
+        const int lim = min(a.Sk, a.causal ? qpos + 1 : a.Sk) - kbase;
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+          for (int e = 0; e < 32; e++)
+            if (c * 32 + e >= lim) v[c][e] = 0xff800000u;
+      }
+      float mx;
+      {
+        float m0 = __uint_as_float(v[0][0]), m1 = __uint_as_float(v[1][0]);
+        float m2 = __uint_as_float(v[2][0]), m3 = __uint_as_float(v[3][0]);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          m0 = max3(m0, __uint_as_float(v[0][e]), __uint_as_float(v[0][e + 1]));
+          m1 = max3(m1, __uint_as_float(v[1][e]), __uint_as_float(v[1][e + 1]));
+          m2 = max3(m2, __uint_as_float(v[2][e]), __uint_as_float(v[2][e + 1]));
+          m3 = max3(m3, __uint_as_float(v[3][e]), __uint_as_float(v[3][e + 1]));
+        }
+        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+      }
+      mx *= a.scale_log2;
+      const bool need = (mx > m + RESCALE_THRESHOLD) || (m == -INFINITY);
+      const bool rescale = __any_sync(0xffffffffu, need);
+      float alpha = 1.f;
+      if (rescale) {
+        const float m_new = fmaxf(m, mx);
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+        l *= alpha;
+        m = m_new;
+      }
+      const float msub = (m == -INFINITY) ? 0.f : m;
+      unsigned long long rsc[4] = {0ull, 0ull, 0ull, 0ull};
+      const unsigned long long scale2 = f2pack(a.scale_log2, a.scale_log2);
+      const unsigned long long negm2 = f2pack(-msub, -msub);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const unsigned long long x2 =
+              fma2(f2pack(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), scale2, negm2);
+          float x0, x1;
+          f2unpack(x2, x0, x1);
+          float p0, p1;
+          if (emu_pair<EMU>(i)) {
+            p0 = exp2_fma(x0);
+            p1 = exp2_fma(x1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          rsc[i & 3] = add2(rsc[i & 3], f2pack(p0, p1));
+          v[c][i] = pack_bf16x2(p0, p1);
+        }
+      }
+      {
+        float a0, a1, b0, b1;
+        f2unpack(add2(rsc[0], rsc[1]), a0, a1);
+        f2unpack(add2(rsc[2], rsc[3]), b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
+      if (rescale && j > 0) {
+        // O_t is quiescent once P.V(j-1) of this tile completed
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (j - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int oc = 0; oc < 4; oc++) {
+          uint32_t o[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3]), "=r"(o[4]), "=r"(o[5]), "=r"(o[6]), "=r"(o[7]),
+                "=r"(o[8]), "=r"(o[9]), "=r"(o[10]), "=r"(o[11]), "=r"(o[12]), "=r"(o[13]), "=r"(o[14]),
+                "=r"(o[15])
+              : "r"(tO + oc * 32));
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x16(tO + oc * 32, o);
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3]), "=r"(o[4]), "=r"(o[5]), "=r"(o[6]), "=r"(o[7]),
+                "=r"(o[8]), "=r"(o[9]), "=r"(o[10]), "=r"(o[11]), "=r"(o[12]), "=r"(o[13]), "=r"(o[14]),
+                "=r"(o[15])
+              : "r"(tO + oc * 32 + 16));
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x16(tO + oc * 32 + 16, o);
+        }
+        tmem_st_wait();
+      }
+      // the shared P buffer: the other tile's P.V of the previous turn must have read it
+      // (tile A at block j waits for tile B's block j-1, tile B for tile A's block j)
+      if (has_b) {
+        const int other = t ^ 1;
+        const int need_blk = t == 0 ? j - 1 : j;
+        if (need_blk >= 0 && !__all_sync(0xffffffffu, mbar_wait(&sm.p_free[other], need_blk & 1))) {
+          ok = false;
+          break;
+        }
+      } else if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sm.p_free[0], (j - 1) & 1))) {
+        ok = false;
+        break;
+      }
+      // P row: keys 8c..8c+7 -> 16-byte chunk c, 128-byte swizzle within each 64-key chunk
+#pragma unroll
+      for (int c = 0; c < 16; c++) {
+        const uint4 w = make_uint4(v[c >> 2][(c & 3) * 4 + 0], v[c >> 2][(c & 3) * 4 + 1],
+                                   v[c >> 2][(c & 3) * 4 + 2], v[c >> 2][(c & 3) * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow + (c >> 3) * CHUNK + (((c & 7) ^ (r & 7)) << 4)) = w;
+      }
+      fence_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[t]);
+    }
+    if (active && ok && n_kv > 0 && __all_sync(0xffffffffu, mbar_wait(&sm.o_done[t], (n_kv - 1) & 1))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tO + c * 32, v);
+        tmem_ld_wait();
+        if (qpos < a.Sq) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[u * 8 + 0]) * inv, __uint_as_float(v[u * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[u * 8 + 2]) * inv, __uint_as_float(v[u * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[u * 8 + 4]) * inv, __uint_as_float(v[u * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[u * 8 + 6]) * inv, __uint_as_float(v[u * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(out + c * 32 + u * 8) = w;
+          }
+        }
+      }
+    } else if (active && n_kv == 0 && qpos < a.Sq) {
+      __nv_bfloat16* out = a.o + (long long)b * a.o_batch + (long long)qpos * a.o_row + h * HD;
+      for (int d = 0; d < HD; d++) out[d] = __float2bfloat16(0.f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 bool make_tmap_3d(CUtensorMap* map, const void* base, int H, int S, int B, long long row_stride,
                   long long batch_stride) {
   // dims (inner->outer): head*dim columns, sequence rows, batch; box 64 x 128 x 1, 128-byte swizzle
@@ -1443,6 +1811,20 @@ cudaError_t attention_fwd(const AttnProblem& p, cudaStream_t stream) {
       return cudaGetLastError();
     };
     return p.diag_mode == 200 ? go1(attn1_fwd_kernel<0>) : go1(attn1_fwd_kernel<1>);
+  }
+  if (p.diag_mode >= 400 && p.diag_mode <= 402) {  // P through shared memory (see attnP_fwd_kernel)
+    a.diag = 0;
+    const int smemP = (int)sizeof(SmemP) + 1024;
+    const long long gridP = (long long)a.n_qblocks * p.Hq * p.B;
+    if (gridP > 0x7fffffff) return cudaErrorInvalidValue;
+    auto goP = [&](auto kern) -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smemP);
+      if (e != cudaSuccess) return e;
+      kern<<<(int)gridP, NTHREADS, smemP, stream>>>(tq, tk, tv, a);
+      return cudaGetLastError();
+    };
+    return p.diag_mode == 400 ? goP(attnP_fwd_kernel<0>)
+                              : (p.diag_mode == 401 ? goP(attnP_fwd_kernel<1>) : goP(attnP_fwd_kernel<2>));
   }
   if (p.diag_mode >= 300 && p.diag_mode <= 302) {  // split-row variant (see attn2x_fwd_kernel)
     a.diag = 0;

@@ -226,12 +226,13 @@ def test_attention_one_tile_kernel(mode, B, Sq, Sk, H, Hk, causal):
     assert rel_err(o, ops.attention(q, k, v, causal=causal)) < 1e-2
 
 
-@pytest.mark.parametrize("mode", [300, 301, 302])
+@pytest.mark.parametrize("mode", [300, 301, 302, 400, 401, 402])
 @pytest.mark.parametrize("B,Sq,Sk,H,Hk,causal", [(1, 128, 128, 1, 1, False), (2, 300, 300, 4, 4, False),
                                                  (1, 384, 1000, 8, 2, False), (2, 500, 500, 4, 4, True),
                                                  (1, 1024, 2048, 2, 1, False)])
 def test_attention_split_row_kernel(mode, B, Sq, Sk, H, Hk, causal):
-    """The split-row kernel (two warps per query row, ``_diag_mode`` 300-302) against the fp32
+    """The split-row kernel (two warps per query row, ``_diag_mode`` 300-302) and the
+    P-through-shared-memory kernel (event-driven MMA issue, modes 400-402) against the fp32
     reference and the default kernel; keys with growing scale exercise the rescale path."""
     torch.manual_seed(11)
     q = torch.randn(B, Sq, H, 128, device=DEV).bfloat16()
