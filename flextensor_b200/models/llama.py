@@ -154,7 +154,7 @@ class LlamaLayer(nn.Module):
         qn, kn = self.hq * D, self.hk * D
         ag_fused = tp.collective in ("fused", "fused_ag")
         rs_fused = tp.collective in ("fused", "fused_rs")
-        _ag, _rs = tp.buffers(B * S)
+        _ag, _rs = tp.tp_buffers(B * S)
 
         def gathered_gemm(norm_w, w, epi):
             if ag_fused:  # RMSNorm of the own rows straight into the all-gather buffer
@@ -350,7 +350,7 @@ class LlamaTP(nn.Module):
         if tokens_total not in self._by_rows:
             self._by_rows[tokens_total] = self._make(tokens_total)
 
-    def buffers(self, rows: int):
+    def tp_buffers(self, rows: int):
         """(all-gather, reduce-scatter) objects sized for ``rows`` token rows."""
         if rows not in self._by_rows:
             raise ValueError(f"no fused TP buffers for {rows} rows: call setup()/add_rows() on every rank first")
