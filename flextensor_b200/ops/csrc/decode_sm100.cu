@@ -2,24 +2,24 @@
 // ("flash-decoding"), GQA, head_dim 128, bf16, for sm_100a.
 //
 // A decode step reads every cached key and value once and does ~2 FLOPs per byte: the kernel is
-// bound by HBM bandwidth, not by a tensor core (the G <= 16 query heads of a KV group would fill
-// at most 1/8 of a 128-row tcgen05 tile). So it streams the cache with TMA and computes on the
-// FMA pipe:
-//   * grid = (key split, KV head, sequence); each CTA covers a contiguous run of 64-key tiles of
-//     one sequence's cache for one KV head and ALL G query heads that share it (the K/V bytes
-//     are read once per group, not once per query head);
-//   * warp 8 (one elected lane) loads K and V tiles with 4-D tensor maps ([B, L, Hk, 128]
-//     cache, 128-byte swizzle, no multicast) into a 2-stage ring guarded by mbarriers;
-//   * warps 0-7: S = q K^T with four threads per key (each G/4 of the heads, fp32 pairs on the
-//     FMA pipe), an online softmax per head (warp h owns head h: tile max and sum by shuffles,
-//     exp2 on MUFU, running max / sum in registers), and O += P V with warp w owning keys
-//     8w..8w+7 of the tile and lane l owning dims 4l..4l+3 of every head;
-//   * after the last tile the eight warps' partial O are summed in shared memory; a single split
-//     writes bf16 output directly, otherwise (O, max, sum) per split go to a caller-provided
-//     fp32 scratch and decode_combine_kernel merges them (weights 2^(m_s - M)).
-// Keys at or past a sequence's length are masked. All waits are bounded: a timeout records the
-// device error word, the producer drains its own loads, and the consumers fall through their
-// remaining tiles without computing.
+// bound by HBM bandwidth. The G <= 16 query heads that share a KV head form the M side of the
+// products (padded to 16 rows), far below the 64/128 rows of a tcgen05 tile, so the products use
+// warp-level m16n8k16 MMAs with the query fragments held in registers for the whole CTA:
+//   * grid = (key split, KV head, sequence); a CTA covers a contiguous run of 64-key tiles of one
+//     sequence's cache for one KV head and all G query heads of that group, so each K/V byte is
+//     read once per group;
+//   * warp 4 (one elected lane) streams K and V tiles with 4-D tensor maps ([B, L, Hk, 128]
+//     cache, 128-byte swizzle, no multicast) into a 6-stage ring guarded by mbarriers;
+//   * warps 0-3 each take every 4th tile: S = Q K^T (K fragments by ldmatrix from the swizzled
+//     tile), an online softmax on the accumulator fragments (row max / sum across the four lanes
+//     of a row by shuffles, exp2 on MUFU), P re-packed in registers as the A operand, and
+//     O += P V (V fragments by ldmatrix.trans); O stays in registers;
+//   * the four warps' (O, max, sum) are merged in shared memory; one split writes bf16 output,
+//     several write fp32 partials to a caller-provided scratch that decode_combine_kernel merges.
+// Keys at or past a sequence's length are masked in S, and their V rows (possibly uninitialised
+// cache memory) are zeroed in shared memory so 0 * NaN never reaches O. Every wait is bounded:
+// a timeout records the device error word, the producer drains its own loads and the consumers
+// fall through their remaining tiles without computing.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -35,14 +35,14 @@ namespace {
 
 constexpr int DHD = 128;              // head dim
 constexpr int KT = 64;                // keys per tile
-constexpr int DSTAGES = 2;
-constexpr int DCONS = 256;            // consumer threads (warps 0-7)
-constexpr int DTHREADS = DCONS + 32;  // + producer warp
+constexpr int DSTAGES = 6;
+constexpr int NCW = 4;                // consumer warps
+constexpr int DTHREADS = 32 * (NCW + 1);
 constexpr int BOX_BYTES = KT * 128;   // one [64 keys x 64 dims] bf16 box (8 KB)
-constexpr int QSTRIDE = DHD + 4;      // padded fp32 q rows (bank spread across heads)
+constexpr int STAGE_BYTES = 4 * BOX_BYTES;  // K (two boxes) + V (two boxes)
 
 struct DecArgs {
-  int B, Hq, Hk, L;            // L: cache capacity (tokens)
+  int B, Hq, Hk, L, G;         // L: cache capacity (tokens); G: query heads per KV head
   const __nv_bfloat16* q;      // [B, Hq, 128]
   long long q_b;               // elements between sequences
   __nv_bfloat16* o;            // [B, Hq, 128]
@@ -55,28 +55,16 @@ struct DecArgs {
   float* part_ml;              // [n_split, B, Hq, 2]   running max (log2 units) and sum
 };
 
-template <int G>
 struct DecSmem {
-  uint8_t k[DSTAGES][2 * BOX_BYTES];
-  uint8_t v[DSTAGES][2 * BOX_BYTES];
-  alignas(16) float q[G][QSTRIDE];
-  float s[G][KT + 1];
-  alignas(16) float p[KT][(G + 3) / 4 * 4];  // P per key, all heads (float4 reads)
-  float alpha[G];
-  float ml[G][2];
+  uint8_t stage[DSTAGES][STAGE_BYTES];  // per stage: K box 0 | K box 1 | V box 0 | V box 1
+  float wm[NCW][16], wl[NCW][16];       // per warp: row max / sum for the merge
   uint64_t full[DSTAGES], empty[DSTAGES];
 };
 
-// 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled box
-__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
-
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& w, float (&f)[8]) {
-  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    f[2 * i] = __uint_as_float(u[i] << 16);
-    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
-  }
+// byte offset of 16-byte chunk `c` (0..15 over 128 dims) of row `r` in a [64 x 128] tile stored
+// as two 128-byte-swizzled [64 x 64] boxes
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {
+  return (uint32_t)((c >> 3) * BOX_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -92,15 +80,33 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
-__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
 
-template <int G>
-__global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
+// D += A(16x16, row) * B(16x8, col), bf16 inputs, fp32 accumulators
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t ldq2(const __nv_bfloat16* p, bool ok) {
+  return ok ? *reinterpret_cast<const uint32_t*>(p) : 0u;
+}
+
+__global__ void __launch_bounds__(DTHREADS, 1)
     decode_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, DecArgs a) {
-  constexpr int HPT = (G + 3) / 4;  // heads per thread in q K^T
-  constexpr int GP = (G + 3) / 4 * 4;
   extern __shared__ uint8_t smem_raw[];
-  DecSmem<G>& sm = *reinterpret_cast<DecSmem<G>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DecSmem& sm = *reinterpret_cast<DecSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int len = a.seqlens ? min(a.seqlens[b], a.L) : a.kv_len;
@@ -111,18 +117,13 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
   if (tid == 0) {
     for (int s = 0; s < DSTAGES; s++) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 8);  // lane 0 of every consumer warp
+      mbar_init(&sm.empty[s], 1);  // the consumer warp that used the stage
     }
     fence_barrier_init();
   }
-  // q of the group, pre-scaled into log2 units
-  for (int i = tid; i < G * DHD; i += DTHREADS) {
-    const int g = i / DHD, d = i % DHD;
-    sm.q[g][d] = __bfloat162float(a.q[(long long)b * a.q_b + (long long)(hk * G + g) * DHD + d]) * a.scale_log2;
-  }
   __syncthreads();
 
-  if (warp == 8) {
+  if (warp == NCW) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&tmK);
@@ -137,10 +138,10 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
           break;
         }
         const int key0 = (t_begin + i) * KT;
-        mbar_arrive_expect_tx(&sm.full[s], 4 * BOX_BYTES);
+        mbar_arrive_expect_tx(&sm.full[s], STAGE_BYTES);
         for (int c = 0; c < 2; c++) {
-          tma_load_4d(sm.k[s] + c * BOX_BYTES, &tmK, &sm.full[s], c * 64, hk, key0, b);
-          tma_load_4d(sm.v[s] + c * BOX_BYTES, &tmV, &sm.full[s], c * 64, hk, key0, b);
+          tma_load_4d(sm.stage[s] + c * BOX_BYTES, &tmK, &sm.full[s], c * 64, hk, key0, b);
+          tma_load_4d(sm.stage[s] + (2 + c) * BOX_BYTES, &tmV, &sm.full[s], c * 64, hk, key0, b);
         }
         pend |= 1u << s;
         pph = (pph & ~(1u << s)) | (ph << s);
@@ -156,166 +157,175 @@ __global__ void __launch_bounds__(DTHREADS, G <= 8 ? 2 : 1)
     }
   } else {
     // ------------------------------------------------------------------ consumers
-    const int key = tid & (KT - 1), hg = tid >> 6;      // q K^T: thread = (key, head group)
-    const int hs = warp;                                // softmax: warp = head (and head + 8)
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    unsigned long long acc[G][2];  // (dims 4l, 4l+1) and (4l+2, 4l+3) of every head, fp32 pairs
+    const int r0 = lane >> 2, cq = (lane & 3) * 2;  // accumulator rows r0 / r0+8, columns cq, cq+1
+    // Q as A fragments for the 8 k-steps (rows = heads of the group, zero past G)
+    uint32_t qa[8][4];
+    {
+      const __nv_bfloat16* qb = a.q + (long long)b * a.q_b + (long long)hk * a.G * DHD;
+      const bool ok0 = r0 < a.G, ok1 = r0 + 8 < a.G;
 #pragma unroll
-    for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = 0ull;
+      for (int kk = 0; kk < 8; kk++) {
+        qa[kk][0] = ldq2(qb + r0 * DHD + kk * 16 + cq, ok0);
+        qa[kk][1] = ldq2(qb + (r0 + 8) * DHD + kk * 16 + cq, ok1);
+        qa[kk][2] = ldq2(qb + r0 * DHD + kk * 16 + 8 + cq, ok0);
+        qa[kk][3] = ldq2(qb + (r0 + 8) * DHD + kk * 16 + 8 + cq, ok1);
+      }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int dn = 0; dn < 16; dn++) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows r0, r0+8 (l: this lane's part)
     bool ok = true;
-    for (int i = 0; i < n_tiles; i++) {
+    for (int i = warp; i < n_tiles; i += NCW) {
       const int s = i % DSTAGES;
-      const uint32_t ph = (i / DSTAGES) & 1;
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.full[s], ph));
-      const int key0 = (t_begin + i) * KT;
-      // ---- S = q K^T for this thread's key and heads
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.full[s], (i / DSTAGES) & 1));
       if (ok) {
-        const uint8_t* kt = sm.k[s];
-        unsigned long long accp[HPT];
+        const int key0 = (t_begin + i) * KT;
+        const int nvalid = min(KT, len - key0);
+        const uint32_t kbase = smem_u32(sm.stage[s]);
+        const uint32_t vbase = kbase + 2 * BOX_BYTES;
+        if (nvalid < KT) {  // zero the V rows past the length (cache memory there may hold NaN)
+          uint8_t* vt = sm.stage[s] + 2 * BOX_BYTES;
+          for (int e = lane; e < (KT - nvalid) * 16; e += 32) {
+            const int rr = nvalid + e / 16, c = e % 16;
+            *reinterpret_cast<uint4*>(vt + tile_off(rr, c)) = make_uint4(0u, 0u, 0u, 0u);
+          }
+          __syncwarp();
+        }
+        // ---- S = Q K^T : 8 n-tiles of 8 keys
+        float sc[8][4];
 #pragma unroll
-        for (int u = 0; u < HPT; u++) accp[u] = 0ull;
-#pragma unroll 4
-        for (int c = 0; c < 16; c++) {
-          const uint4 w = *reinterpret_cast<const uint4*>(kt + (c >> 3) * BOX_BYTES + swz(key, c & 7));
-          float kf[8];
-          bf16x8_to_f32(w, kf);
+        for (int jn = 0; jn < 8; jn++) {
+          sc[jn][0] = sc[jn][1] = sc[jn][2] = sc[jn][3] = 0.f;
+          const int krow = jn * 8 + (lane & 7);
 #pragma unroll
-          for (int u = 0; u < HPT; u++) {
-            const int g = hg * HPT + u;
-            if (g < G) {
-              const float4 q0 = *reinterpret_cast<const float4*>(&sm.q[g][c * 8]);
-              const float4 q1 = *reinterpret_cast<const float4*>(&sm.q[g][c * 8 + 4]);
-              unsigned long long x = accp[u];
-              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(x) : "l"(((unsigned long long)__float_as_uint(kf[1]) << 32) | __float_as_uint(kf[0])),
-                  "l"(((unsigned long long)__float_as_uint(q0.y) << 32) | __float_as_uint(q0.x)));
-              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(x) : "l"(((unsigned long long)__float_as_uint(kf[3]) << 32) | __float_as_uint(kf[2])),
-                  "l"(((unsigned long long)__float_as_uint(q0.w) << 32) | __float_as_uint(q0.z)));
-              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(x) : "l"(((unsigned long long)__float_as_uint(kf[5]) << 32) | __float_as_uint(kf[4])),
-                  "l"(((unsigned long long)__float_as_uint(q1.y) << 32) | __float_as_uint(q1.x)));
-              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(x) : "l"(((unsigned long long)__float_as_uint(kf[7]) << 32) | __float_as_uint(kf[6])),
-                  "l"(((unsigned long long)__float_as_uint(q1.w) << 32) | __float_as_uint(q1.z)));
-              accp[u] = x;
-            }
+          for (int kp = 0; kp < 4; kp++) {  // k-step pairs: chunks 4kp .. 4kp+3
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kbase + tile_off(krow, 4 * kp + (lane >> 3)), b0, b1, b2, b3);
+            mma16816(sc[jn], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0, b1);
+            mma16816(sc[jn], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], b2, b3);
           }
         }
-        const bool valid = key0 + key < len;
+        // ---- online softmax on the fragments (rows r0: sc[.][0..1], r0+8: sc[.][2..3])
+        float tm0 = -INFINITY, tm1 = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < HPT; u++) {
-          const int g = hg * HPT + u;
-          if (g < G) {
-            const float sv = __uint_as_float((uint32_t)accp[u]) + __uint_as_float((uint32_t)(accp[u] >> 32));
-            sm.s[g][key] = valid ? sv : -INFINITY;
+        for (int jn = 0; jn < 8; jn++) {
+          const int k = jn * 8 + cq;
+#pragma unroll
+          for (int e = 0; e < 2; e++) {
+            const bool v = k + e < nvalid;
+            sc[jn][e] = v ? sc[jn][e] * a.scale_log2 : -INFINITY;
+            sc[jn][2 + e] = v ? sc[jn][2 + e] * a.scale_log2 : -INFINITY;
+            tm0 = fmaxf(tm0, sc[jn][e]);
+            tm1 = fmaxf(tm1, sc[jn][2 + e]);
           }
         }
-      }
-      cons_sync();
-      // ---- online softmax, one warp per head
-      if (ok) {
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 1));
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 2));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 1));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 2));
+        const float n0 = fmaxf(m0, tm0), n1 = fmaxf(m1, tm1);
+        const float s0 = n0 == -INFINITY ? 0.f : n0, s1 = n1 == -INFINITY ? 0.f : n1;
+        const float al0 = m0 == -INFINITY ? 0.f : ex2f(m0 - s0), al1 = m1 == -INFINITY ? 0.f : ex2f(m1 - s1);
+        m0 = n0;
+        m1 = n1;
+        l0 *= al0;
+        l1 *= al1;
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-          const int g = hs + 8 * hh;
-          if (g < G) {
-            const float s0 = sm.s[g][lane], s1 = sm.s[g][lane + 32];
-            float mx = fmaxf(s0, s1);
-#pragma unroll
-            for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float m_new = fmaxf(m_run[hh], mx);
-            const float msub = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = m_run[hh] == -INFINITY ? 0.f : ex2f(m_run[hh] - msub);
-            const float p0 = ex2f(s0 - msub), p1 = ex2f(s1 - msub);
-            float ps = p0 + p1;
-#pragma unroll
-            for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            l_run[hh] = l_run[hh] * alpha + ps;
-            m_run[hh] = m_new;
-            sm.p[lane][g] = p0;
-            sm.p[lane + 32][g] = p1;
-            if (lane == 0) sm.alpha[g] = alpha;
-          }
+        for (int dn = 0; dn < 16; dn++) {
+          o[dn][0] *= al0;
+          o[dn][1] *= al0;
+          o[dn][2] *= al1;
+          o[dn][3] *= al1;
         }
-        if (G < GP && warp == 0 && lane < KT / 2) {  // padded heads read as zero
+        uint32_t pa[4][4];  // P as A fragments, one per 16-key k-step
 #pragma unroll
-          for (int g = G; g < GP; g++) {
-            sm.p[lane][g] = 0.f;
-            sm.p[lane + 32][g] = 0.f;
-          }
+        for (int jn = 0; jn < 8; jn++) {
+          const float p0 = ex2f(sc[jn][0] - s0), p1 = ex2f(sc[jn][1] - s0);
+          const float p2 = ex2f(sc[jn][2] - s1), p3 = ex2f(sc[jn][3] - s1);
+          l0 += p0 + p1;
+          l1 += p2 + p3;
+          pa[jn >> 1][(jn & 1) * 2 + 0] = pack_bf16x2(p0, p1);
+          pa[jn >> 1][(jn & 1) * 2 + 1] = pack_bf16x2(p2, p3);
         }
-      }
-      cons_sync();
-      // ---- O += P V: warp owns keys 8w..8w+7, lane owns dims 4l..4l+3 of every head
-      if (ok) {
+        // ---- O += P V : 16 n-tiles of 8 dims, 4 k-steps of 16 keys
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-          const float al = sm.alpha[g];
-          const unsigned long long al2 = ((unsigned long long)__float_as_uint(al) << 32) | __float_as_uint(al);
+        for (int kp = 0; kp < 4; kp++) {
+          const int vrow = kp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
-          for (int e = 0; e < 2; e++) asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(acc[g][e]) : "l"(al2));
-        }
-        const uint8_t* vt = sm.v[s] + (lane >> 4) * BOX_BYTES;
-        const int cc = (lane & 15) >> 1, sub = (lane & 1) * 8;
-        const int nvalid = len - key0;  // keys past the length: P is 0, but their V rows may be
-                                        // uninitialised cache memory (0 * NaN = NaN), so skip them
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-          const int kr = warp * 8 + kk;
-          if (kr >= nvalid) break;
-          const uint2 w = *reinterpret_cast<const uint2*>(vt + swz(kr, cc) + sub);
-          const unsigned long long v01 =
-              ((unsigned long long)(w.x & 0xffff0000u) << 32) | (unsigned long long)(w.x << 16);
-          const unsigned long long v23 =
-              ((unsigned long long)(w.y & 0xffff0000u) << 32) | (unsigned long long)(w.y << 16);
-#pragma unroll
-          for (int g4 = 0; g4 < GP; g4 += 4) {
-            const float4 pp = *reinterpret_cast<const float4*>(&sm.p[kr][g4]);
-            const float pv[4] = {pp.x, pp.y, pp.z, pp.w};
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-              if (g4 + u < G) {
-                const unsigned long long p2 =
-                    ((unsigned long long)__float_as_uint(pv[u]) << 32) | __float_as_uint(pv[u]);
-                asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[g4 + u][0]) : "l"(p2), "l"(v01));
-                asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[g4 + u][1]) : "l"(p2), "l"(v23));
-              }
-            }
+          for (int dp = 0; dp < 8; dp++) {  // dim n-tile pairs 2dp, 2dp+1
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vbase + tile_off(vrow, 2 * dp + (lane >> 4)), b0, b1, b2, b3);
+            mma16816(o[2 * dp], pa[kp][0], pa[kp][1], pa[kp][2], pa[kp][3], b0, b1);
+            mma16816(o[2 * dp + 1], pa[kp][0], pa[kp][1], pa[kp][2], pa[kp][3], b2, b3);
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty[s]);
     }
-    // ---- sum the eight warps' partial O in the K/V ring: every tile loaded has been consumed
-    // and the producer issues nothing more
-    cons_sync();
-    float* red = reinterpret_cast<float*>(&sm.k[0][0]);  // [8 warps][G][128]
-#pragma unroll
-    for (int g = 0; g < G; g++)
-      *reinterpret_cast<float4*>(&red[(warp * G + g) * DHD + lane * 4]) =
-          make_float4(__uint_as_float((uint32_t)acc[g][0]), __uint_as_float((uint32_t)(acc[g][0] >> 32)),
-                      __uint_as_float((uint32_t)acc[g][1]), __uint_as_float((uint32_t)(acc[g][1] >> 32)));
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      const int g = hs + 8 * hh;
-      if (g < G && lane == 0) {
-        sm.ml[g][0] = m_run[hh];
-        sm.ml[g][1] = l_run[hh];
-      }
+    // ---- merge the four warps: row sums over the lanes of a row, then (O, m, l) across warps
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if ((lane & 3) == 0) {
+      sm.wm[warp][r0] = m0;
+      sm.wm[warp][r0 + 8] = m1;
+      sm.wl[warp][r0] = l0;
+      sm.wl[warp][r0 + 8] = l1;
     }
-    cons_sync();
-    for (int i = tid; i < G * DHD; i += DCONS) {
-      const int g = i / DHD, d = i % DHD;
-      float o = 0.f;
+    // consumers only (the producer may still be draining): named barrier over the 4 warps
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
+    float M0 = -INFINITY, M1 = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < 8; w++) o += red[(w * G + g) * DHD + d];
-      const int hq = hk * G + g;
+    for (int w = 0; w < NCW; w++) {
+      M0 = fmaxf(M0, sm.wm[w][r0]);
+      M1 = fmaxf(M1, sm.wm[w][r0 + 8]);
+    }
+    const float f0 = M0 == -INFINITY || m0 == -INFINITY ? 0.f : ex2f(m0 - M0);
+    const float f1 = M1 == -INFINITY || m1 == -INFINITY ? 0.f : ex2f(m1 - M1);
+    float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; w++) {
+      const float mw0 = sm.wm[w][r0], mw1 = sm.wm[w][r0 + 8];
+      L0 += mw0 == -INFINITY ? 0.f : ex2f(mw0 - M0) * sm.wl[w][r0];
+      L1 += mw1 == -INFINITY ? 0.f : ex2f(mw1 - M1) * sm.wl[w][r0 + 8];
+    }
+    // every warp's O, weighted, summed through shared memory: red[row][dim] fp32 (8 KB), reusing
+    // stage 0 (all loads of this CTA landed and were consumed)
+    float* red = reinterpret_cast<float*>(sm.stage[0]);
+    for (int e = tid; e < 16 * DHD; e += 32 * NCW) red[e] = 0.f;
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
+#pragma unroll
+    for (int dn = 0; dn < 16; dn++) {
+      const int d = dn * 8 + cq;
+      atomicAdd(&red[r0 * DHD + d], o[dn][0] * f0);
+      atomicAdd(&red[r0 * DHD + d + 1], o[dn][1] * f0);
+      atomicAdd(&red[(r0 + 8) * DHD + d], o[dn][2] * f1);
+      atomicAdd(&red[(r0 + 8) * DHD + d + 1], o[dn][3] * f1);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
+    if (warp == 0 && (lane & 3) == 0) {  // the merged row statistics (every warp read wm/wl above)
+      sm.wm[0][r0] = M0;
+      sm.wm[0][r0 + 8] = M1;
+      sm.wl[0][r0] = L0;
+      sm.wl[0][r0 + 8] = L1;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
+    for (int e = tid; e < a.G * DHD; e += 32 * NCW) {
+      const int g = e / DHD, d = e % DHD;
+      const int hq = hk * a.G + g;
+      const float val = red[g * DHD + d];
       if (a.n_split == 1) {
-        const float l = sm.ml[g][1];
-        a.o[(long long)b * a.o_b + (long long)hq * DHD + d] = __float2bfloat16(ok && l > 0.f ? o / l : 0.f);
+        const float L = sm.wl[0][g];
+        a.o[(long long)b * a.o_b + (long long)hq * DHD + d] = __float2bfloat16(ok && L > 0.f ? val / L : 0.f);
       } else {
         const long long row = ((long long)split * a.B + b) * a.Hq + hq;
-        a.part_o[row * DHD + d] = ok ? o : 0.f;
+        a.part_o[row * DHD + d] = ok ? val : 0.f;
         if (d == 0) {
-          a.part_ml[row * 2] = ok ? sm.ml[g][0] : -INFINITY;
-          a.part_ml[row * 2 + 1] = ok ? sm.ml[g][1] : 0.f;
+          a.part_ml[row * 2] = ok ? sm.wm[0][g] : -INFINITY;
+          a.part_ml[row * 2 + 1] = ok ? sm.wl[0][g] : 0.f;
         }
       }
     }
@@ -350,26 +360,13 @@ bool make_tmap_cache(CUtensorMap* map, const void* base, int Hk, int L, int B, l
                            (uint64_t)batch_stride, 64, 1, KT, 1);
 }
 
-template <int G>
-cudaError_t launch_g(const CUtensorMap& tk, const CUtensorMap& tv, const DecArgs& a, dim3 grid, cudaStream_t st) {
-  const int smem = (int)sizeof(DecSmem<G>) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  decode_split_kernel<G><<<grid, DTHREADS, smem, st>>>(tk, tv, a);
-  return cudaGetLastError();
-}
-
 }  // namespace
 
 int decode_splits(int B, int Hk, int max_len, int num_sms) {
   const int tiles = (max(max_len, 1) + KT - 1) / KT;
   const int base = max(1, B * Hk);
-  int n = (2 * max(num_sms, 1) + base - 1) / base;  // about two CTAs per SM
-  n = max(1, min(n, (tiles + 1) / 2));               // at least two tiles per split where possible
+  int n = (4 * max(num_sms, 1) + base - 1) / base;  // about four CTAs' worth of work per SM
+  n = max(1, min(n, tiles / NCW));                    // at least one tile per consumer warp
   return n;
 }
 
@@ -381,7 +378,10 @@ cudaError_t decode_attention(const DecodeProblem& p, cudaStream_t stream) {
   if (p.B == 0) return cudaSuccess;
   if (p.Hk <= 0 || p.Hq % p.Hk || p.L <= 0) return cudaErrorInvalidValue;
   const int G = p.Hq / p.Hk;
-  if ((reinterpret_cast<uintptr_t>(p.k) & 15) || (reinterpret_cast<uintptr_t>(p.v) & 15)) return cudaErrorMisalignedAddress;
+  if (G > 16) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(p.k) & 15) || (reinterpret_cast<uintptr_t>(p.v) & 15) ||
+      (reinterpret_cast<uintptr_t>(p.q) & 3) || (p.q_b & 1))
+    return cudaErrorMisalignedAddress;
   CUtensorMap tk, tv;
   if (!make_tmap_cache(&tk, p.k, p.Hk, p.L, p.B, p.k_tok, p.k_batch)) return cudaErrorInvalidValue;
   if (!make_tmap_cache(&tv, p.v, p.Hk, p.L, p.B, p.v_tok, p.v_batch)) return cudaErrorInvalidValue;
@@ -390,6 +390,7 @@ cudaError_t decode_attention(const DecodeProblem& p, cudaStream_t stream) {
   a.Hq = p.Hq;
   a.Hk = p.Hk;
   a.L = p.L;
+  a.G = G;
   a.q = p.q;
   a.q_b = p.q_b;
   a.o = p.o;
@@ -404,17 +405,15 @@ cudaError_t decode_attention(const DecodeProblem& p, cudaStream_t stream) {
   a.part_ml = p.scratch ? p.scratch + (size_t)a.n_split * p.B * p.Hq * DHD : nullptr;
   if (a.n_split > 1 && p.scratch == nullptr) return cudaErrorInvalidValue;
   if (p.B > 65535 || p.Hk > 65535) return cudaErrorInvalidValue;
-  const dim3 grid(a.n_split, p.Hk, p.B);
-  cudaError_t e;
-  switch (G) {
-    case 1: e = launch_g<1>(tk, tv, a, grid, stream); break;
-    case 2: e = launch_g<2>(tk, tv, a, grid, stream); break;
-    case 4: e = launch_g<4>(tk, tv, a, grid, stream); break;
-    case 6: e = launch_g<6>(tk, tv, a, grid, stream); break;
-    case 8: e = launch_g<8>(tk, tv, a, grid, stream); break;
-    case 16: e = launch_g<16>(tk, tv, a, grid, stream); break;
-    default: return cudaErrorInvalidValue;
+  const int smem = (int)sizeof(DecSmem) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
   }
+  decode_split_kernel<<<dim3(a.n_split, p.Hk, p.B), DTHREADS, smem, stream>>>(tk, tv, a);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || a.n_split == 1) return e;
   decode_combine_kernel<<<p.B * p.Hq, DHD, 0, stream>>>(a);
   return cudaGetLastError();
