@@ -106,9 +106,9 @@ class MixtralLayer(nn.Module):
             return self.moe_single(h, ids, wts, x, impl)
         if isinstance(ep, NcclExpertParallel):
             return ep(h, ids, wts, [e.w_gate_up for e in self.experts], [e.w_down for e in self.experts], x)
-        pos = ep.dispatch(h, ids)
+        slots = ep.dispatch(h, ids)
         ep.experts([e.w_gate_up for e in self.experts], [e.w_down for e in self.experts])
-        return ep.combine(pos, wts, residual=x, out=x)
+        return ep.combine(slots, wts, residual=x, out=x)
 
 
 class MixtralModel(nn.Module):
@@ -190,6 +190,32 @@ class MixtralModel(nn.Module):
             if i + 1 < max_new:
                 logits = self.decode_step(nxt, cache, S + i, ep)
         return torch.stack(out, dim=1)
+
+
+class MixtralStack(nn.Module):
+    """The decoder layers alone (no embedding / head): the offloadable body for end-to-end runs.
+    ``ep``: an :class:`~flextensor_b200.parallel.ep.ExpertParallel` per token-row count (e.g. the
+    prefill's and the decode step's), chosen by the rows of ``x``."""
+
+    def __init__(self, cfg: MixtralConfig = MIXTRAL_8X22B, rank: int = 0, world: int = 1, layers: int | None = None):
+        super().__init__()
+        self.cfg = cfg
+        el = cfg.n_experts // world
+        mine = list(range(rank * el, (rank + 1) * el))
+        self.layers = nn.ModuleList([MixtralLayer(cfg, mine) for _ in range(layers or cfg.n_layers)])
+
+    def new_cache(self, batch: int, max_len: int, device=None, dtype=torch.bfloat16):
+        c = self.cfg
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        return [(torch.empty(batch, max_len, c.n_kv_heads, c.head_dim, device=dev, dtype=dtype),
+                 torch.empty(batch, max_len, c.n_kv_heads, c.head_dim, device=dev, dtype=dtype))
+                for _ in self.layers]
+
+    def forward(self, x, B, S, rope, ep: dict | None = None, cache=None, pos: int = 0):
+        e = None if not ep else ep.get(x.shape[0])
+        for i, L in enumerate(self.layers):
+            x = L(x, B, S, rope, "fused", ep=e, cache=None if cache is None else cache[i], pos=pos)
+        return x
 
 
 @torch.no_grad()

@@ -135,3 +135,56 @@ def test_reference_ulysses_matches_unsharded_over_gloo():
     for p in ps:
         p.join(30)
     assert all(err < 1e-4 for _, err in res), res
+
+
+def _mixtral_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    from llama_torch import rope_cos_sin
+    from mixtral_torch import MixtralEP, MixtralShape, init_params_
+
+    cfg = MixtralShape(dim=128, n_layers=2, n_heads=2, n_kv_heads=1, ffn_dim=64, n_experts=4, topk=2)
+    cfg_head = cfg.head_dim
+    full = MixtralEP(cfg, 0, 1)
+    init_params_(full, seed=5)
+    mine = MixtralEP(cfg, rank, world)
+    el = cfg.n_experts // world
+    with torch.no_grad():
+        for lf, lm in zip(full.layers, mine.layers):
+            for name, p in lm.named_parameters():
+                if name.startswith("experts."):
+                    j = int(name.split(".")[1])
+                    p.copy_(lf.get_parameter(name.replace(f"experts.{j}.", f"experts.{rank * el + j}.")))
+                else:
+                    p.copy_(lf.get_parameter(name))
+    B, S = 2, 8
+    cos, sin = rope_cos_sin(S, cfg_head, cfg.rope_theta, "cpu")
+    x = torch.randn(B * S, cfg.dim, generator=torch.Generator().manual_seed(rank))
+    with torch.no_grad():
+        want = full(x, B, S, cos, sin)
+        got = mine(x, B, S, cos, sin)
+    q.put((rank, float((got - want).abs().max())))
+    dist.destroy_process_group()
+
+
+def test_reference_mixtral_expert_parallel_matches_single_rank_over_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_mixtral_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(30)
+    assert all(err < 1e-4 for _, err in res), res
