@@ -248,6 +248,9 @@ void decode_attention(const Tensor& q, const Tensor& kc, const Tensor& vc, Tenso
   p.v_batch = vc.stride(0);
   p.o = reinterpret_cast<__nv_bfloat16*>(o3.data_ptr());
   p.o_b = o3.stride(0);
+  // reachable extents from the data pointers: the last sequence's last head row
+  p.q_elems = (B - 1) * q3.stride(0) + Hq * 128;
+  p.o_elems = (B - 1) * o3.stride(0) + Hq * 128;
   if (seqlens && seqlens->defined()) {
     TORCH_CHECK(seqlens->is_cuda() && seqlens->scalar_type() == at::kInt && seqlens->numel() == B &&
                     seqlens->is_contiguous(),

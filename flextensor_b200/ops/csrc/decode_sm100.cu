@@ -53,7 +53,17 @@ struct DecArgs {
   int n_split, tiles_per_split;
   float* part_o;               // [n_split, B, Hq, 128] unnormalised partial outputs
   float* part_ml;              // [n_split, B, Hq, 2]   running max (log2 units) and sum
+  long long q_elems, o_elems;  // extents of q / o (elements) for the bounds checks below
 };
+
+// Global stores are bounds-checked against the extents the host passed (one compare each; they
+// run once per output element, not in the key loop): an index outside records kErrBadArgs in
+// the device error word and the access is skipped.
+__device__ __forceinline__ bool in_range(long long i, long long n) {
+  if (i >= 0 && i < n) return true;
+  record_error(kErrBadArgs);
+  return false;
+}
 
 struct DecSmem {
   uint8_t stage[DSTAGES][STAGE_BYTES];  // per stage: K box 0 | K box 1 | V box 0 | V box 1
@@ -161,14 +171,20 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     // Q as A fragments for the 8 k-steps (rows = heads of the group, zero past G)
     uint32_t qa[8][4];
     {
-      const __nv_bfloat16* qb = a.q + (long long)b * a.q_b + (long long)hk * a.G * DHD;
+      // rows past G are zero; their addresses are clamped to row 0 so no address past the
+      // group (or past the end of q for the last group) is ever formed
+      const long long qoff = (long long)b * a.q_b + (long long)hk * a.G * DHD;
       const bool ok0 = r0 < a.G, ok1 = r0 + 8 < a.G;
+      const bool in0 = in_range(qoff + (ok0 ? r0 : 0) * DHD + DHD - 1, a.q_elems);
+      const bool in1 = in_range(qoff + (ok1 ? r0 + 8 : 0) * DHD + DHD - 1, a.q_elems);
+      const __nv_bfloat16* q0p = a.q + qoff + (ok0 ? r0 : 0) * DHD;
+      const __nv_bfloat16* q1p = a.q + qoff + (ok1 ? r0 + 8 : 0) * DHD;
 #pragma unroll
       for (int kk = 0; kk < 8; kk++) {
-        qa[kk][0] = ldq2(qb + r0 * DHD + kk * 16 + cq, ok0);
-        qa[kk][1] = ldq2(qb + (r0 + 8) * DHD + kk * 16 + cq, ok1);
-        qa[kk][2] = ldq2(qb + r0 * DHD + kk * 16 + 8 + cq, ok0);
-        qa[kk][3] = ldq2(qb + (r0 + 8) * DHD + kk * 16 + 8 + cq, ok1);
+        qa[kk][0] = ldq2(q0p + kk * 16 + cq, ok0 && in0);
+        qa[kk][1] = ldq2(q1p + kk * 16 + cq, ok1 && in1);
+        qa[kk][2] = ldq2(q0p + kk * 16 + 8 + cq, ok0 && in0);
+        qa[kk][3] = ldq2(q1p + kk * 16 + 8 + cq, ok1 && in1);
       }
     }
     float o[16][4];
@@ -319,9 +335,12 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       const float val = red[g * DHD + d];
       if (a.n_split == 1) {
         const float L = sm.wl[0][g];
-        a.o[(long long)b * a.o_b + (long long)hq * DHD + d] = __float2bfloat16(ok && L > 0.f ? val / L : 0.f);
+        const long long oi = (long long)b * a.o_b + (long long)hq * DHD + d;
+        if (in_range(oi, a.o_elems)) a.o[oi] = __float2bfloat16(ok && L > 0.f ? val / L : 0.f);
       } else {
         const long long row = ((long long)split * a.B + b) * a.Hq + hq;
+        const long long rows = (long long)a.n_split * a.B * a.Hq;
+        if (!in_range(row, rows)) continue;
         a.part_o[row * DHD + d] = ok ? val : 0.f;
         if (d == 0) {
           a.part_ml[row * 2] = ok ? sm.wm[0][g] : -INFINITY;
@@ -351,7 +370,8 @@ __global__ void __launch_bounds__(DHD) decode_combine_kernel(DecArgs a) {
       num += w * a.part_o[r * DHD + d];
     }
   }
-  a.o[(long long)b * a.o_b + (long long)hq * DHD + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+  const long long oi = (long long)b * a.o_b + (long long)hq * DHD + d;
+  if (in_range(oi, a.o_elems)) a.o[oi] = __float2bfloat16(den > 0.f ? num / den : 0.f);
 }
 
 bool make_tmap_cache(CUtensorMap* map, const void* base, int Hk, int L, int B, long long tok_stride,
@@ -401,6 +421,9 @@ cudaError_t decode_attention(const DecodeProblem& p, cudaStream_t stream) {
   a.n_split = max(1, p.n_split);
   const int tiles = (max(p.max_len, 1) + KT - 1) / KT;
   a.tiles_per_split = (tiles + a.n_split - 1) / a.n_split;
+  a.q_elems = p.q_elems;
+  a.o_elems = p.o_elems;
+  if (a.q_elems <= 0 || a.o_elems <= 0) return cudaErrorInvalidValue;
   a.part_o = p.scratch;
   a.part_ml = p.scratch ? p.scratch + (size_t)a.n_split * p.B * p.Hq * DHD : nullptr;
   if (a.n_split > 1 && p.scratch == nullptr) return cudaErrorInvalidValue;

@@ -70,6 +70,7 @@ struct DecodeProblem {
   float scale = 1.f;
   int n_split = 1;
   float* scratch = nullptr;      // decode_scratch_floats(B, Hq, n_split) fp32 when n_split > 1
+  long long q_elems = 0, o_elems = 0;  // extents of the q / o allocations (elements from q / o)
 };
 int decode_splits(int B, int Hk, int max_len, int num_sms);
 size_t decode_scratch_floats(int B, int Hq, int n_split);
