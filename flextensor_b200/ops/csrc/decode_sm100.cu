@@ -8,8 +8,10 @@
 //   * grid = (key split, KV head, sequence); a CTA covers a contiguous run of 64-key tiles of one
 //     sequence's cache for one KV head and all G query heads of that group, so each K/V byte is
 //     read once per group;
-//   * warp 4 (one elected lane) streams K and V tiles with 4-D tensor maps ([B, L, Hk, 128]
-//     cache, 128-byte swizzle, no multicast) into a 6-stage ring guarded by mbarriers;
+//   * warp 4 (one elected lane) streams 32-key K and V tiles with 4-D tensor maps ([B, L, Hk,
+//     128] cache, 128-byte swizzle, no multicast) into mbarrier-guarded stages; every consumer
+//     warp owns two stages of its own, so a stage is only ever waited on by one warp, in order
+//     (a phase-parity wait can then never see a phase two ahead of the one it means);
 //   * warps 0-3 each take every 4th tile: S = Q K^T (K fragments by ldmatrix from the swizzled
 //     tile), an online softmax on the accumulator fragments (row max / sum across the four lanes
 //     of a row by shuffles, exp2 on MUFU), P re-packed in registers as the A operand, and
@@ -34,11 +36,12 @@ FT_DEFINE_ERROR_READER(decode_device_error)
 namespace {
 
 constexpr int DHD = 128;              // head dim
-constexpr int KT = 64;                // keys per tile
-constexpr int DSTAGES = 6;
+constexpr int KT = 32;                // keys per tile
 constexpr int NCW = 4;                // consumer warps
+constexpr int SPW = 2;                // stages per consumer warp
+constexpr int DSTAGES = NCW * SPW;
 constexpr int DTHREADS = 32 * (NCW + 1);
-constexpr int BOX_BYTES = KT * 128;   // one [64 keys x 64 dims] bf16 box (8 KB)
+constexpr int BOX_BYTES = KT * 128;   // one [32 keys x 64 dims] bf16 box (4 KB)
 constexpr int STAGE_BYTES = 4 * BOX_BYTES;  // K (two boxes) + V (two boxes)
 
 struct DecArgs {
@@ -71,8 +74,8 @@ struct DecSmem {
   uint64_t full[DSTAGES], empty[DSTAGES];
 };
 
-// byte offset of 16-byte chunk `c` (0..15 over 128 dims) of row `r` in a [64 x 128] tile stored
-// as two 128-byte-swizzled [64 x 64] boxes
+// byte offset of 16-byte chunk `c` (0..15 over 128 dims) of row `r` in a [32 x 128] tile stored
+// as two 128-byte-swizzled [32 x 64] boxes
 __device__ __forceinline__ uint32_t tile_off(int r, int c) {
   return (uint32_t)((c >> 3) * BOX_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
@@ -141,8 +144,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       uint32_t pend = 0, pph = 0;
       bool ok = true;
       for (int i = 0; i < n_tiles && ok; i++) {
-        const int s = i % DSTAGES;
-        const uint32_t ph = (i / DSTAGES) & 1;
+        const int j = i / NCW;                      // use number of tile i's warp
+        const int s = (i % NCW) * SPW + (j % SPW);  // that warp's stage
+        const uint32_t ph = (j / SPW) & 1;
         if (!mbar_wait(&sm.empty[s], ph ^ 1)) {
           ok = false;
           break;
@@ -193,8 +197,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows r0, r0+8 (l: this lane's part)
     bool ok = true;
     for (int i = warp; i < n_tiles; i += NCW) {
-      const int s = i % DSTAGES;
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.full[s], (i / DSTAGES) & 1));
+      const int j = i / NCW;
+      const int s = warp * SPW + (j % SPW);
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.full[s], (j / SPW) & 1));
       if (ok) {
         const int key0 = (t_begin + i) * KT;
         const int nvalid = min(KT, len - key0);
@@ -208,10 +213,10 @@ __global__ void __launch_bounds__(DTHREADS, 1)
           }
           __syncwarp();
         }
-        // ---- S = Q K^T : 8 n-tiles of 8 keys
-        float sc[8][4];
+        // ---- S = Q K^T : 4 n-tiles of 8 keys
+        float sc[4][4];
 #pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
+        for (int jn = 0; jn < 4; jn++) {
           sc[jn][0] = sc[jn][1] = sc[jn][2] = sc[jn][3] = 0.f;
           const int krow = jn * 8 + (lane & 7);
 #pragma unroll
@@ -225,7 +230,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         // ---- online softmax on the fragments (rows r0: sc[.][0..1], r0+8: sc[.][2..3])
         float tm0 = -INFINITY, tm1 = -INFINITY;
 #pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
+        for (int jn = 0; jn < 4; jn++) {
           const int k = jn * 8 + cq;
 #pragma unroll
           for (int e = 0; e < 2; e++) {
@@ -254,9 +259,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
           o[dn][2] *= al1;
           o[dn][3] *= al1;
         }
-        uint32_t pa[4][4];  // P as A fragments, one per 16-key k-step
+        uint32_t pa[2][4];  // P as A fragments, one per 16-key k-step
 #pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
+        for (int jn = 0; jn < 4; jn++) {
           const float p0 = ex2f(sc[jn][0] - s0), p1 = ex2f(sc[jn][1] - s0);
           const float p2 = ex2f(sc[jn][2] - s1), p3 = ex2f(sc[jn][3] - s1);
           l0 += p0 + p1;
@@ -264,9 +269,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
           pa[jn >> 1][(jn & 1) * 2 + 0] = pack_bf16x2(p0, p1);
           pa[jn >> 1][(jn & 1) * 2 + 1] = pack_bf16x2(p2, p3);
         }
-        // ---- O += P V : 16 n-tiles of 8 dims, 4 k-steps of 16 keys
+        // ---- O += P V : 16 n-tiles of 8 dims, 2 k-steps of 16 keys
 #pragma unroll
-        for (int kp = 0; kp < 4; kp++) {
+        for (int kp = 0; kp < 2; kp++) {
           const int vrow = kp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
           for (int dp = 0; dp < 8; dp++) {  // dim n-tile pairs 2dp, 2dp+1
@@ -309,7 +314,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       L1 += mw1 == -INFINITY ? 0.f : ex2f(mw1 - M1) * sm.wl[w][r0 + 8];
     }
     // every warp's O, weighted, summed through shared memory: red[row][dim] fp32 (8 KB), reusing
-    // stage 0 (all loads of this CTA landed and were consumed)
+    // stages 0-1 (all loads of this CTA landed and were consumed)
     float* red = reinterpret_cast<float*>(sm.stage[0]);
     for (int e = tid; e < 16 * DHD; e += 32 * NCW) red[e] = 0.f;
     asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
