@@ -194,6 +194,9 @@ class FlexTensorOffloadWorker(Worker):
         if kwargs.get("load_dummy_weights"):
             raise FlexTensorWorkerError("load_dummy_weights=True is not supported")
         _validate(self.vllm_config, cfg)
+        from flextensor_b200.contrib.vllm.graph_join import install_segment_join
+
+        install_segment_join()  # copy stream joined at every eager break of a graph capture
         inc, exc = resolve_vllm_patterns(cfg)
         from vllm.config import CompilationMode, CUDAGraphMode
 
