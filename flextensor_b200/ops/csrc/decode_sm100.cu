@@ -313,18 +313,17 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       L0 += mw0 == -INFINITY ? 0.f : ex2f(mw0 - M0) * sm.wl[w][r0];
       L1 += mw1 == -INFINITY ? 0.f : ex2f(mw1 - M1) * sm.wl[w][r0 + 8];
     }
-    // every warp's O, weighted, summed through shared memory: red[row][dim] fp32 (8 KB), reusing
-    // stages 0-1 (all loads of this CTA landed and were consumed)
+    // every warp's weighted O into its own slice red[warp][row][dim] (fp32, 8 KB per warp, in the
+    // idle K/V stages: every load of this CTA landed and was consumed), rows >= G skipped; then
+    // each output element is the sum of the four slices
     float* red = reinterpret_cast<float*>(sm.stage[0]);
-    for (int e = tid; e < 16 * DHD; e += 32 * NCW) red[e] = 0.f;
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
+    float* mine = red + warp * 16 * DHD;
+    const bool w0 = r0 < a.G, w1 = r0 + 8 < a.G;
 #pragma unroll
     for (int dn = 0; dn < 16; dn++) {
       const int d = dn * 8 + cq;
-      atomicAdd(&red[r0 * DHD + d], o[dn][0] * f0);
-      atomicAdd(&red[r0 * DHD + d + 1], o[dn][1] * f0);
-      atomicAdd(&red[(r0 + 8) * DHD + d], o[dn][2] * f1);
-      atomicAdd(&red[(r0 + 8) * DHD + d + 1], o[dn][3] * f1);
+      if (w0) *reinterpret_cast<float2*>(&mine[r0 * DHD + d]) = make_float2(o[dn][0] * f0, o[dn][1] * f0);
+      if (w1) *reinterpret_cast<float2*>(&mine[(r0 + 8) * DHD + d]) = make_float2(o[dn][2] * f1, o[dn][3] * f1);
     }
     asm volatile("bar.sync 1, %0;" ::"n"(32 * NCW) : "memory");
     if (warp == 0 && (lane & 3) == 0) {  // the merged row statistics (every warp read wm/wl above)
@@ -337,7 +336,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     for (int e = tid; e < a.G * DHD; e += 32 * NCW) {
       const int g = e / DHD, d = e % DHD;
       const int hq = hk * a.G + g;
-      const float val = red[g * DHD + d];
+      float val = 0.f;
+#pragma unroll
+      for (int w = 0; w < NCW; w++) val += red[(w * 16 + g) * DHD + d];
       if (a.n_split == 1) {
         const float L = sm.wl[0][g];
         const long long oi = (long long)b * a.o_b + (long long)hq * DHD + d;
@@ -390,8 +391,8 @@ bool make_tmap_cache(CUtensorMap* map, const void* base, int Hk, int L, int B, l
 int decode_splits(int B, int Hk, int max_len, int num_sms) {
   const int tiles = (max(max_len, 1) + KT - 1) / KT;
   const int base = max(1, B * Hk);
-  int n = (4 * max(num_sms, 1) + base - 1) / base;  // about four CTAs' worth of work per SM
-  n = max(1, min(n, tiles / NCW));                    // at least one tile per consumer warp
+  int n = (2 * max(num_sms, 1) + base - 1) / base;  // about two waves of CTAs
+  n = max(1, min(n, tiles / (4 * NCW)));              // at least four tiles per consumer warp
   return n;
 }
 
