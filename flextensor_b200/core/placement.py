@@ -63,23 +63,23 @@ class ModelPlacementState:
     @classmethod
     def from_dict(cls, data: dict[str, Any]) -> "ModelPlacementState":
         if not isinstance(data, dict):
-            raise ValueError("Model placement state must be a dictionary")
+            raise ValueError("a saved placement must be a JSON object")
         if data.get("version") != SCHEMA_VERSION:
             raise ValueError(f"Unsupported model placement schema version {data.get('version')!r}; "
                              f"expected {SCHEMA_VERSION}")
         trows, srows = data.get("tensors"), data.get("storages")
         if not isinstance(trows, list) or not isinstance(srows, list):
-            raise ValueError("Model placement state tensors and storages must be lists")
+            raise ValueError("placement 'tensors' and 'storages' must both be lists")
         if any(not isinstance(r, dict) or not isinstance(r.get("names"), list) for r in trows):
-            raise ValueError("Each tensor entry must be a dictionary with a names list")
+            raise ValueError("every tensor record needs to be an object carrying a 'names' list")
         if any(not isinstance(r, dict) for r in srows):
-            raise ValueError("Each storage entry must be a dictionary")
+            raise ValueError("every storage record needs to be an object")
         try:
             tensors = tuple(TensorState(r["id"], tuple(r["names"]), r["storage_id"], r["logical_bytes"], r["kind"])
                             for r in trows)
             storages = tuple(StorageState(r["id"], r["device"], r["nbytes"], r["pinned"]) for r in srows)
         except (KeyError, TypeError) as e:
-            raise ValueError(f"Invalid model placement state entry: {e}") from e
+            raise ValueError(f"malformed placement record: {e}") from e
         st = cls(tensors=tensors, storages=storages)
         validate_state(st)
         return st
@@ -136,7 +136,7 @@ def _nonneg_int(v: object) -> bool:
 def _check_device(d: object) -> None:
     ok = d == "cpu" or (isinstance(d, str) and d.startswith("cuda:") and d[5:].isdigit())
     if not ok:
-        raise ValueError(f"Unsupported device {d!r}; expected 'cpu' or an explicit CUDA device")
+        raise ValueError(f"device {d!r} is neither 'cpu' nor a CUDA device with an index")
 
 
 def validate_state(st: ModelPlacementState) -> None:
@@ -148,35 +148,35 @@ def validate_state(st: ModelPlacementState) -> None:
     used: set[str] = set()
     for t in st.tensors:
         if not isinstance(t.id, str) or not t.id or t.id in seen_ids:
-            raise ValueError(f"Tensor IDs must be unique non-empty strings: {t.id!r}")
+            raise ValueError(f"tensor id {t.id!r} is empty or repeated")
         seen_ids.add(t.id)
         if not isinstance(t.names, tuple) or any(not isinstance(n, str) or not n for n in t.names):
-            raise ValueError(f"Tensor {t.id!r} names must be non-empty strings")
+            raise ValueError(f"tensor {t.id!r} lists an empty or non-string name")
         dup = seen_names.intersection(t.names)
         if dup or len(set(t.names)) != len(t.names):
-            raise ValueError(f"Tensor names must be unique: {sorted(dup or set(t.names))}")
+            raise ValueError(f"a tensor name appears more than once: {sorted(dup or set(t.names))}")
         seen_names.update(t.names)
         if not isinstance(t.storage_id, str) or not t.storage_id:
-            raise ValueError(f"Tensor {t.id!r} has an invalid storage ID")
+            raise ValueError(f"tensor {t.id!r} points at no valid storage")
         used.add(t.storage_id)
         if not _nonneg_int(t.logical_bytes):
-            raise ValueError(f"Tensor {t.id!r} logical_bytes must be a non-negative integer")
+            raise ValueError(f"tensor {t.id!r}: logical_bytes has to be an int >= 0")
         if not isinstance(t.kind, str) or not t.kind:
-            raise ValueError(f"Tensor {t.id!r} kind must be a non-empty string")
+            raise ValueError(f"tensor {t.id!r}: kind is missing")
     sids: set[str] = set()
     for s in st.storages:
         if not isinstance(s.id, str) or not s.id or s.id in sids:
-            raise ValueError(f"Storage IDs must be unique non-empty strings: {s.id!r}")
+            raise ValueError(f"storage id {s.id!r} is empty or repeated")
         sids.add(s.id)
         _check_device(s.device)
         if not _nonneg_int(s.nbytes):
-            raise ValueError(f"Storage {s.id!r} nbytes must be a non-negative integer")
+            raise ValueError(f"storage {s.id!r}: nbytes has to be an int >= 0")
         if type(s.pinned) is not bool:
-            raise ValueError(f"Storage {s.id!r} pinned must be a boolean")
+            raise ValueError(f"storage {s.id!r}: pinned has to be true or false")
         if s.pinned and s.device != "cpu":
-            raise ValueError(f"Storage {s.id!r} cannot be pinned on {s.device}")
+            raise ValueError(f"storage {s.id!r} is on {s.device}, which cannot be pinned")
     if used != sids:
-        raise ValueError(f"Storage inventory must exactly match tensor references: missing={sorted(used - sids)}, "
+        raise ValueError(f"storages and tensor references do not exactly match: missing={sorted(used - sids)}, "
                          f"unreferenced={sorted(sids - used)}")
 
 
@@ -185,36 +185,36 @@ def _check_transition(cur: ModelPlacementState, tgt: ModelPlacementState, spec: 
     validate_state(cur)
     validate_state(tgt)
     if {t.id: t for t in cur.tensors} != {t.id: t for t in tgt.tensors}:
-        raise ValueError("Current and target tensor inventory must match; only storage placement may change")
+        raise ValueError("the two states hold different tensors; a transition may only move storages")
     cs, ts = {s.id: s for s in cur.storages}, {s.id: s for s in tgt.storages}
     if cs.keys() != ts.keys():
-        raise ValueError("Current and target storage inventory must match")
+        raise ValueError("the two states hold different storages")
     for sid, c in cs.items():
         t = ts[sid]
         if c.nbytes != t.nbytes:
-            raise ValueError(f"Storage {sid!r} size differs between current and target state")
+            raise ValueError(f"storage {sid!r} changes size between the two states")
         if c.pinned and c.device == t.device and not t.pinned:
-            raise ValueError(f"Unpinning storage {sid!r} is unsupported")
+            raise ValueError(f"storage {sid!r} would lose its pinning, which transitions never do")
         if c.device != t.device and c.device.startswith("cuda:") and t.device.startswith("cuda:"):
             raise ValueError(f"Cross-device CUDA migration is not modeled by this planner: {c.device} -> {t.device}")
     gpus = {s.device for st in (cur, tgt) for s in st.storages if s.device != "cpu"}
     if len(gpus) > 1:
-        raise ValueError(f"Capacity accounting across multiple CUDA devices is unsupported: {sorted(gpus)}")
+        raise ValueError(f"the capacity check covers one CUDA device, these states use {sorted(gpus)}")
     counts = [cap.host_bytes, cap.gpu_bytes, spec.extra_gpu_bytes]
     counts += [a.nbytes for a in spec.host_allocations] + [a.temporary_copy_bytes for a in spec.host_allocations]
     if not all(_nonneg_int(v) for v in counts):
-        raise ValueError("Capacity and transition byte counts must be non-negative integers")
+        raise ValueError("capacities and byte counts have to be ints >= 0")
     pin_ids = set(spec.pinning_copy_storage_ids)
     if len(pin_ids) != len(spec.pinning_copy_storage_ids):
-        raise ValueError("pinning_copy_storage_ids must be unique")
+        raise ValueError("pinning_copy_storage_ids repeats an id")
     newly_pinned = {sid for sid, c in cs.items() if not c.pinned and ts[sid].pinned}
     if not pin_ids <= newly_pinned:
-        raise ValueError("Pinning-copy storage IDs must refer to newly pinned target storages")
+        raise ValueError("pinning_copy_storage_ids may only name storages the target state newly pins")
     rel = set(spec.release_host_storage_ids)
     if len(rel) != len(spec.release_host_storage_ids) or not rel <= ts.keys():
-        raise ValueError("release_host_storage_ids must contain unique known storage IDs")
+        raise ValueError("release_host_storage_ids repeats an id or names an unknown storage")
     if any(ts[sid].device != "cpu" for sid in rel):
-        raise ValueError("Only target host storages can be released during loader construction")
+        raise ValueError("only host storages of the target state can be released while the loader is built")
     return cs, ts
 
 
@@ -242,7 +242,7 @@ def _exhaustive_order(ms: tuple[StorageMigration, ...], cap: MemoryCapacity,
                 return [ms[i] for i in order]
             continue
         if len(seen) >= SEARCH_STATE_LIMIT:
-            raise RuntimeError(f"Capacity-safe migration ordering search exceeded {SEARCH_STATE_LIMIT} states")
+            raise RuntimeError(f"no capacity-safe move order found within {SEARCH_STATE_LIMIT} search states")
         for i, m in enumerate(ms):
             bit = 1 << i
             if not left & bit:
@@ -337,7 +337,7 @@ def _reachable_tensors(model: torch.nn.Module) -> dict[int, torch.Tensor]:
 
 def _storage_key(name: str, t: torch.Tensor) -> tuple[str, int, int, bool]:
     if t.is_meta:
-        raise ValueError(f"Cannot capture meta tensor {name}")
+        raise ValueError(f"{name} is a meta tensor: nothing to capture")
     if t.device.type not in ("cpu", "cuda"):
         raise ValueError(f"Cannot capture tensor {name} on unsupported device {t.device}")
     if t.layout != torch.strided:
@@ -346,7 +346,7 @@ def _storage_key(name: str, t: torch.Tensor) -> tuple[str, int, int, bool]:
     try:
         st = t.untyped_storage()
     except (NotImplementedError, RuntimeError) as e:
-        raise ValueError(f"Cannot inspect backing storage for tensor {name}") from e
+        raise ValueError(f"the storage behind {name} cannot be read") from e
     dev = f"cuda:{t.device.index if t.device.index is not None else torch.cuda.current_device()}" \
         if t.device.type == "cuda" else "cpu"
     return dev, st._cdata, st.nbytes(), bool(t.device.type == "cpu" and t.is_pinned())  # noqa: SLF001
