@@ -94,6 +94,12 @@ struct CpArgs {
   int pieces_per_part, pieces_per_batch, batches;
 };
 
+__device__ __forceinline__ unsigned long long f2pack_early(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -114,6 +120,30 @@ __device__ __forceinline__ float exp2_fma(float x) {
   const int ri = __float_as_int(t) - 0x4B400000;
   const float y = __int_as_float(__float_as_int(p) + (ri << 23));
   return x <= -126.f ? 0.f : y;
+}
+
+// exp2 of a PAIR on the FMA pipe with packed fp32x2 arithmetic (same reduction and cubic as
+// exp2_fma): the magic add leaves r in the low mantissa bits of t, so (bits(t) << 23) is r in the
+// exponent field (the magic constant's own bits shift out of the 32-bit word), and 2^r * p is one
+// integer add per element.
+__device__ __forceinline__ unsigned long long exp2_fma2(float x0, float x1) {
+  const unsigned long long xc = f2pack_early(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  unsigned long long t, r, f, p;
+  const unsigned long long magic = f2pack_early(12582912.f, 12582912.f);
+  const unsigned long long nmagic = f2pack_early(-12582912.f, -12582912.f);
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(xc), "l"(magic));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(t), "l"(nmagic));
+  const unsigned long long neg1 = f2pack_early(-1.f, -1.f);
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(f) : "l"(r), "l"(neg1), "l"(xc));
+  const unsigned long long c3 = f2pack_early(0.05517098f, 0.05517098f), c2 = f2pack_early(0.24260971f, 0.24260971f);
+  const unsigned long long c1 = f2pack_early(0.69326097f, 0.69326097f), c0 = f2pack_early(0.99992818f, 0.99992818f);
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(c3), "l"(f), "l"(c2));
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(p) : "l"(f), "l"(c1));
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(p) : "l"(f), "l"(c0));
+  const uint32_t t0 = (uint32_t)t, t1 = (uint32_t)(t >> 32);
+  const uint32_t y0 = (uint32_t)p + (t0 << 23), y1 = (uint32_t)(p >> 32) + (t1 << 23);
+  const uint32_t z0 = x0 <= -126.f ? 0u : y0, z1 = x1 <= -126.f ? 0u : y1;
+  return ((unsigned long long)z1 << 32) | z0;
 }
 
 // Registers written by an asynchronous tcgen05.ld are only valid after tcgen05.wait::ld; this
@@ -612,8 +642,9 @@ __global__ void __launch_bounds__(CP ? NTHREADS_CP : NTHREADS, 1)
           f2unpack(x2, x0, x1);
           float p0, p1;
           if (emu_pair<EMU>(i)) {  // EMU pairs in 8 on the FMA pipe
-            p0 = exp2_fma(x0);
-            p1 = exp2_fma(x1);
+            const unsigned long long e2 = exp2_fma2(x0, x1);
+            p0 = __uint_as_float((uint32_t)e2);
+            p1 = __uint_as_float((uint32_t)(e2 >> 32));
           } else {
             p0 = ex2(x0);
             p1 = ex2(x1);
@@ -946,8 +977,9 @@ __global__ void __launch_bounds__(NTHREADS1, 1)
           f2unpack(x2, x0, x1);
           float p0, p1;
           if (emu_pair<EMU>(i)) {
-            p0 = exp2_fma(x0);
-            p1 = exp2_fma(x1);
+            const unsigned long long e2 = exp2_fma2(x0, x1);
+            p0 = __uint_as_float((uint32_t)e2);
+            p1 = __uint_as_float((uint32_t)(e2 >> 32));
           } else {
             p0 = ex2(x0);
             p1 = ex2(x1);
@@ -1315,8 +1347,9 @@ __global__ void __launch_bounds__(NTHREADS2X, 1)
           f2unpack(x2, x0, x1);
           float p0, p1;
           if (emu_pair<EMU>(i)) {
-            p0 = exp2_fma(x0);
-            p1 = exp2_fma(x1);
+            const unsigned long long e2 = exp2_fma2(x0, x1);
+            p0 = __uint_as_float((uint32_t)e2);
+            p1 = __uint_as_float((uint32_t)(e2 >> 32));
           } else {
             p0 = ex2(x0);
             p1 = ex2(x1);
@@ -1656,8 +1689,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           f2unpack(x2, x0, x1);
           float p0, p1;
           if (emu_pair<EMU>(i)) {
-            p0 = exp2_fma(x0);
-            p1 = exp2_fma(x1);
+            const unsigned long long e2 = exp2_fma2(x0, x1);
+            p0 = __uint_as_float((uint32_t)e2);
+            p1 = __uint_as_float((uint32_t)(e2 >> 32));
           } else {
             p0 = ex2(x0);
             p1 = ex2(x1);

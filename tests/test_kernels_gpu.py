@@ -226,7 +226,7 @@ def test_attention_one_tile_kernel(mode, B, Sq, Sk, H, Hk, causal):
     assert rel_err(o, ops.attention(q, k, v, causal=causal)) < 1e-2
 
 
-@pytest.mark.parametrize("mode", [300, 301, 302, 400, 401, 402])
+@pytest.mark.parametrize("mode", [100, 102, 103, 104, 300, 301, 302, 400, 401, 402])
 @pytest.mark.parametrize("B,Sq,Sk,H,Hk,causal", [(1, 128, 128, 1, 1, False), (2, 300, 300, 4, 4, False),
                                                  (1, 384, 1000, 8, 2, False), (2, 500, 500, 4, 4, True),
                                                  (1, 1024, 2048, 2, 1, False)])
