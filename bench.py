@@ -46,7 +46,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=40, help="(testing only) fewer blocks; invalid for the headline")
     ap.add_argument("--profiling-iters", type=int, default=3)
     ap.add_argument("--placement", choices=["auto", "pinned_arena", "device", "pageable"], default="auto",
-                    help="where the weights start before offload() (auto: pinned arena at N=1, device at N>1)")
+                    help="where the weights start before offload() (auto: pinned arena at N=1; at N>1 device "
+                         "for ours, pageable for the reference)")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -143,6 +144,24 @@ def barrier(pg):
 
 
 # ----------------------------------------------------------------------------- model + runtime per arm
+def to_pageable(model) -> None:
+    """Move every parameter and buffer to its own pageable host tensor (a model loaded on the CPU).
+
+    The reference arm starts here on several GPUs: its runtime stops with "Block data not
+    available" when the weights start on the device (observed on B200), and a pinned arena per
+    rank would be a second whole host copy of the model beside the one its runtime pins."""
+    import torch
+
+    with torch.no_grad():
+        for p in model.parameters():
+            p.data = p.data.cpu()
+        for _, b in model.named_buffers():
+            b.data = b.data.cpu()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
 def build_model(impl: str, layers: int, device, seed: int, placement: str = "pinned_arena"):
     """Random-init Wan-14B-shape DiT (initialised on the GPU, then placed).
 
@@ -177,12 +196,8 @@ def build_model(impl: str, layers: int, device, seed: int, placement: str = "pin
     model = model.to_empty(device=device).to(torch.bfloat16)
     init(model, seed=seed)
     if placement in ("device", "pageable"):
-        with torch.no_grad():
-            if placement == "pageable":
-                for p in model.parameters():
-                    p.data = p.data.cpu()
-                for _, b in model.named_buffers():
-                    b.data = b.data.cpu()
+        if placement == "pageable":
+            to_pageable(model)
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         model.eval()
@@ -339,7 +354,9 @@ def main():
         enable_striped_streaming()
     placement = args.placement
     if placement == "auto":
-        placement = "pinned_arena" if world == 1 else "device"
+        # one process: a pinned arena (a loaded checkpoint); several: ours keeps the weights on
+        # its GPU and packs only its stripe, the reference starts from pageable host tensors
+        placement = "pinned_arena" if world == 1 else ("device" if args.impl == "ours" else "pageable")
 
     if args.impl == "reference" and world > 1:
         # The reference keeps a whole pinned copy of its offloaded weights in every process.

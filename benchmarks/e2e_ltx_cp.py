@@ -60,6 +60,8 @@ def build(impl: str, layers: int, device, world: int):
         init = init_params_
     model = model.to_empty(device=device).to(torch.bfloat16)
     init(model, seed=0)
+    if impl == "reference":
+        bench.to_pageable(model)
     model.eval()
     model.requires_grad_(False)
     return model, cfg

@@ -88,6 +88,7 @@ def main():
             model = MixtralEP(cfg, rank, world, layers=a.layers)
         model = model.to_empty(device=dev).to(torch.bfloat16)
         init_params_(model, seed=rank)
+        bench.to_pageable(model)
         cos, sin = rope_cos_sin(PROMPT + NEW, cfg.head_dim, cfg.rope_theta, dev)
         ep = {}
 

@@ -117,6 +117,13 @@ class OffloadConfig(BaseModel):
     profile_mode: ProfileMode = Field(default="view")
     """Profiling mechanism: ``view`` (slot views), ``getter`` (property getters) or ``torch_function``."""
 
+    # ---- fields beyond the reference schema
+    hold_device_weights: bool = Field(default=True)
+    """Unit weights that already sit on the compute device stay there through discovery and
+    profiling and are packed device -> pinned arena once the plan exists (no per-tensor host copy).
+    ``False`` moves them to pinned host memory at warm-up, which frees device memory for the
+    profiling passes."""
+
     model_config = {"arbitrary_types_allowed": True, "use_attribute_docstrings": True}
 
     @field_validator("include_patterns", "exclude_patterns", mode="before")

@@ -216,7 +216,7 @@ def pack_tensors(label: str, items: list[tuple[int, str, torch.Tensor]], buffer:
     for (tid, name, t), off, n in zip(items, offs, sizes):
         e = PackedEntry(tid, name, off, n, t.dtype, tuple(t.shape))
         if n:
-            blk.view(e).copy_(t.detach().to("cpu"))
+            blk.view(e).copy_(t.detach())  # a device source is copied straight into the block
         blk.entries.append(e)
         if release_sources is not None:
             release_sources(tid)

@@ -24,11 +24,14 @@ def available_bytes(device: torch.device) -> tuple[int, int]:
     return int(total), int(free + max(0, cached_unused))
 
 
-def resolve_gpu_budget(device: torch.device, fraction: float, strategy_invisible_bytes: int = 0) -> int:
+def resolve_gpu_budget(device: torch.device, fraction: float, strategy_invisible_bytes: int = 0,
+                       reclaimable_bytes: int = 0) -> int:
+    """``reclaimable_bytes``: unit weights still held on the device that the plan may stream
+    (they are freed once packed), so they count as obtainable."""
     if not (0.0 < fraction <= 1.0):
         raise ValueError(f"max_gpu_mem_fraction must be in (0, 1], got {fraction}")
     total, obtainable = available_bytes(torch.device(device))
-    budget = min(int(total * fraction), obtainable + int(strategy_invisible_bytes))
+    budget = min(int(total * fraction), obtainable + int(strategy_invisible_bytes) + int(reclaimable_bytes))
     budget = max(budget, MIN_BUDGET)
     return max(MIN_BUDGET, budget - int(strategy_invisible_bytes))
 

@@ -188,7 +188,8 @@ class OffloadManager:
         return TensorManager(
             dev, resolve_load_strategy(c), loader_type=c.transfer_mode, blocks=c.num_blocks,
             pinned_memory=c.pinned_memory, pinned_memory_mode=c.pinned_memory_mode, profile_mode=c.profile_mode,
-            max_gpu_mem_fraction=c.max_gpu_mem_fraction, offload_timing=c.offload_timing,
+            max_gpu_mem_fraction=c.max_gpu_mem_fraction, hold_device_weights=c.hold_device_weights,
+            offload_timing=c.offload_timing,
             enable_diagnostics=c.enable_diagnostics, shm_store=shm_store, piecewise_prefetch=c.piecewise_prefetch)
 
     def get_tensor_manager(self) -> TensorManager | None:

@@ -73,6 +73,12 @@ class _ForeignReadMode(TorchFunctionMode):
         self.cache: dict[int, torch.Tensor] = {}
 
     def _swap(self, x):
+        if isinstance(x, torch.Tensor) and self.tm._held_ptr_to_tid and x.device == self.tm.device:
+            # a device-held weight is read in place; a read from another unit's trap is recorded
+            tid = self.tm._held_ptr_to_tid.get(x.data_ptr())
+            if tid is not None and self.tm.owner.get(tid) != self.label:
+                self.tm._foreign_reads.setdefault(tid, set()).add(self.label)
+            return x
         if isinstance(x, torch.Tensor) and x.device.type == "cpu" and self.tm.device.type != "cpu":
             tid = self.tm._host_ptr_to_tid.get(x.data_ptr())
             if tid is not None:
@@ -112,6 +118,7 @@ class TensorManager:
         pinned_memory_mode: str = "torch",
         profile_mode: str = "view",
         max_gpu_mem_fraction: float | None = None,
+        hold_device_weights: bool = True,
         offload_timing: str = "off",
         enable_diagnostics: bool = False,
         shm_store: Any = None,
@@ -136,6 +143,7 @@ class TensorManager:
         self.pinner = make_host_pinner(self.pinned_memory, pinned_memory_mode)
         self.profile_mode = profile_mode
         self.max_gpu_mem_fraction = max_gpu_mem_fraction
+        self.hold_device_weights = hold_device_weights
         self.offload_timing = offload_timing
         self.enable_diagnostics = enable_diagnostics
         self.shm_store = shm_store
@@ -154,6 +162,7 @@ class TensorManager:
         self.unit_tids: dict[str, list[int]] = {}
         self.host: dict[int, torch.Tensor] = {}        # offloadable tid -> host tensor
         self._host_ptr_to_tid: dict[int, int] = {}
+        self._held_ptr_to_tid: dict[int, int] = {}     # device-held unit weights (see warmup)
         self.resident: set[int] = set()                # tids permanently on device
         self._foreign_reads: dict[int, set[str]] = {}
         self.collector = IterativeLayerStatisticsCollector()
@@ -217,6 +226,22 @@ class TensorManager:
         self.host[tid] = t
         self._host_ptr_to_tid[t.data_ptr()] = tid
 
+    def _hold(self, tid: int) -> None:
+        """Keep a unit weight that starts on the compute device where it is until the plan exists.
+
+        Discovery and profiling then read it in place, and the plan's streamed weights are
+        packed straight from the device into the pinned arena (or this rank's stripe of it),
+        so the host never holds a second, per-tensor copy of the model. The bytes count as
+        obtainable in the memory-mode budget, since every streamed weight is freed after packing."""
+        p = self.params_by_tid[tid]
+        self._orig_device.setdefault(tid, p.device)
+        p.requires_grad_(False)
+        self.host[tid] = p.data
+        self._held_ptr_to_tid[p.data.data_ptr()] = tid
+
+    def _held_bytes(self) -> int:
+        return sum(tensor_nbytes(h) for h in self.host.values() if h.device == self.device)
+
     def _to_device(self, tid: int) -> None:
         p = self.params_by_tid[tid]
         self._orig_device.setdefault(tid, p.device)
@@ -226,6 +251,7 @@ class TensorManager:
         old = self.host.pop(tid, None)
         if old is not None:
             self._host_ptr_to_tid.pop(old.data_ptr(), None)
+            self._held_ptr_to_tid.pop(old.data_ptr(), None)
 
     def _move_non_unit_to_device(self) -> None:
         for tid in self.params_by_tid:
@@ -287,13 +313,9 @@ class TensorManager:
                 if keep_on_device is not None and tid in keep_on_device:
                     self._to_device(tid)
                     continue
-                if self._stripe is not None and p.device == self.device:
-                    # Striped streaming: the host keeps only this rank's stripe of each packed
-                    # block, so weights that start on the device stay there until the plan is
-                    # built and are then packed stripe by stripe (no full host copy per rank).
-                    self._orig_device.setdefault(tid, p.device)
-                    p.requires_grad_(False)
-                    self.host[tid] = p.data
+                if p.device == self.device and self.device.type == "cuda" and (
+                        self._stripe is not None or self.hold_device_weights):
+                    self._hold(tid)
                     continue
                 self._to_host(tid)
             self._move_non_unit_to_device()
@@ -538,7 +560,8 @@ class TensorManager:
 
         invisible = sum(tensor_nbytes(self.params_by_tid[t].data) for t in self.resident if t not in self.owner)
         invisible += sum(b.numel() * b.element_size() for b in self.model.buffers())
-        return resolve_gpu_budget(self.device, self.max_gpu_mem_fraction, invisible)
+        return resolve_gpu_budget(self.device, self.max_gpu_mem_fraction, invisible,
+                                  reclaimable_bytes=self._held_bytes())
 
     def initialize_inference(self) -> nn.Module:
         self._staging = None
@@ -623,6 +646,12 @@ class TensorManager:
         self.unmapped_bytes = sum(tensor_nbytes(self.params_by_tid[t].data) for t in self.resident)
         idx = {l: i for i, l in enumerate(order)}
         if self.loader_type == "strategy":
+            for tid in streamed:  # the per-tensor loader streams from pinned host copies
+                if self.host[tid].device == self.device:
+                    self._held_ptr_to_tid.pop(self.host[tid].data_ptr(), None)
+                    self._to_host(tid)
+            if self.device.type == "cuda":
+                torch.cuda.empty_cache()
             self.loader = TensorStrategyLoader(self.device, order, load, {k: t2c[k] for k in load}, dict(self.host),
                                                self.params_by_tid)
             self.loader.bind(self.params_by_tid)
@@ -674,6 +703,7 @@ class TensorManager:
                                    release_sources=self._release_host)
                 arena_off += sz
                 host_blocks[label] = blk
+                self._rebind_to_block(blk)
                 continue
             buf = (self.shm_store.block_buffer(label, items, must_exist=self.load_from_shm)
                    if self.shm_store is not None else None)
@@ -686,6 +716,7 @@ class TensorManager:
             else:
                 blk = pack_tensors(label, items, buffer=buf, pinned=self.pinned_memory,
                                    release_sources=self._release_host)
+                self._rebind_to_block(blk)
             host_blocks[label] = blk
         slot_of = {l: l2b.get(l, i % max(2, self.blocks)) for i, l in enumerate(host_blocks)}
         slot_bytes: dict[int, int] = {}
@@ -709,8 +740,12 @@ class TensorManager:
         self.loader = BlockLoader(self.device, plan, engine, timing=self.timing,
                                   prefetch_policy=PiecewisePrefetchPolicy.from_mode(self.piecewise_prefetch))
         self.loader.bind(self.params_by_tid, setter=self._set_param)
-        if stripe is not None:
-            torch.cuda.empty_cache()  # the device copies that were packed into stripes are free now
+        if self.device.type == "cuda":
+            # the per-tensor sources that were packed are free now: device-held weights go back
+            # to the device allocator, per-tensor pinned copies to the pinned host cache
+            torch.cuda.empty_cache()
+            if self.pinned_memory and hasattr(torch._C, "_host_emptyCache"):
+                torch._C._host_emptyCache()
         self.loader.preload()
         self.phase = TMPhase.INFERENCE
 
@@ -737,6 +772,22 @@ class TensorManager:
         old = self.host.get(tid)
         if old is not None:
             self._host_ptr_to_tid.pop(old.data_ptr(), None)
+            self._held_ptr_to_tid.pop(old.data_ptr(), None)
+
+    def _rebind_to_block(self, blk: HostBlock) -> None:
+        """Point each packed tensor's host entry and parameter at its bytes in ``blk``.
+
+        The per-tensor source (a pinned host copy or a device-held weight) then has no
+        reference left and is freed; one in-place ``cudaHostRegister`` is undone first."""
+        for e in blk.entries:
+            old = self.host.get(e.tensor_id)
+            v = blk.view(e)
+            if old is not None and old.device.type == "cpu" and old.data_ptr() != v.data_ptr():
+                self.pinner.registry.release(old.data_ptr())
+            self.host[e.tensor_id] = v
+            p = self.params_by_tid[e.tensor_id]
+            if not p.is_meta:
+                p.data = v
 
     # ================================================================== state / profile
     def export_state(self) -> TensorManagerState:
@@ -929,4 +980,5 @@ class TensorManager:
             self.shm_store.close(unlink=not self.load_from_shm)
         self.host.clear()
         self._host_ptr_to_tid.clear()
+        self._held_ptr_to_tid.clear()
         self.phase = TMPhase.NONE

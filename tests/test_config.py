@@ -13,7 +13,9 @@ def test_defaults_match_reference_schema():
         "transfer_budget_scale", "transfer_mode", "num_blocks", "min_blocks", "max_gpu_mem_fraction",
         "profile_storage_dir", "profile_read_only", "load_strategy", "enable_instrumentation",
         "instrumentation_output_dir", "offload_timing", "piecewise_prefetch", "include_patterns", "exclude_patterns",
-        "enable_diagnostics", "profile_mode"]
+        "enable_diagnostics", "profile_mode",
+        # beyond the reference schema
+        "hold_device_weights"]
     assert (c.enabled, c.gpu_device, c.pinned_memory, c.pinned_memory_mode) == (True, 0, True, "torch")
     assert (c.shm_enabled, c.shm_namespace, c.shm_wait_timeout) == (False, None, 0.0)
     assert (c.discovery_iters, c.skip_discovery, c.profiling_iters, c.external_compile) == (1, False, 10, False)
@@ -25,6 +27,7 @@ def test_defaults_match_reference_schema():
     assert (c.offload_timing, c.piecewise_prefetch) == ("off", "warn")
     assert c.include_patterns == ["*"] and c.exclude_patterns == []
     assert not c.enable_diagnostics and c.profile_mode == "view"
+    assert c.hold_device_weights
 
 
 @pytest.mark.parametrize("kw", [dict(num_blocks=2, min_blocks=3), dict(shm_enabled=True),

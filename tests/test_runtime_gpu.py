@@ -144,3 +144,71 @@ def test_state_adoption_into_gpu_loaded_model():
     tm = tm_plan.get_tensor_manager()
     assert all(p.device == DEV for t, p in tm.params_by_tid.items() if names[t] not in streamed)
     ft.release("adopt")
+
+
+@pytest.mark.parametrize("hold", [True, False])
+def test_device_start_model_keeps_one_host_copy(hold):
+    """A model that starts on the GPU: after planning, every streamed weight's host bytes are its
+    view in the packed pinned arena (no per-tensor host copy stays alive beside it)."""
+    m, inp = tiny()
+    m = m.to(DEV)
+    with torch.no_grad():
+        want = tiny()[0].to(DEV)(*inp)
+    om = ft.get_offload_manager()
+    mm = om.offload(m, cfg(hold_device_weights=hold))
+    with torch.no_grad():
+        for _ in range(4):
+            assert torch.equal(mm(*inp), want)
+    tm = om.get_tensor_manager()
+    spans = [(b.data.data_ptr(), b.data.data_ptr() + b.data.numel()) for b in tm.loader.plan.host_blocks.values()]
+    assert tm.host
+    for h in tm.host.values():
+        assert h.device.type == "cpu" and h.is_pinned()
+        assert any(lo <= h.data_ptr() < hi for lo, hi in spans)
+    assert not tm._held_ptr_to_tid
+    ft.release()
+
+
+class _PeerBlock(torch.nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.lin = torch.nn.Linear(d, d, bias=False)
+        self._peer = []          # another block whose weight this one also reads (not registered)
+
+    def forward(self, x):
+        y = self.lin(x)
+        for p in self._peer:
+            y = y + torch.nn.functional.linear(x, p.lin.weight)
+        return y
+
+
+class _PeerNet(torch.nn.Module):
+    def __init__(self, d=256, n=4):
+        super().__init__()
+        self.blocks = torch.nn.ModuleList([_PeerBlock(d) for _ in range(n)])
+        self.blocks[2]._peer.append(self.blocks[0])
+
+    def forward(self, x):
+        for b in self.blocks:
+            x = torch.tanh(b(x))
+        return x
+
+
+def test_discovery_finds_cross_unit_read_of_a_device_held_weight():
+    torch.manual_seed(0)
+    m = _PeerNet().to(DEV)
+    x = torch.randn(8, 256, device=DEV)
+    with torch.no_grad():
+        want = m(x).clone()
+    om = ft.get_offload_manager()
+    mm = om.offload(m, ft.OffloadConfig(include_patterns=["blocks.*"], discovery_iters=1, profiling_iters=1,
+                                        num_blocks=2, min_blocks=2,
+                                        load_strategy=NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2,
+                                                                       cyclic=True)))
+    with torch.no_grad():
+        for _ in range(4):
+            torch.testing.assert_close(mm(x), want, rtol=0, atol=0)
+    tm = om.get_tensor_manager()
+    shared = tm.name_to_id["blocks.0.lin.weight"]
+    assert shared in tm.resident and shared not in tm.host
+    ft.release()

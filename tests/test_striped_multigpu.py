@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, on_device, gather="sm"):
+def _worker(rank, world, port, q, on_device, gather="ce"):
     import datetime
 
     import torch.distributed as dist
