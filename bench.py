@@ -143,6 +143,48 @@ def barrier(pg):
     torch.cuda.synchronize()
 
 
+def close_dist(pg) -> None:
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+def _pow2_ceil(n: int) -> int:
+    return 1 << max(0, int(n) - 1).bit_length()
+
+
+def host_need_bytes(model, impl: str, streamed_frac: float, unit_prefix: str = "") -> int:
+    """Estimated peak host bytes of ONE rank's offload setup (shapes only; ``model`` may be on meta).
+
+    * ours: the packed pinned arena of the streamed bytes (weights that start on the GPU are
+      packed from there, with no per-tensor host copy);
+    * reference: its per-tensor pinned copies of every unit weight (the caching host allocator
+      rounds each to a power of two) plus its packed blocks of the streamed bytes, or the
+      pageable start copy of the whole model, whichever is larger.
+    Both get 2 GB for the process itself."""
+    unit = [p.numel() * p.element_size() for n, p in model.named_parameters() if n.startswith(unit_prefix)]
+    total = sum(p.numel() * p.element_size() for p in model.parameters())
+    streamed = int(streamed_frac * sum(unit))
+    if impl == "ours":
+        return streamed + (2 << 30)
+    return max(total, sum(_pow2_ceil(n) for n in unit) + streamed) + (2 << 30)
+
+
+def host_gate(pg, need_per_rank: int, world: int) -> tuple[bool, str]:
+    """All ranks of this node together need ``world * need_per_rank`` host bytes: do they fit in
+    90 % of what the node has available now? Every rank gets the same answer (rank 0 decides)."""
+    import psutil
+    import torch
+
+    avail = psutil.virtual_memory().available
+    ok = torch.tensor([1.0 if world * need_per_rank <= 0.9 * avail else 0.0, float(avail)],
+                      dtype=torch.float64, device="cuda")
+    if pg is not None:
+        pg.broadcast(ok, src=0)
+    why = (f"host RAM (estimated): {world} ranks x {need_per_rank / 1e9:.0f} GB > 90% of "
+           f"{float(ok[1]) / 1e9:.0f} GB available")
+    return bool(ok[0] > 0), why
+
+
 # ----------------------------------------------------------------------------- model + runtime per arm
 def to_pageable(model) -> None:
     """Move every parameter and buffer to its own pageable host tensor (a model loaded on the CPU).

@@ -56,12 +56,21 @@ def main():
             print(json.dumps({"impl": a.impl, "unavailable": why}))
         return
     M = BATCH * PROMPT
+
+    def host_fits(meta_model) -> bool:
+        ok, why = bench.host_gate(pg, bench.host_need_bytes(meta_model, a.impl, 1 - RESIDENT, "layers."), world)
+        if not ok and rank == 0:
+            print(json.dumps({"impl": a.impl, "n_gpus": world, "unavailable": why}))
+        return ok
+
     if a.impl == "ours":
         from flextensor_b200.models.llama import LLAMA3_70B, LlamaTP, init_llama_params_, rope_tables_1d
 
         cfg = LLAMA3_70B
         with torch.device("meta"):
             model = LlamaTP(cfg, rank, world, layers=a.layers)
+        if not host_fits(model):
+            return bench.close_dist(pg)
         model = model.to_empty(device=dev).to(torch.bfloat16)
         init_llama_params_(model, seed=rank)
         if world > 1:
@@ -79,6 +88,8 @@ def main():
         cfg = LlamaShape()
         with torch.device("meta"):
             model = LlamaShard(cfg, world, layers=a.layers)
+        if not host_fits(model):
+            return bench.close_dist(pg)
         model = model.to_empty(device=dev).to(torch.bfloat16)
         init_params_(model, seed=rank)
         bench.to_pageable(model)

@@ -38,7 +38,7 @@ TOKENS = GRID[0] * GRID[1] * GRID[2]
 RESIDENT = 0.5
 
 
-def build(impl: str, layers: int, device, world: int):
+def build(impl: str, layers: int, device, world: int, host_fits=None):
     import torch
 
     if impl == "ours":
@@ -58,6 +58,8 @@ def build(impl: str, layers: int, device, world: int):
         with torch.device("meta"):
             model = WanTorchDiT(cfg)
         init = init_params_
+    if host_fits is not None and not host_fits(model):
+        return None, cfg
     model = model.to_empty(device=device).to(torch.bfloat16)
     init(model, seed=0)
     if impl == "reference":
@@ -89,7 +91,15 @@ def main():
         from flextensor_b200.parallel import enable_striped_streaming
 
         enable_striped_streaming()
-    model, cfg = build(a.impl, a.layers, device, world)
+    def host_fits(meta_model) -> bool:
+        ok, why = bench.host_gate(pg, bench.host_need_bytes(meta_model, a.impl, 1 - RESIDENT, "blocks."), world)
+        if not ok and rank == 0:
+            print(json.dumps({"impl": a.impl, "n_gpus": world, "unavailable": why}))
+        return ok
+
+    model, cfg = build(a.impl, a.layers, device, world, host_fits)
+    if model is None:
+        return bench.close_dist(pg)
     total = sum(p.numel() * p.element_size() for p in model.parameters())
     frac = RESIDENT * total / torch.cuda.get_device_properties(device).total_memory
     om = ft.get_offload_manager()

@@ -59,6 +59,13 @@ def main():
     if BATCH % world:
         raise SystemExit(f"{BATCH} sequences do not split over {world} ranks")
     B = BATCH // world
+
+    def host_fits(meta_model) -> bool:
+        ok, why = bench.host_gate(pg, bench.host_need_bytes(meta_model, a.impl, 1 - a.resident, "layers."), world)
+        if not ok and rank == 0:
+            print(json.dumps({"impl": a.impl, "n_gpus": world, "unavailable": why}))
+        return ok
+
     if a.impl == "ours":
         from flextensor_b200.models.llama import rope_tables_1d
         from flextensor_b200.models.mixtral import MIXTRAL_8X22B, MixtralStack, init_mixtral_params_
@@ -66,6 +73,8 @@ def main():
         cfg = MIXTRAL_8X22B
         with torch.device("meta"):
             model = MixtralStack(cfg, rank, world, layers=a.layers)
+        if not host_fits(model):
+            return bench.close_dist(pg)
         model = model.to_empty(device=dev).to(torch.bfloat16)
         init_mixtral_params_(model, seed=0)
         ep = {}
@@ -86,6 +95,8 @@ def main():
         cfg = MixtralShape()
         with torch.device("meta"):
             model = MixtralEP(cfg, rank, world, layers=a.layers)
+        if not host_fits(model):
+            return bench.close_dist(pg)
         model = model.to_empty(device=dev).to(torch.bfloat16)
         init_params_(model, seed=rank)
         bench.to_pageable(model)

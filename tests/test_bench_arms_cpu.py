@@ -188,3 +188,20 @@ def test_reference_mixtral_expert_parallel_matches_single_rank_over_gloo():
     for p in ps:
         p.join(30)
     assert all(err < 1e-4 for _, err in res), res
+
+
+def test_host_need_estimates():
+    """Ours needs the streamed bytes once; the reference pays the pinned copies (power-of-two
+    rounded) of every unit weight plus its packed streamed blocks."""
+    import torch
+    from torch import nn
+
+    import bench
+
+    with torch.device("meta"):
+        m = nn.ModuleDict({"layers": nn.ModuleList([nn.Linear(1000, 1000, bias=False) for _ in range(4)]),
+                           "head": nn.Linear(1000, 10, bias=False)})
+    unit = 4 * 1000 * 1000 * 4
+    assert bench.host_need_bytes(m, "ours", 0.5, "layers.") == unit // 2 + (2 << 30)
+    per = 1 << (1000 * 1000 * 4 - 1).bit_length()
+    assert bench.host_need_bytes(m, "reference", 0.5, "layers.") == 4 * per + unit // 2 + (2 << 30)
