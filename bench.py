@@ -152,7 +152,7 @@ def _pow2_ceil(n: int) -> int:
     return 1 << max(0, int(n) - 1).bit_length()
 
 
-def host_need_bytes(model, impl: str, streamed_frac: float, unit_prefix: str = "") -> int:
+def host_need_bytes(model, impl: str, streamed_frac: float, unit_prefix: str = "", elem_bytes: int = 2) -> int:
     """Estimated peak host bytes of ONE rank's offload setup (shapes only; ``model`` may be on meta).
 
     * ours: the packed pinned arena of the streamed bytes (weights that start on the GPU are
@@ -160,9 +160,10 @@ def host_need_bytes(model, impl: str, streamed_frac: float, unit_prefix: str = "
     * reference: its per-tensor pinned copies of every unit weight (the caching host allocator
       rounds each to a power of two) plus its packed blocks of the streamed bytes, or the
       pageable start copy of the whole model, whichever is larger.
-    Both get 2 GB for the process itself."""
-    unit = [p.numel() * p.element_size() for n, p in model.named_parameters() if n.startswith(unit_prefix)]
-    total = sum(p.numel() * p.element_size() for p in model.parameters())
+    Both get 2 GB for the process itself. Parameters count ``elem_bytes`` each (bf16: the meta
+    model may still carry its construction dtype)."""
+    unit = [p.numel() * elem_bytes for n, p in model.named_parameters() if n.startswith(unit_prefix)]
+    total = sum(p.numel() * elem_bytes for p in model.parameters())
     streamed = int(streamed_frac * sum(unit))
     if impl == "ours":
         return streamed + (2 << 30)
@@ -235,7 +236,7 @@ def build_model(impl: str, layers: int, device, seed: int, placement: str = "pin
         with torch.device("meta"):
             model = WanTorchDiT(cfg)
         init = init_params_
-    model = model.to_empty(device=device).to(torch.bfloat16)
+    model = model.to(torch.bfloat16).to_empty(device=device)  # bf16 before any bytes exist
     init(model, seed=seed)
     if placement in ("device", "pageable"):
         if placement == "pageable":

@@ -60,7 +60,7 @@ def build(impl: str, layers: int, device, world: int, host_fits=None):
         init = init_params_
     if host_fits is not None and not host_fits(model):
         return None, cfg
-    model = model.to_empty(device=device).to(torch.bfloat16)
+    model = model.to(torch.bfloat16).to_empty(device=device)  # bf16 before any bytes exist
     init(model, seed=0)
     if impl == "reference":
         bench.to_pageable(model)
@@ -79,6 +79,7 @@ def main():
     a = ap.parse_args()
     import torch
 
+    rss0 = bench._rss_bytes()
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank, world, local, pg = bench.dist_setup(world)
     device = torch.device("cuda", local)
@@ -147,6 +148,7 @@ def main():
     torch.cuda.synchronize()
     bench.barrier(pg)
     ck = clocks.stop()
+    host_peak = round(bench.allreduce_max((bench._peak_rss_bytes() - rss0) / 1e9, pg), 1)
     ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
     eng = bench._engine(om) if a.impl == "ours" else None
     heap = getattr(eng, "device_bytes", 0) if eng is not None else 0
@@ -166,7 +168,7 @@ def main():
             "metric": "s/step (one denoise step), LTX-shape DiT, context parallel, 50% weights offloaded",
             "value": round(ms_max / 1000, 4), "unit": "s/step", "impl": a.impl, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "peak_gpu_gb": round(peak_max, 2), "transfer_hidden_pct": hidden,
-            "weights_gb": round(total / 1e9, 2), "setup_s": round(setup_s, 1), "clocks": ck,
+            "weights_gb": round(total / 1e9, 2), "setup_s": round(setup_s, 1), "host_peak_gb_per_rank": host_peak, "clocks": ck,
             "config": {"model": f"LTX-shape DiT ({a.layers} blocks, d=4096, 32 heads, FFN 16384, 40480 tokens, "
                                 "text 256x4096)" + ("" if a.layers == 48 else " [NOT the full config]"),
                        "parallelism": (f"cp{world} " + ("fused K/V all-gather in attention + striped streaming"

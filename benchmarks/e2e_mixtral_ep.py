@@ -48,6 +48,7 @@ def main():
     a = ap.parse_args()
     import torch
 
+    rss0 = bench._rss_bytes()
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank, world, local, pg = bench.dist_setup(world)
     dev = torch.device("cuda", local)
@@ -75,7 +76,7 @@ def main():
             model = MixtralStack(cfg, rank, world, layers=a.layers)
         if not host_fits(model):
             return bench.close_dist(pg)
-        model = model.to_empty(device=dev).to(torch.bfloat16)
+        model = model.to(torch.bfloat16).to_empty(device=dev)  # bf16 before any bytes exist
         init_mixtral_params_(model, seed=0)
         ep = {}
         if world > 1:
@@ -97,7 +98,7 @@ def main():
             model = MixtralEP(cfg, rank, world, layers=a.layers)
         if not host_fits(model):
             return bench.close_dist(pg)
-        model = model.to_empty(device=dev).to(torch.bfloat16)
+        model = model.to(torch.bfloat16).to_empty(device=dev)  # bf16 before any bytes exist
         init_params_(model, seed=rank)
         bench.to_pageable(model)
         cos, sin = rope_cos_sin(PROMPT + NEW, cfg.head_dim, cfg.rope_theta, dev)
@@ -145,6 +146,7 @@ def main():
     torch.cuda.synchronize()
     bench.barrier(pg)
     ck = clocks.stop()
+    host_peak = round(bench.allreduce_max((bench._peak_rss_bytes() - rss0) / 1e9, pg), 1)
     pre_ms = bench.allreduce_max(ps.elapsed_time(pe), pg)
     dec_ms = bench.allreduce_max(sum(s.elapsed_time(e) for s, e in dec) / max(1, len(dec)), pg)
     peak = bench.allreduce_max(torch.cuda.max_memory_allocated(dev) / 1e9, pg)
@@ -164,7 +166,7 @@ def main():
             "decode_ms_per_step": round(dec_ms, 3), "decode_steps_timed": a.decode_steps,
             "peak_gpu_gb": round(peak, 2), "transfer_hidden_pct": hidden,
             "weights_gb_per_rank": round(total / 1e9, 2), "resident_fraction": a.resident,
-            "setup_s": round(setup_s, 1), "clocks": ck,
+            "setup_s": round(setup_s, 1), "host_peak_gb_per_rank": host_peak, "clocks": ck,
             "config": {"model": f"Mixtral-8x22B-shape layers ({a.layers} of 56, d=6144, 48/8 heads, 8 experts top-2, "
                                 "FFN 16384)" + ("" if a.layers == 56 else " [NOT the full config]"),
                        "batch": f"{BATCH} x ({PROMPT} prompt + {NEW} decode)",

@@ -70,7 +70,7 @@ def main():
 
     m = build()
     pp = WanPipelineParallel(m, depth=a.depth)  # drops the other stages' blocks while still on meta
-    m = m.to_empty(device=dev).to(torch.bfloat16)
+    m = m.to(torch.bfloat16).to_empty(device=dev)
     init_wan_params_(m, seed=0)
     m.eval().requires_grad_(False)
     res = {"n_gpus": W, "tokens": S, "layers": a.layers, "micro_batches": a.micro, "stages": pp.bounds}

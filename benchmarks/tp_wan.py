@@ -59,7 +59,7 @@ def main():
     for impl in ("fused", "nccl"):
         with torch.device("meta"):
             m = WanDiT(cfg)
-        m = m.to_empty(device=dev).to(torch.bfloat16)
+        m = m.to(torch.bfloat16).to_empty(device=dev)
         init_wan_params_(m, seed=0)
         m.eval().requires_grad_(False)
         tp = WanTensorParallel(m, impl=impl, max_tokens=S)

@@ -41,7 +41,7 @@ from typing import Any, Protocol
 import torch
 import torch.distributed as dist
 
-__all__ = ["PipelineGroups", "PipelineStage", "TorchP2P", "pipeline_groups", "split_stages"]
+__all__ = ["PipelineGroups", "PipelineStage", "TorchP2P", "connect_pipeline", "pipeline_groups", "split_stages"]
 
 
 def split_stages(costs: Sequence[float], n_stages: int) -> list[tuple[int, int]]:
@@ -92,7 +92,36 @@ def pipeline_groups(group: Any = None) -> PipelineGroups:
     collective call: every process of the default group calls it (``new_group`` needs them all)."""
     ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
     even, odd, back = (dist.new_group(ranks) for _ in range(3))
-    return PipelineGroups(ranks=ranks, links=(even, odd), back=back)
+    groups = PipelineGroups(ranks=ranks, links=(even, odd), back=back)
+    if dist.get_rank() in ranks and len(ranks) > 1:
+        connect_pipeline(groups)
+    return groups
+
+
+def connect_pipeline(groups: PipelineGroups) -> None:
+    """Open every point-to-point connection the pipeline uses, on every rank in the same order.
+
+    NCCL opens the connection between two ranks of a communicator at their first send/receive
+    pair, and that handshake blocks the host until the peer reaches the same communicator. A
+    pipeline's first operations differ by stage (the first stage posts its return receives on
+    ``back``, the second its forward receives on ``links[0]``), so without this each could wait
+    for the other. Here each communicator in turn exchanges one element with both ring
+    neighbours (stage s with s - 1 and s + 1, which covers every link and the last-to-first
+    return) as one batched group."""
+    me = groups.ranks.index(dist.get_rank())
+    n = len(groups.ranks)
+    nxt, prv = groups.ranks[(me + 1) % n], groups.ranks[(me - 1) % n]
+    backend = dist.get_backend(groups.back)
+    device = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    for g in (groups.links[0], groups.links[1], groups.back):
+        out = torch.zeros(2, device=device)
+        inp = torch.empty(2, device=device)
+        ops = [dist.P2POp(dist.isend, out[0:1], nxt, g), dist.P2POp(dist.irecv, inp[0:1], prv, g),
+               dist.P2POp(dist.isend, out[1:2], prv, g), dist.P2POp(dist.irecv, inp[1:2], nxt, g)]
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
 
 
 class Handle(Protocol):
