@@ -107,7 +107,9 @@ def main():
     config = bench.make_config(ft, local, frac, a.profiling_iters)
     config = config.model_copy(update={"include_patterns": ["layers.*"]}) if hasattr(config, "model_copy") \
         else config
+    rss_built = bench._rss_bytes()
     model = om.offload(model, config)
+    rss_offloaded = bench._rss_bytes()
     cache = model.new_cache(BATCH, PROMPT + NEW, dev)
     g = torch.Generator(device=dev).manual_seed(11 + rank)
     x_pre = torch.randn(rows_pre, cfg.dim, device=dev, generator=g).bfloat16()
@@ -120,6 +122,7 @@ def main():
             fwd(x_pre.clone(), PROMPT, cache, 0, c_pre, s_pre)
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t0
+    rss_setup = bench._rss_bytes()
     torch.cuda.reset_peak_memory_stats(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     clocks = bench.ClockSampler(local)
@@ -143,6 +146,8 @@ def main():
     bench.barrier(pg)
     ck = clocks.stop()
     host_peak = round(bench.allreduce_max((bench._peak_rss_bytes() - rss0) / 1e9, pg), 1)
+    rss_stages = {k: round((v - rss0) / 1e9, 1) for k, v in (
+        ("built", rss_built), ("offloaded", rss_offloaded), ("setup", rss_setup), ("end", bench._rss_bytes()))}
     pre_ms = bench.allreduce_max(ps.elapsed_time(pe), pg)
     dec_ms = bench.allreduce_max(sum(s.elapsed_time(e) for s, e in dec) / max(1, len(dec)), pg)
     peak = bench.allreduce_max(torch.cuda.max_memory_allocated(dev) / 1e9, pg)
@@ -161,7 +166,7 @@ def main():
             "impl": a.impl, "n_gpus": world, "prefill_s": round(pre_ms / 1000, 4),
             "decode_ms_per_step": round(dec_ms, 3), "decode_steps_timed": a.decode_steps,
             "peak_gpu_gb": round(peak, 2), "transfer_hidden_pct": hidden, "weights_gb_per_rank": round(total / 1e9, 2),
-            "setup_s": round(setup_s, 1), "host_peak_gb_per_rank": host_peak, "clocks": ck,
+            "setup_s": round(setup_s, 1), "host_peak_gb_per_rank": host_peak, "host_rss_gb_rank0": rss_stages, "clocks": ck,
             "config": {"model": f"Llama-3-70B-shape decoder layers ({a.layers} of 80, d=8192, 64/8 heads, FFN 28672)"
                                 + ("" if a.layers == 80 else " [NOT the full config]"),
                        "batch": f"{BATCH} x ({PROMPT} prompt + {NEW} decode)",

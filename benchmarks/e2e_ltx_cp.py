@@ -104,7 +104,9 @@ def main():
     total = sum(p.numel() * p.element_size() for p in model.parameters())
     frac = RESIDENT * total / torch.cuda.get_device_properties(device).total_memory
     om = ft.get_offload_manager()
+    rss_built = bench._rss_bytes()
     model = om.offload(model, bench.make_config(ft, local, frac, a.profiling_iters))
+    rss_offloaded = bench._rss_bytes()
     cp = None
     if world > 1:
         if a.impl == "ours":
@@ -131,6 +133,7 @@ def main():
             step()
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t0
+    rss_setup = bench._rss_bytes()
     torch.cuda.reset_peak_memory_stats(device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     clocks = bench.ClockSampler(local)
@@ -149,6 +152,8 @@ def main():
     bench.barrier(pg)
     ck = clocks.stop()
     host_peak = round(bench.allreduce_max((bench._peak_rss_bytes() - rss0) / 1e9, pg), 1)
+    rss_stages = {k: round((v - rss0) / 1e9, 1) for k, v in (
+        ("built", rss_built), ("offloaded", rss_offloaded), ("setup", rss_setup), ("end", bench._rss_bytes()))}
     ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
     eng = bench._engine(om) if a.impl == "ours" else None
     heap = getattr(eng, "device_bytes", 0) if eng is not None else 0
@@ -168,7 +173,7 @@ def main():
             "metric": "s/step (one denoise step), LTX-shape DiT, context parallel, 50% weights offloaded",
             "value": round(ms_max / 1000, 4), "unit": "s/step", "impl": a.impl, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "peak_gpu_gb": round(peak_max, 2), "transfer_hidden_pct": hidden,
-            "weights_gb": round(total / 1e9, 2), "setup_s": round(setup_s, 1), "host_peak_gb_per_rank": host_peak, "clocks": ck,
+            "weights_gb": round(total / 1e9, 2), "setup_s": round(setup_s, 1), "host_peak_gb_per_rank": host_peak, "host_rss_gb_rank0": rss_stages, "clocks": ck,
             "config": {"model": f"LTX-shape DiT ({a.layers} blocks, d=4096, 32 heads, FFN 16384, 40480 tokens, "
                                 "text 256x4096)" + ("" if a.layers == 48 else " [NOT the full config]"),
                        "parallelism": (f"cp{world} " + ("fused K/V all-gather in attention + striped streaming"
