@@ -118,8 +118,20 @@ def make_host_pinner(pinned_memory: bool, mode: str) -> HostPinner:
     return HostPinner(mode)
 
 
+EXACT_PIN_MIN = 16 << 20
+
+
 def alloc_host_bytes(nbytes: int, pinned: bool) -> torch.Tensor:
+    """``nbytes`` of host memory, page-locked when ``pinned``. Large pinned requests get exactly
+    their size from the native extension (one cudaHostAlloc freed with the last view): torch's
+    caching host allocator would round each up to a power of two, which for a multi-GB packed
+    arena pins up to twice its bytes."""
     if pinned and _cuda_ok():
+        if nbytes >= EXACT_PIN_MIN:
+            from flextensor_b200.ops import native
+
+            if native.available():
+                return native.pinned_empty(int(nbytes))
         return torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     return torch.empty(nbytes, dtype=torch.uint8)
 

@@ -170,7 +170,7 @@ def tp_allgather_gemm(a_full: torch.Tensor, weight: torch.Tensor, *, peer_a: lis
     """All-gather -> GEMM: ``a_full [M, K]`` is this rank's full-row buffer with its own rows
     written and published; the kernel pulls peers' rows over NVLink while multiplying.
     ``epi="swiglu"``: weight rows interleaved (gate, up) -> ``[M, N/2]``. ``_pair``: the
-    experimental CTA-pair (cta_group::2) kernel, not yet run on a GPU."""
+    experimental CTA-pair (cta_group::2) kernel (tested on emulated ranks)."""
     n_out = weight.shape[0] // 2 if epi == "swiglu" else weight.shape[0]
     if out is None:
         out = torch.empty(a_full.shape[0], n_out, dtype=torch.bfloat16, device=a_full.device)
@@ -191,7 +191,7 @@ def tp_gemm_reducescatter(a: torch.Tensor, weight: torch.Tensor, *, stage: list[
                           rank: int, epoch: int, counters: torch.Tensor, _pair: bool = False) -> None:
     """GEMM -> reduce-scatter, sender side: partial ``a @ weight.T`` rows go straight into the
     owning rank's staging slot ``[world, M/world, N]`` (``stage[p]``); then flags. ``_pair``:
-    the experimental CTA-pair (cta_group::2) kernel, not yet run on a GPU."""
+    the experimental CTA-pair (cta_group::2) kernel (tested on emulated ranks)."""
     native.lib().tp_gemm_rs(a, weight, [int(p) for p in stage], [int(p) for p in peer_flags], int(rank), int(epoch),
                             counters, bool(_pair))
     _count()

@@ -707,6 +707,18 @@ struct PyEngine {
 
 }  // namespace
 
+// Exact-size pinned host bytes: one portable cudaHostAlloc, released with cudaFreeHost when the
+// last tensor (or view) over it goes away. torch's caching host allocator rounds each request up
+// to a power of two, which for a 36 GB packed arena pins 64 GB of host memory.
+at::Tensor pinned_empty(int64_t nbytes) {
+  TORCH_CHECK(nbytes > 0, "pinned_empty: nbytes must be positive, got ", nbytes);
+  void* p = nullptr;
+  const cudaError_t e = cudaHostAlloc(&p, static_cast<size_t>(nbytes), cudaHostAllocPortable);
+  TORCH_CHECK(e == cudaSuccess, "cudaHostAlloc(", nbytes, " bytes) failed: ", cudaGetErrorString(e));
+  return torch::from_blob(
+      p, {nbytes}, [](void* q) { cudaFreeHost(q); }, at::TensorOptions().dtype(at::kByte).device(at::kCPU));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "flextensor_b200 native kernels (sm_100a) and runtime";
   m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A W^T)", py::arg("A"), py::arg("W"), py::arg("C"),
@@ -744,6 +756,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gemm", &moe_gemm);
   m.def("moe_reduce", &moe_reduce);
   m.def("p2p_wait_acks_raw", &p2p_wait_acks_raw);
+  m.def("pinned_empty", &pinned_empty, py::arg("nbytes"));
   m.def("host_register", [](uintptr_t p, size_t n) { ft::host_register(reinterpret_cast<void*>(p), n); });
   m.def("host_unregister", [](uintptr_t p) { ft::host_unregister(reinterpret_cast<void*>(p)); });
   m.def("device_malloc", [](size_t n) { return reinterpret_cast<uintptr_t>(ft::device_malloc(n)); });

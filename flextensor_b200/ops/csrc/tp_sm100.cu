@@ -713,7 +713,7 @@ __global__ void tp_ack_kernel(AckList a) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Experimental CTA-pair variant (TpGemmProblem::pair; not yet run on a GPU): 256 x 256 tiles over
+// Experimental CTA-pair variant (TpGemmProblem::pair; tested on emulated ranks): 256 x 256 tiles over
 // a cluster of 2 CTAs with tcgen05.mma.cta_group::2. Each CTA loads its own 128 rows of A (and,
 // all-gather, waits for exactly those rows to land) and its own 128 rows of W; both loads count on
 // the leader's barrier (no multicast: every CTA fetches its half itself). The leader's MMA thread

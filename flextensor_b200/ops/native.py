@@ -60,6 +60,11 @@ def available() -> bool:
         return False
 
 
+def pinned_empty(nbytes: int) -> torch.Tensor:
+    """``nbytes`` uint8 CPU tensor in page-locked memory of exactly that size (no rounding)."""
+    return lib().pinned_empty(int(nbytes))
+
+
 def host_register(ptr: int, nbytes: int) -> None:
     lib().host_register(int(ptr), int(nbytes))
 

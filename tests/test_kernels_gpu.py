@@ -206,8 +206,6 @@ def test_attention_large_logits():
     assert rel_err(o, _attn_ref(q, k, v)) < 2e-2
 
 
-@pytest.mark.skipif(os.environ.get("FT_TEST_EXPERIMENTAL") != "1",
-                    reason="experimental one-tile attention kernel: opt-in (FT_TEST_EXPERIMENTAL=1)")
 @pytest.mark.parametrize("mode", [200, 201])
 @pytest.mark.parametrize("B,Sq,Sk,H,Hk,causal", [(1, 128, 128, 1, 1, False), (2, 300, 300, 4, 4, False),
                                                  (1, 384, 1000, 8, 2, False), (2, 500, 500, 4, 4, True)])

@@ -212,3 +212,23 @@ def test_discovery_finds_cross_unit_read_of_a_device_held_weight():
     shared = tm.name_to_id["blocks.0.lin.weight"]
     assert shared in tm.resident and shared not in tm.host
     ft.release()
+
+
+def test_exact_size_pinned_arena():
+    """Large pinned host buffers come from one exact-size page-locked allocation (no power-of-two
+    rounding) that supports asynchronous copies both ways and is freed with its last view."""
+    from flextensor_b200.core.host_store import EXACT_PIN_MIN, alloc_host_bytes
+
+    n = EXACT_PIN_MIN + 4096 * 3
+    h = alloc_host_bytes(n, pinned=True)
+    assert h.numel() == n and h.is_pinned() and h.dtype == torch.uint8
+    src = torch.randint(0, 255, (n,), dtype=torch.uint8, device=DEV)
+    v = h[4096:]
+    v.copy_(src[4096:], non_blocking=True)
+    back = torch.empty_like(src)
+    back[4096:].copy_(v, non_blocking=True)
+    torch.cuda.synchronize()
+    assert torch.equal(back[4096:], src[4096:])
+    del h, v
+    small = alloc_host_bytes(1024, pinned=True)
+    assert small.is_pinned() and small.numel() == 1024

@@ -203,8 +203,6 @@ def test_reduce_bias_gate_residual():
         assert _rel(outs[p], ref) < 2e-2, p
 
 
-@pytest.mark.skipif(os.environ.get("FT_TEST_EXPERIMENTAL") != "1",
-                    reason="experimental CTA-pair TP kernels: opt-in (FT_TEST_EXPERIMENTAL=1)")
 @pytest.mark.parametrize("W,R,K,N,epi", [(2, 256, 512, 1024, "none"), (4, 200, 256, 640, "swiglu"),
                                          (8, 96, 128, 384, "bias")])
 def test_pair_kernels_emulated(W, R, K, N, epi):
