@@ -49,6 +49,8 @@ def parse():
                     help="where the weights start before offload() (auto: pinned arena at N=1; at N>1 device "
                          "for ours, pageable for the reference)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--resident", type=float, default=RESIDENT_FRACTION,
+                    help="(study only) share of weight bytes on the GPU; the headline config is 0.25")
     return ap.parse_args()
 
 
@@ -267,7 +269,7 @@ def build_model(impl: str, layers: int, device, seed: int, placement: str = "pin
     return model, cfg
 
 
-def weight_budget_fraction(model, device) -> float:
+def weight_budget_fraction(model, device, resident: float = RESIDENT_FRACTION) -> float:
     import torch
 
     total = sum(p.numel() * p.element_size() for p in model.parameters())
@@ -275,7 +277,7 @@ def weight_budget_fraction(model, device) -> float:
     other = total - block
     dev_total = torch.cuda.get_device_properties(device).total_memory
     # planner-visible budget = 25% of all weight bytes minus the always-resident non-block weights
-    return (RESIDENT_FRACTION * total) / dev_total, total, block, other
+    return (resident * total) / dev_total, total, block, other
 
 
 def make_config(ft, local: int, frac: float, profiling_iters: int):
@@ -350,7 +352,7 @@ def setup_arm(args, ft, local: int, device, placement: str):
     import torch
 
     model, cfg = build_model(args.impl, args.layers, device, seed=0, placement=placement)
-    frac, total_w, block_w, other_w = weight_budget_fraction(model, device)
+    frac, total_w, block_w, other_w = weight_budget_fraction(model, device, args.resident)
     config = make_config(ft, local, frac, args.profiling_iters)
     om = ft.get_offload_manager()
     model = om.offload(model, config)
@@ -539,7 +541,8 @@ def main():
                    "global_batch": world, "seq_len": tokens,
                    "parallelism": f"dp{world}" + (" + striped host streaming (1/N per rank, NVLink gather)"
                                                   if world > 1 and args.impl == "ours" else ""),
-                   "weight_budget": f"{int(RESIDENT_FRACTION * 100)}% of weight bytes on GPU (incl. ring slots)",
+                   "weight_budget": f"{round(args.resident * 100)}% of weight bytes on GPU (incl. ring slots)"
+                                    + ("" if args.resident == RESIDENT_FRACTION else " [NOT the headline config]"),
                    "l2": "flushed (256 MB write) before every timed step",
                    "denoise_steps_timed": args.steps},
     }
