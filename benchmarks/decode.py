@@ -9,8 +9,9 @@ Shapes (B sequences, context, query heads, KV heads):
 
 For each: the split-KV decode kernel (``ops.decode_attention``), the prefill kernel given one
 query per sequence (``ops.attention``, what the decode path used before), and PyTorch SDPA
-(``enable_gqa``). Times are CUDA-event medians; the L2 is flushed with a 256 MB write before
-each launch. Roofline: K + V bytes of the
+(``enable_gqa``). Times are CUDA-event medians of device time (the GPU is given a head start so
+host launch overhead is not counted); the L2 is flushed by reading 256 MB before each launch (a write flush would leave ~126 MB of dirty
+lines whose write-back the timed kernel would pay for). Roofline: K + V bytes of the
 context at the measured copy bandwidth (``MEASURED_PEAKS.json`` ``hbm_gbs``, else 6650 GB/s).
 """
 
@@ -39,12 +40,16 @@ def hbm_gbs() -> float:
 
 
 def timed(fn, iters, flush):
+    """Device time of ``fn``: the GPU sleeps ~50 us after the L2 flush, before the start event, so
+    the host has enqueued ``fn``'s launches when the start event fires (host-side launch overhead
+    is not counted, for every timed op alike)."""
     ts = []
     for _ in range(3):
         fn()
     for _ in range(iters):
-        flush.fill_(1)
+        flush.sum()  # read 256 MB: evicts the L2 without leaving dirty lines for fn to write back
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(100_000)
         s.record()
         fn()
         e.record()
@@ -57,12 +62,13 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default="llama70b,llama70b_tp8,mixtral")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--n-split", type=int, default=0, help="0: the library's choice")
     a = ap.parse_args()
     from flextensor_b200 import ops
     from flextensor_b200.ops import native
 
     dev = torch.device("cuda", 0)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
     bw = hbm_gbs()
     for name in a.shapes.split(","):
         B, L, Hq, Hk = SHAPES[name]
@@ -73,7 +79,7 @@ def main():
         out = torch.empty_like(q)
         kv_bytes = 2 * B * L * Hk * 128 * 2
         roof_us = kv_bytes / (bw * 1e9) * 1e6
-        t_dec = timed(lambda: ops.decode_attention(q, kc, vc, L, out=out), a.iters, flush)
+        t_dec = timed(lambda: ops.decode_attention(q, kc, vc, L, out=out, n_split=a.n_split), a.iters, flush)
         t_pre = timed(lambda: ops.attention(q, kc, vc), a.iters, flush)
         qt, kt, vt = q.transpose(1, 2), kc.transpose(1, 2), vc.transpose(1, 2)
         t_sdpa = timed(lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, enable_gqa=True),
@@ -82,6 +88,7 @@ def main():
         assert native.device_error(reset=True) == 0
         print(json.dumps({"shape": name, "B": B, "ctx": L, "Hq": Hq, "Hk": Hk, "kv_MB": round(kv_bytes / 1e6, 1),
                           "roofline_us": round(roof_us, 1), "decode_us": round(t_dec, 1),
+                          "n_split": a.n_split or native.lib().decode_splits(B, Hk, L, torch.cuda.get_device_properties(dev).multi_processor_count),
                           "decode_x_roofline": round(t_dec / roof_us, 2), "prefill_kernel_us": round(t_pre, 1),
                           "sdpa_us": round(t_sdpa, 1), "max_abs_diff_vs_prefill_kernel": err}))
 

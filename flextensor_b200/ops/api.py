@@ -122,7 +122,7 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     sequence, over the KV cache ``k_cache`` / ``v_cache [B, L, Hk, 128]`` (GQA when Hk < Hq).
     ``kv_len``: keys per sequence, an int (every sequence) or an int32 CUDA tensor ``[B]`` (then
     ``max_len`` bounds it, default L). Keys are split over CTAs and the splits merged in a second
-    pass (``n_split``: 0 = about two CTAs per SM)."""
+    pass (``n_split``: 0 = about one CTA per SM)."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     if out is None:

@@ -391,7 +391,10 @@ bool make_tmap_cache(CUtensorMap* map, const void* base, int Hk, int L, int B, l
 int decode_splits(int B, int Hk, int max_len, int num_sms) {
   const int tiles = (max(max_len, 1) + KT - 1) / KT;
   const int base = max(1, B * Hk);
-  int n = (2 * max(num_sms, 1) + base - 1) / base;  // about two waves of CTAs
+  // about one wave of CTAs: each split adds a partial row to write and a merge pass, which cost
+  // more than a partly empty wave (B200, Llama-70B decode shape 32 x 2304, 8 KV heads: 1 split
+  // 54.3 us, 2 splits 66.6 us, 4 splits 76.8 us); splits pay off when B * Hk is below the SM count
+  int n = (max(num_sms, 1) + base - 1) / base;
   n = max(1, min(n, tiles / (4 * NCW)));              // at least four tiles per consumer warp
   return n;
 }
