@@ -413,4 +413,8 @@ def main(argv=None):
 
 
 if __name__ == "__main__":
-    main()
+    _res = main()
+    if _res is not None and int(os.environ.get("RANK", "0")) == 0:
+        import json
+
+        print(json.dumps(_res))
