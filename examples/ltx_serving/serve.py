@@ -117,8 +117,10 @@ def _stage_config(name: str, budget: float | None, device: torch.device):
     import flextensor_b200 as ft
 
     include = ["blocks.*"]
+    # every rank's managers run on its own GPU (the config's default device is GPU 0)
     return ft.OffloadConfig(include_patterns=include, num_blocks=2, min_blocks=2, max_gpu_mem_fraction=budget,
-                            profiling_iters=1, discovery_iters=1, pinned_memory=device.type == "cuda")
+                            profiling_iters=1, discovery_iters=1, pinned_memory=device.type == "cuda",
+                            gpu_device=(device.index or 0) if device.type == "cuda" else 0)
 
 
 class DenoiseEngine:

@@ -71,3 +71,13 @@ def test_profile_then_serve_from_profiles(tmp_path):
     ns = f"ftserve_{os.getpid()}"
     out2 = mod.main(["serve", "--profile-dir", pdir, "--tiny", "--cpu", "--once", "--shm-namespace", ns])
     assert out2["ok"] and out2["checksum"] == out["checksum"]
+
+
+def test_stage_config_uses_the_ranks_gpu():
+    """Every rank's stage managers are configured for its own GPU, not the config's default 0."""
+    import torch
+
+    mod = _load()
+    assert mod._stage_config("dit", 0.1, torch.device("cuda", 1)).gpu_device == 1
+    assert mod._stage_config("text", None, torch.device("cuda", 0)).gpu_device == 0
+    assert mod._stage_config("dit", None, torch.device("cpu")).gpu_device == 0
