@@ -36,7 +36,7 @@ from __future__ import annotations
 from collections import deque
 from collections.abc import Callable, Sequence
 from dataclasses import dataclass
-from typing import Any, Protocol
+from typing import Any, Protocol, runtime_checkable
 
 import torch
 import torch.distributed as dist
@@ -124,10 +124,12 @@ def connect_pipeline(groups: PipelineGroups) -> None:
         torch.cuda.synchronize(device)
 
 
+@runtime_checkable
 class Handle(Protocol):
     def wait(self) -> Any: ...
 
 
+@runtime_checkable
 class P2P(Protocol):
     """Point-to-point transport between pipeline stages. ``channel`` is ``"fwd"`` for the
     stage-to-stage link and ``"back"`` for the last-to-first return."""

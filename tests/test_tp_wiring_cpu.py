@@ -5,15 +5,23 @@ owner polls, and the acknowledgement an owner writes is the one the sender waits
 ``flags[peer][own * N_SLOTS + slot]``). The kernels are replaced by recorders."""
 
 import pytest
+import torch
 
 from flextensor_b200.parallel import tp as T
+from flextensor_b200.parallel.symm import SymmetricHeap
 
 W = 8
 HEAP = [0x10_0000_0000 * (r + 1) for r in range(W)]  # fake heap bases, one per rank
 
 
-class _Heap:
-    ptrs = HEAP
+_T = torch.zeros(4, 8)  # stands in for every tensor argument: only the wiring is checked
+
+
+class _Heap(SymmetricHeap):
+    """Peer pointers only (no device memory): ``SymmetricHeap.__init__`` is not run."""
+
+    def __init__(self):
+        self.ptrs = HEAP
 
 
 def _obj(cls, rank, **extra):
@@ -39,16 +47,16 @@ def test_reduce_scatter_flags_and_acks_meet(monkeypatch, slot):
     import flextensor_b200.ops.api as api
 
     monkeypatch.setattr(api, "tp_gemm_reducescatter",
-                        lambda a, w, *, stage, peer_flags, rank, epoch, counters, **kw: sent.setdefault(rank, peer_flags))
+                        lambda a, w, *, stage, peer_flags, rank, epoch, counters, **kw: (sent.setdefault(rank, peer_flags), _T)[1])
     monkeypatch.setattr(api, "tp_reduce", lambda stage, world, rows, out, *, flags_ptr, flag_stride, peer_acks, rank,
-                        **kw: polled.setdefault(rank, (flags_ptr, flag_stride, peer_acks)))
+                        **kw: (polled.setdefault(rank, (flags_ptr, flag_stride, peer_acks)), _T)[1])
     for r in range(W):
         o = _obj(T.TPReduceScatter, r, M=W * 4, N=8, R=4, counters=None, off=[4096, 8192], slot_bytes=4096,
                  _cur=None)
         o._stage = lambda s: None
         o.calls = slot
-        o.gemm(None, None)
-        o.reduce(None)
+        o.gemm(_T, _T)
+        o.reduce(_T)
     for owner in range(W):
         flags_ptr, stride, acks = polled[owner]
         for sender in range(W):
@@ -63,12 +71,12 @@ def test_all_gather_flags_and_acks_meet(monkeypatch, slot):
     import flextensor_b200.ops.api as api
 
     monkeypatch.setattr(api, "tp_allgather_gemm", lambda a, w, *, peer_a, flags_ptr, flag_stride, peer_acks, rank,
-                        epoch, counters, **kw: seen.setdefault(rank, (flags_ptr, flag_stride, peer_acks)))
+                        epoch, counters, **kw: (seen.setdefault(rank, (flags_ptr, flag_stride, peer_acks)), _T)[1])
     for r in range(W):
         o = _obj(T.TPAllGather, r, M=W * 4, K=8, R=4, counters=None, off=[4096, 8192], slot_bytes=4096)
         o._cur = (slot, 1)
         o._buf = lambda s: None
-        o.gemm(None)
+        o.gemm(_T)
     for reader in range(W):
         flags_ptr, stride, acks = seen[reader]
         for pub in range(W):
@@ -83,12 +91,12 @@ def test_distributed_rmsnorm_flags_and_acks_meet(monkeypatch, slot):
     seen = {}
     import flextensor_b200.ops.api as api
 
-    monkeypatch.setattr(api, "tp_rmsnorm", lambda x, w, **kw: seen.setdefault(kw["rank"], kw))
+    monkeypatch.setattr(api, "tp_rmsnorm", lambda x, w, **kw: (seen.setdefault(kw["rank"], kw), _T)[1])
     monkeypatch.setattr(T.native, "lib", lambda: type("L", (), {"p2p_wait_acks_raw": staticmethod(lambda *a: None)}))
     for r in range(W):
         o = _obj(T.TPRMSNorm, r, stage_rows=64, off=[4096, 8192], counter=None)
         o.calls = slot
-        o(type("X", (), {"numel": lambda self: 32, "shape": (4, 8)})(), None, 64)
+        o(torch.zeros(4, 8), None, 64)
     for owner in range(W):
         kw = seen[owner]
         for sender in range(W):
