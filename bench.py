@@ -172,9 +172,17 @@ def host_need_bytes(model, impl: str, streamed_frac: float, unit_prefix: str = "
     return max(total, sum(_pow2_ceil(n) for n in unit) + streamed) + (2 << 30)
 
 
-def host_gate(pg, need_per_rank: int, world: int) -> tuple[bool, str]:
+def host_start_bytes(model, impl: str, elem_bytes: int = 2) -> int:
+    """Host bytes an arm certainly holds per rank before offloading: the reference arm starts from
+    a pageable host copy of the whole model (its runtime rejects a device start); ours starts on
+    the GPU."""
+    return sum(p.numel() * elem_bytes for p in model.parameters()) if impl == "reference" else 0
+
+
+def host_gate(pg, need_per_rank: int, world: int, certain_per_rank: int = 0) -> tuple[bool, str]:
     """All ranks of this node together need ``world * need_per_rank`` host bytes: do they fit in
-    90 % of what the node has available now? Every rank gets the same answer (rank 0 decides)."""
+    90 % of what the node has available now? Every rank gets the same answer (rank 0 decides).
+    ``certain_per_rank``: the part of the need that is not an estimate (named in the message)."""
     import psutil
     import torch
 
@@ -185,6 +193,9 @@ def host_gate(pg, need_per_rank: int, world: int) -> tuple[bool, str]:
         pg.broadcast(ok, src=0)
     why = (f"host RAM (estimated): {world} ranks x {need_per_rank / 1e9:.0f} GB > 90% of "
            f"{float(ok[1]) / 1e9:.0f} GB available")
+    if certain_per_rank:
+        why += (f"; of that, {world} x {certain_per_rank / 1e9:.0f} GB is the host copy of the "
+                f"weights each rank starts from")
     return bool(ok[0] > 0), why
 
 

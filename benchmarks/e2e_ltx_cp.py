@@ -93,7 +93,8 @@ def main():
 
         enable_striped_streaming()
     def host_fits(meta_model) -> bool:
-        ok, why = bench.host_gate(pg, bench.host_need_bytes(meta_model, a.impl, 1 - RESIDENT, "blocks."), world)
+        ok, why = bench.host_gate(pg, bench.host_need_bytes(meta_model, a.impl, 1 - RESIDENT, "blocks."), world,
+                                  bench.host_start_bytes(meta_model, a.impl))
         if not ok and rank == 0:
             print(json.dumps({"impl": a.impl, "n_gpus": world, "unavailable": why}))
         return ok

@@ -205,3 +205,15 @@ def test_host_need_estimates():
     assert bench.host_need_bytes(m, "ours", 0.5, "layers.") == unit // 2 + (2 << 30)
     per = 1 << (1000 * 1000 * 2 - 1).bit_length()
     assert bench.host_need_bytes(m, "reference", 0.5, "layers.") == 4 * per + unit // 2 + (2 << 30)
+
+
+def test_host_start_bytes():
+    import torch
+    from torch import nn
+
+    import bench
+
+    with torch.device("meta"):
+        m = nn.Linear(100, 10, bias=False)
+    assert bench.host_start_bytes(m, "reference") == 100 * 10 * 2
+    assert bench.host_start_bytes(m, "ours") == 0
