@@ -926,6 +926,10 @@ class TensorManager:
         self._build_runtime([s.label for s in state.stats], load, dict(state.transfer_to_compute_map),
                             dict(state.label_to_block_id))
         self.state = state
+        if self.enable_diagnostics:
+            from flextensor_b200.runtime.diagnostics import log_plan
+
+            log_plan(self)
 
     # ================================================================== misc API
     def get_gpu_memory_usage(self) -> GPUMemoryUsage:
