@@ -298,14 +298,23 @@ class GlobalOffloadStrategy:
 
 
 def _de_select(cands: list[tuple[str, TensorStatistics]], layer_stats, interp, n_blocks, assignment, budget,
-               seed_mask: np.ndarray | None, pop_size: int, epoch: int, max_early_stop: int, seed: int | None,
-               memory_first: bool):
-    """Differential evolution over per-candidate binaries. Returns best StrategyResult."""
-    from scipy.optimize import differential_evolution
+               seed_mask: np.ndarray | list[np.ndarray] | None, pop_size: int, epoch: int, max_early_stop: int,
+               seed: int | None, memory_first: bool, optimizer: str = "DE", seed_ratio: float = 0.0):
+    """Search over per-candidate offload binaries (x_i > 0.5 streams candidate i); returns the best
+    StrategyResult found, never worse (by the same cost) than the first seed plan.
+
+    ``optimizer``: ``DE`` -- differential evolution over a population whose first
+    ``max(1, seed_ratio * pop)`` members start from the seed plans (``seed_mask``: one mask or a
+    list of them, e.g. knapsack plans at several scales); ``SA`` (alias ``DA``) -- dual annealing
+    (generalised simulated annealing, local search off: the cost is piecewise constant) started
+    from the first seed plan. Both stop after ``epoch`` iterations, or once ``max_early_stop``
+    iterations (DE generations; SA minima reported) brought no improvement."""
+    from scipy.optimize import differential_evolution, dual_annealing
 
     if not cands:
         return StrategyResult({}, build_block_data({}, layer_stats, n_blocks, assignment))
     total_model = sum(t.size_bytes for l in layer_stats for t in l.tensors) or 1
+    masks = [] if seed_mask is None else ([seed_mask] if isinstance(seed_mask, np.ndarray) else list(seed_mask))
 
     def build(x: np.ndarray) -> StrategyResult:
         plan: dict[str, list[TensorStatistics]] = {}
@@ -324,13 +333,51 @@ def _de_select(cands: list[tuple[str, TensorStatistics]], layer_stats, interp, n
             return pen * 10 + off + over
         return pen * 10 + over * 10 - off * 0.1
 
+    best = {"f": np.inf, "stale": 0}
+    patience = max(1, int(max_early_stop))
+
+    def improved(f: float) -> bool:
+        """Record ``f``; True once ``patience`` consecutive reports brought no improvement."""
+        if f < best["f"] - 1e-12:
+            best["f"], best["stale"] = f, 0
+        else:
+            best["stale"] += 1
+        return best["stale"] >= patience
+
     rng = np.random.default_rng(seed)
-    init = rng.random((max(5, pop_size), len(cands)))
-    if seed_mask is not None:
-        init[0] = np.where(seed_mask, 0.9, 0.1)
-    res = differential_evolution(cost, bounds=[(0.0, 1.0)] * len(cands), maxiter=max(1, epoch), init=init,
-                                 seed=seed, polish=False, tol=1e-6, updating="deferred")
-    return build(res.x)
+    bounds = [(0.0, 1.0)] * len(cands)
+    if optimizer == "DE":
+        n_pop = max(5, pop_size)
+        init = rng.random((n_pop, len(cands)))
+        n_seeded = min(n_pop, max(1 if masks else 0, int(round(seed_ratio * n_pop))))
+        for i in range(n_seeded):
+            m = masks[i % len(masks)]
+            jitter = rng.uniform(0.0, 0.3, len(cands)) if i >= len(masks) else 0.0
+            init[i] = np.clip(np.where(m, 0.9, 0.1) + np.where(m, -jitter, jitter), 0.0, 1.0)
+
+        def de_cb(intermediate_result):
+            if improved(float(intermediate_result.fun)):
+                raise StopIteration
+
+        res = differential_evolution(cost, bounds=bounds, maxiter=max(1, epoch), init=init, seed=seed,
+                                     polish=False, tol=1e-6, updating="deferred", callback=de_cb)
+        x = res.x
+    elif optimizer in ("SA", "DA"):
+        x0 = np.where(masks[0], 0.9, 0.1) if masks else rng.random(len(cands))
+
+        def sa_cb(xk, f, context):
+            return improved(float(f))
+
+        res = dual_annealing(cost, bounds=bounds, maxiter=max(1, epoch), seed=seed, x0=x0, no_local_search=True,
+                             callback=sa_cb)
+        x = res.x
+    else:
+        raise ValueError(f"optimizer must be 'DE' or 'SA', got {optimizer!r}")
+    if masks:
+        x0 = np.where(masks[0], 1.0, 0.0)
+        if cost(x0) < cost(x):
+            x = x0
+    return build(x)
 
 
 class GlobalTensorSelectionStrategy:
@@ -340,8 +387,8 @@ class GlobalTensorSelectionStrategy:
                  min_blocks: int | None = None, max_blocks: int | None = None, threshold_mb: float = 0.1,
                  pop_size: int = 50, epoch: int = 200, max_early_stop: int = 25, optimizer: str = "DE",
                  seed_ratio: float = 0.25, seed: int | None = None, assignment_strategy=None):
-        if optimizer not in ("DE", "DA"):
-            raise ValueError("optimizer must be 'DE' or 'DA'")
+        if optimizer not in ("DE", "SA", "DA"):
+            raise ValueError("optimizer must be 'DE' (differential evolution) or 'SA' (dual annealing; alias 'DA')")
         self.scale, self.scale_ub, self.n_blocks, self.threshold_mb = scale, scale_ub, n_blocks, threshold_mb
         self.pop_size, self.epoch, self.max_early_stop, self.seed = pop_size, epoch, max_early_stop, seed
         self.optimizer, self.seed_ratio = optimizer, seed_ratio
@@ -351,14 +398,21 @@ class GlobalTensorSelectionStrategy:
     def compute(self, layer_stats, memory_stats=None, max_gpu_mem_bytes=None) -> StrategyResult:
         require_layers(layer_stats)
         interp = interpolator_for(layer_stats, memory_stats)
-        base = KnapsackBlockStrategy(self.scale, threshold_mb=self.threshold_mb, n_blocks=self.n_blocks).compute(
-            layer_stats, memory_stats, max_gpu_mem_bytes)
-        chosen = {t.tensor_id for ts in base.strategy_map.values() for t in ts}
         cands = [(layer_stats[j - 1].label, t) for j in range(1, len(layer_stats))
                  for t in eligible(layer_stats[j].tensors, self.threshold_mb)]
-        mask = np.array([t.tensor_id in chosen for _, t in cands], dtype=bool)
-        return _de_select(cands, layer_stats, interp, self.n_blocks, self.assignment, max_gpu_mem_bytes, mask,
-                          self.pop_size, self.epoch, self.max_early_stop, self.seed, memory_first=False)
+        # seed plans: the knapsack plan at the base scale and, up to scale_ub, at larger scales
+        scales = [self.scale]
+        if self.scale_ub is not None and self.scale_ub > self.scale:
+            scales += list(np.linspace(self.scale, self.scale_ub, 4)[1:])
+        masks = []
+        for sc in scales:
+            base = KnapsackBlockStrategy(float(sc), threshold_mb=self.threshold_mb, n_blocks=self.n_blocks).compute(
+                layer_stats, memory_stats, max_gpu_mem_bytes)
+            chosen = {t.tensor_id for ts in base.strategy_map.values() for t in ts}
+            masks.append(np.array([t.tensor_id in chosen for _, t in cands], dtype=bool))
+        return _de_select(cands, layer_stats, interp, self.n_blocks, self.assignment, max_gpu_mem_bytes, masks,
+                          self.pop_size, self.epoch, self.max_early_stop, self.seed, memory_first=False,
+                          optimizer=self.optimizer, seed_ratio=self.seed_ratio)
 
 
 # --------------------------------------------------------------------------- budget-fill family

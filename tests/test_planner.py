@@ -159,3 +159,48 @@ def test_interpolator_tied_end_durations_extrapolate_to_the_outer_point():
     assert it.duration_to_bytes(5.0) == pytest.approx(4 << 20)
     lo = MemoryTransferInterpolator({1 << 20: 1.0, 2 << 20: 1.0, 4 << 20: 2.0})
     assert lo.duration_to_bytes(0.5) == pytest.approx(1 << 20)
+
+
+@pytest.mark.parametrize("optimizer", ["DE", "SA", "DA"])
+def test_tensor_selection_optimizers(optimizer):
+    """Both optimizers (differential evolution, dual annealing) return a valid plan no worse than
+    the knapsack seed by the selection cost; seeds at several scales up to scale_ub are accepted."""
+    from flextensor_b200.planner.common import estimated_overhead
+
+    layers = make_layers(n=6)
+    from flextensor_b200.planner.interpolator import create_interpolator_from_benchmarks
+
+    interp = create_interpolator_from_benchmarks(MEM)
+    r = GlobalTensorSelectionStrategy(n_blocks=2, pop_size=8, epoch=20, seed=0, optimizer=optimizer,
+                                      scale_ub=2.0, seed_ratio=0.5).compute(layers, MEM, None)
+    _check(r, layers)
+    seed = KnapsackBlockStrategy(n_blocks=2).compute(layers, MEM, None)
+    assert estimated_overhead(r.strategy_map, layers, interp) <= estimated_overhead(seed.strategy_map, layers,
+                                                                                    interp) + 1e-9
+
+
+def test_tensor_selection_rejects_unknown_optimizer():
+    with pytest.raises(ValueError):
+        GlobalTensorSelectionStrategy(optimizer="PSO")
+
+
+def test_selection_stops_early_without_improvement(monkeypatch):
+    """max_early_stop ends the search after that many generations without a better cost."""
+    import flextensor_b200.planner.strategies as S
+
+    calls = {"n": 0}
+    real = S.estimated_overhead
+
+    def counting(*a, **k):
+        calls["n"] += 1
+        return real(*a, **k)
+
+    monkeypatch.setattr(S, "estimated_overhead", counting)
+    layers = make_layers(n=5)
+    GlobalTensorSelectionStrategy(n_blocks=2, pop_size=8, epoch=400, max_early_stop=2, seed=0).compute(
+        layers, MEM, None)
+    early = calls["n"]
+    calls["n"] = 0
+    GlobalTensorSelectionStrategy(n_blocks=2, pop_size=8, epoch=400, max_early_stop=400, seed=0).compute(
+        layers, MEM, None)
+    assert early < calls["n"]
