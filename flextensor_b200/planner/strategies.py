@@ -210,7 +210,8 @@ class NthLayerStrategy:
 
 
 class KnapsackStrategy:
-    """Per-pair subset-sum fill for the per-tensor (non-block) loader; cyclic by default."""
+    """Per-pair subset-sum fill for the per-tensor (non-block) loader; cyclic by default.
+    ``n_blocks`` is accepted for the reference's signature: the per-tensor loader has no ring."""
 
     def __init__(self, scale: float = 1.0, cyclic: bool = True, group_size: int = 1, threshold_mb: float = 0.1,
                  n_blocks: int = 4):
@@ -546,9 +547,29 @@ class BudgetFillLayerDEStrategy:
         n = len(layer_stats) - 1
         rng = np.random.default_rng(self.seed)
         init = rng.random((max(5, self.pop_size), n))
-        init[0] = 1.0
+        init[0] = 1.0  # stream everything eligible
+        # the greedy budget fill at this scale, as per-layer fractions
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            greedy = BudgetFillGreedyStrategy(self.n_blocks, threshold_mb=self.threshold_mb, scale=self.scale,
+                                              assignment_strategy=self.assignment).compute(
+                layer_stats, memory_stats, max_gpu_mem_bytes)
+        for j in range(1, len(layer_stats)):
+            tot = sum(t.size_bytes for t in eligible(layer_stats[j].tensors, self.threshold_mb))
+            got = sum(t.size_bytes for t in greedy.strategy_map.get(layer_stats[j - 1].label, ()))
+            init[1, j - 1] = min(1.0, got / tot) if tot else 0.0
+        state = {"f": np.inf, "stale": 0}
+
+        def stop_when_stale(intermediate_result):
+            if intermediate_result.fun < state["f"] - 1e-12:
+                state["f"], state["stale"] = intermediate_result.fun, 0
+            else:
+                state["stale"] += 1
+            if state["stale"] >= max(1, self.max_early_stop):
+                raise StopIteration
+
         res = differential_evolution(cost, [(0.0, 1.0)] * n, maxiter=self.epoch, init=init, seed=self.seed,
-                                     polish=False, tol=1e-7, updating="deferred")
+                                     polish=False, tol=1e-7, updating="deferred", callback=stop_when_stale)
         r = self._build(res.x, layer_stats)
         if peak_memory(r, layer_stats) > max_gpu_mem_bytes:
             full = self._build(np.ones(n), layer_stats)

@@ -204,3 +204,16 @@ def test_selection_stops_early_without_improvement(monkeypatch):
     GlobalTensorSelectionStrategy(n_blocks=2, pop_size=8, epoch=400, max_early_stop=400, seed=0).compute(
         layers, MEM, None)
     assert early < calls["n"]
+
+
+def test_layer_de_seeded_with_greedy_and_stops_early():
+    """Layer-fraction DE starts from the greedy plan at its scale (so it is never worse than
+    streaming everything) and honours max_early_stop."""
+    from flextensor_b200.planner.strategies import BudgetFillLayerDEStrategy
+
+    layers = make_layers(n=6)
+    total = sum(t.size_bytes for l in layers for t in l.tensors)
+    budget = int(0.6 * total)
+    r = BudgetFillLayerDEStrategy(n_blocks=2, pop_size=8, epoch=300, max_early_stop=3, seed=0).compute(
+        layers, MEM, budget)
+    _check(r, layers)
