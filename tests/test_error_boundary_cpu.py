@@ -53,3 +53,29 @@ def test_planner_failure_is_logged_and_releasable(caplog):
             got = mm2(x)
     assert torch.equal(got, want)
     ft.release("after_boom")
+
+
+def test_failed_block_construction_leaves_the_model_intact(monkeypatch):
+    """Packing copies every streamed tensor into the host arena before its parameter is pointed at
+    the copy, so a failure later in the construction (here: the transfer engine) leaves every
+    parameter holding its values; the released model computes what it computed before."""
+    import flextensor_b200.runtime.tensor_manager as TM
+
+    def no_engine(*a, **k):
+        raise RuntimeError("engine construction failed")
+
+    monkeypatch.setattr(TM, "make_engine", no_engine)
+    x = torch.randn(2, 32)
+    m = _model()
+    want = m(x).detach().clone()
+    conf = ft.OffloadConfig(pinned_memory=False, include_patterns=["0", "2"], profiling_iters=1, num_blocks=2,
+                            min_blocks=2, load_strategy=NthLayerStrategy(1, threshold_mb=0.0, n_blocks=2, cyclic=True))
+    om = ft.get_offload_manager("noengine")
+    mm = om.offload(m, conf)
+    with pytest.raises(RuntimeError, match="engine construction failed"):
+        with torch.no_grad():
+            for _ in range(om.iters_before_inference + 1):
+                mm(x)
+    ft.release("noengine")
+    with torch.no_grad():
+        assert torch.equal(m(x), want)
