@@ -419,25 +419,34 @@ def main():
         # Rank 0 sets up alone first; its MEASURED host footprint (peak RSS growth over the
         # setup) then decides whether the other N-1 ranks fit in the RAM still available.
         ok = torch.zeros(3, dtype=torch.float64, device=device)
+        failure = None
         if rank == 0:
             rss0 = _rss_bytes()
-            arm = setup_arm(args, ft, local, device, placement)
-            foot = max(0, _peak_rss_bytes() - rss0)
-            import psutil
+            try:
+                arm = setup_arm(args, ft, local, device, placement)
+            except Exception as e:  # noqa: BLE001 - reported by every rank below, then re-raised
+                failure = e
+                ok[0] = -2.0
+            else:
+                foot = max(0, _peak_rss_bytes() - rss0)
+                import psutil
 
-            avail = psutil.virtual_memory().available
-            need = (world - 1) * foot * 1.10 + 8e9
-            ok[0] = 1.0 if need <= avail else -1.0
-            ok[1], ok[2] = foot, avail
-        pg.all_reduce(ok, op=pg.ReduceOp.SUM)
+                avail = psutil.virtual_memory().available
+                need = (world - 1) * foot * 1.10 + 8e9
+                ok[0] = 1.0 if need <= avail else -1.0
+                ok[1], ok[2] = foot, avail
+        pg.all_reduce(ok, op=pg.ReduceOp.SUM)  # the other ranks learn rank 0's outcome here
         if float(ok[0]) < 0:
             if rank == 0:
-                print(json.dumps({"impl": args.impl, "n_gpus": world, "unavailable": (
-                    f"host RAM (measured): rank 0's setup grew its resident host memory by "
-                    f"{float(ok[1]) / 1e9:.1f} GB (a whole pinned copy of its offloaded weights); "
-                    f"{world - 1} more such ranks need {(world - 1) * float(ok[1]) / 1e9:.0f} GB + margin "
-                    f"> {float(ok[2]) / 1e9:.0f} GB available")}))
+                why = (f"rank 0's setup failed: {type(failure).__name__}: {failure}" if failure is not None else
+                       f"host RAM (measured): rank 0's setup grew its resident host memory by "
+                       f"{float(ok[1]) / 1e9:.1f} GB (a whole pinned copy of its offloaded weights); "
+                       f"{world - 1} more such ranks need {(world - 1) * float(ok[1]) / 1e9:.0f} GB + margin "
+                       f"> {float(ok[2]) / 1e9:.0f} GB available")
+                print(json.dumps({"impl": args.impl, "n_gpus": world, "unavailable": why}))
             pg.destroy_process_group()
+            if failure is not None:
+                raise failure
             return
         if rank != 0:
             arm = setup_arm(args, ft, local, device, placement)
